@@ -1,0 +1,384 @@
+#!/usr/bin/env python
+"""Qwen3-8B MXFP4 speculative-decode benchmark (BASELINE.json metric).
+
+Workload (k = 4, batch 1, short context): target
+Qwen3-8B with MXFP4 projections (seed 0), draft Qwen3-0.6B MXFP4 (seed 1),
+32-token prompt (uniform ids, seed 2 + rank), 64 new tokens per step, greedy
+speculative decoding with draft length 4.  Weights are seeded synthetic
+tensors generated on the GPU, so a random draft would never agree with the
+target; the headline therefore uses the oracle-draft mode of the config
+(the draft still runs every pass, its proposals replaced by the target's
+greedy tokens, each swapped with probability p = 0.25 for a uniform id),
+which gives an acceptance rate near the reference's published runs.  The
+same line carries the real-draft and p = 0 / 0.5 numbers.
+
+A step is one call of jl_generate_speculative: prefill (not counted in
+`value`, as in the reference's t(65) - t(1) method) plus the 64-token decode
+loop, which runs on the GPU as one CUDA graph.  `value` is device time of the
+decode loops (CUDA events on the stream it runs on); `e2e` is wall time of
+the whole public call with host buffers (prompt in, tokens out), prefill
+included.  Multi-GPU runs are independent replicas (one process per GPU, no
+collective on the data path); the barrier and max-over-ranks timing use
+torch.distributed only for control.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path[:0] = [str(REPO / "jalapenos-at-home_b200"), str(REPO / "oracle")]
+
+PRESETS = {
+    "qwen3-0.6b": dict(layers=28, hidden=1024, q_heads=16, kv_heads=8, inter=3072, vocab=151936, tied=True),
+    "qwen3-1.7b": dict(layers=28, hidden=2048, q_heads=16, kv_heads=8, inter=6144, vocab=151936, tied=True),
+    "qwen3-8b": dict(layers=36, hidden=4096, q_heads=32, kv_heads=8, inter=12288, vocab=151936, tied=False),
+}
+METRIC = "Qwen3-8B MXFP4 spec-decode tok/s (k=4) at 1-8 B200; % of HBM roofline"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--gamma", type=int, default=4)
+    ap.add_argument("--new", type=int, default=64)
+    ap.add_argument("--prompt", type=int, default=32)
+    ap.add_argument("--p", type=float, default=0.25, help="oracle-draft replacement probability")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Dist:
+    """Rank bookkeeping; torch.distributed only when launched by torchrun."""
+
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        import torch
+
+        torch.cuda.synchronize(self.local)
+        if self.pg:
+            self.pg.barrier()
+        torch.cuda.synchronize(self.local)
+
+    def max(self, v: float) -> float:
+        return self._reduce(v, "max")
+
+    def sum(self, v: float) -> float:
+        return self._reduce(v, "sum")
+
+    def _reduce(self, v, op):
+        if not self.pg:
+            return v
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{self.local}")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX if op == "max" else self.pg.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons of one GPU while running."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_models(J, device: int):
+    t = PRESETS["qwen3-8b"]
+    d = PRESETS["qwen3-0.6b"]
+    opts = dict(kv_pool_tokens=4096, max_pass_rows=256, device=device)
+    target = J.Model.synthesize(**t, seed=0, mxfp4=True, name="Qwen3-8B-MXFP4", **opts)
+    draft = J.Model.synthesize(**d, seed=1, mxfp4=True, name="Qwen3-0.6B-MXFP4", **opts)
+    return target, draft
+
+
+def cpu_baseline(J, O, target, draft, prompt, greedy, args, budget_s):
+    """The reference's CPU path (the oracle's restatement of engine/src/lib.rs
+    and speculative.rs) on this host's cores, same models and workload, timed
+    on a bounded number of decode rounds after prefill."""
+    import numpy as np
+
+    def oracle_model(gpu_model, preset, mxfp4):
+        cfg = O.Config(preset, **PRESETS[preset], max_positions=40960, eos=151645)
+        tensors = {}
+
+        def mat(name, rows, cols, q):
+            if q:
+                raw = gpu_model.read_tensor(name, rows * cols // 2 + rows * cols // 32)
+                return O.Matrix(rows, cols, packed=raw[: rows * cols // 2].copy(),
+                                scales=raw[rows * cols // 2:].copy())
+            raw = gpu_model.read_tensor(name, rows * cols * 2)
+            return O.Matrix(rows, cols, bf16=raw.view(np.uint16).copy())
+
+        tensors["embed"] = mat("model.embed_tokens.weight", cfg.vocab, cfg.hidden, False)
+        tensors["lm_head"] = None if cfg.tied else mat("lm_head.weight", cfg.vocab, cfg.hidden, False)
+        tensors["norm"] = np.full(cfg.hidden, O.ONE_BF16, np.uint16)
+        for layer in range(cfg.layers):
+            for p in O.PROJECTIONS:
+                shape = O.shape_of(cfg, p)
+                tensors[f"{layer}.{p}"] = mat(f"model.layers.{layer}.{O.HF_NAMES[p]}", shape[0],
+                                              shape[1], mxfp4)
+            for n in O.NORM_CODE:
+                tensors[f"{layer}.{n}"] = np.full(O.shape_of(cfg, n)[0], O.ONE_BF16, np.uint16)
+        return O.Model(cfg, tensors)
+
+    t_ref = oracle_model(target, "qwen3-8b", True)
+    d_ref = oracle_model(draft, "qwen3-0.6b", True)
+    res = O.generate_scheduled(t_ref, d_ref, prompt, args.new, O.DraftSchedule.fixed(args.gamma),
+                               round_bf16=True, oracle_stream=greedy, oracle_p=args.p,
+                               oracle_seed=5, max_seconds=budget_s)
+    new = len(res.tokens) - len(prompt)
+    return {"value": new / (res.decode_s if res.decode_s > 0 else float("nan")), "unit": "tok/s",
+            "cores": O.threads(), "kind": "port",
+            "sample": (f"oracle spec decode of the same workload (8B MXFP4 + 0.6B MXFP4, k={args.gamma}, "
+                       f"p={args.p}) on {O.threads()} threads: {res.rounds} rounds, {new} tokens in "
+                       f"{res.decode_s:.1f} s after an untimed prefill")}
+
+
+def run_reference(args, dist):
+    """--impl reference: the reference's CPU implementation of this path (its
+    Rust engine does not build here; the oracle restates it), on host cores."""
+    if dist.rank != 0:
+        return
+    import jalapeno as J
+    import oracle as O
+
+    target, draft = make_models(J, dist.local)
+    prompt = O.prompt_ids(args.prompt, 151936, 2)
+    greedy = target.generate(prompt, args.new)
+    samples = []
+    for step in range(args.warmup + args.steps):
+        budget = max(args.cpu_seconds / max(args.steps + args.warmup, 1), 5.0)
+        cb = cpu_baseline(J, O, target, draft, prompt, greedy, args, budget)
+        if step >= args.warmup:
+            samples.append(cb)
+    value = statistics.median(s["value"] for s in samples)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(args),
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": samples[0]["cores"],
+                             "kind": "port", "sample": samples[0]["sample"]},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args):
+    return {"workload": "Qwen3-8B MXFP4 target + Qwen3-0.6B MXFP4 draft, greedy speculative decode",
+            "k": args.gamma, "batch_per_gpu": 1, "prompt_tokens": args.prompt,
+            "new_tokens": args.new, "draft_mode": f"oracle p={args.p}",
+            "embed_lm_head": "bf16", "kv_cache": "bf16 paged", "seeds": "target 0, draft 1, prompt 2+rank",
+            "l2": "weights 4.9 GB per target pass, larger than the 126 MB L2",
+            "parallelism": f"replicas x{args.gpus}, no collective"}
+
+
+def main():
+    args = parse()
+    dist = Dist()
+    if args.impl == "reference":
+        run_reference(args, dist)
+        dist.close()
+        return
+    import jalapeno as J
+    import oracle as O
+
+    peak, peak_kind = measured_peaks()
+    target, draft = make_models(J, dist.local)
+    ti, di = target.info, draft.info
+    prompt = O.prompt_ids(args.prompt, ti.vocab, 2 + dist.rank)
+    greedy = target.generate(prompt, args.new)
+
+    def step(p, stream=True):
+        t0 = time.perf_counter()
+        r = J.generate_speculative(target, draft, prompt, args.new, args.gamma,
+                                   oracle_stream=greedy if stream else None, oracle_p=p,
+                                   oracle_seed=5)
+        wall = time.perf_counter() - t0
+        assert r.tokens == greedy, "speculative output differs from greedy"
+        return r, wall
+
+    for _ in range(args.warmup):
+        step(args.p)
+    dist.barrier()
+    results = []
+    with Clocks(dist.local) as clocks:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            results.append(step(args.p))
+        dist.barrier()
+        wall_total = time.perf_counter() - t0
+    new_tokens = sum(len(r.tokens) - len(prompt) for r, _ in results)
+    decode_ms = sum(r.decode_ms for r, _ in results)
+    e2e_s = sum(w for _, w in results)
+    max_decode_ms = dist.max(decode_ms)
+    max_e2e_s = dist.max(e2e_s)
+    all_tokens = dist.sum(new_tokens)
+    value = all_tokens / (max_decode_ms / 1000.0)
+    e2e = all_tokens / max_e2e_s
+    r0 = results[0][0]
+    rounds = sum(r.rounds for r, _ in results)
+    verify = sum(r.verify.passes for r, _ in results)
+    drafts = sum(r.draft.passes for r, _ in results)
+
+    # algorithmic bytes of the decode loops: every verify pass reads the
+    # target's weights, every draft pass the draft's; KV reads are added per
+    # pass from the context length (bf16 cache).
+    ctx = len(prompt) + args.new / 2
+    kv_t = ti.kv_bytes_per_token * ctx
+    kv_d = di.kv_bytes_per_token * ctx
+    bytes_total = verify * (ti.pass_bytes + kv_t) + drafts * (di.pass_bytes + kv_d)
+    path_gbs = bytes_total / (decode_ms / 1000.0) / 1e9
+    tokens_per_round = new_tokens / rounds
+    bytes_per_round = ti.pass_bytes + args.gamma * di.pass_bytes
+    roof_tps = peak * 1e9 * tokens_per_round / bytes_per_round
+
+    # dominant kernel: the target's gate/up projection inside a k+1-row verify pass
+    kern = {"gate_up": J.PROJ_GATE_UP, "qkv": J.PROJ_QKV, "down": J.PROJ_DOWN, "o": J.PROJ_O}
+    kt = {}
+    for name, which in kern.items():
+        ms, nb = target.time_projection(0, which, args.gamma + 1, iters=20)
+        kt[name] = (ms, nb)
+    ms, nb = kt["gate_up"]
+    achieved = nb / (ms / 1000.0) / 1e9
+    traffic = None
+    tfile = REPO / "profiles" / "traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("gate_up_verify_8b")
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": max_decode_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 activations, MXFP4 weights",
+        "data": "synthetic (seeded N(0,0.02) weights generated on the GPU, uniform prompt ids)",
+        "config": workload_config(args),
+        "acceptance": {"accepted": sum(r.accepted for r, _ in results),
+                       "drafted": sum(r.drafted for r, _ in results), "rounds": rounds,
+                       "tokens_per_round": tokens_per_round},
+        "path_roofline": {"bytes_per_round_k": bytes_per_round, "roofline_tok_s": roof_tps,
+                          "frac": value / dist.world / roof_tps, "achieved_gbs": path_gbs,
+                          "peak_gbs": peak, "peak_kind": peak_kind},
+        "roofline": {"bound": "hbm", "kernel": "skinny MXFP4 gate/up projection, 5-row verify",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "bytes_per_launch": nb, "ms_per_launch": ms,
+                     "peak_kind": peak_kind},
+        "kernels_gbs": {k: v[1] / (v[0] / 1000.0) / 1e9 for k, v in kt.items()},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * (len(prompt) + len(greedy)),
+                "d2h_bytes_per_step": 4 * len(greedy) + 16 * (rounds // args.steps)},
+        "gpu_launches": None,
+        "clocks": clocks.summary(),
+        "wall_s": wall_total,
+    }
+    # kernels in the timed steps: a pass is embed + 8 per layer + 3 for the
+    # head; the loop adds verify-setup and accept per verify pass, one
+    # bookkeeping kernel per draft pass and one round-begin kernel per round.
+    per_pass_t = 8 * ti.layers + 4
+    per_pass_d = 8 * di.layers + 4
+    line["gpu_launches"] = (args.steps * (per_pass_t + per_pass_d) + verify * (per_pass_t + 2)
+                            + drafts * (per_pass_d + 1) + rounds)
+    if not args.no_sweep:
+        sweep = {}
+        for p, stream in ((0.0, True), (0.5, True), (0.0, False)):
+            r, w = step(p, stream)
+            n = len(r.tokens) - len(prompt)
+            sweep["real draft" if not stream else f"oracle p={p}"] = {
+                "tok_s": n / (r.decode_ms / 1000.0), "accepted": r.accepted, "drafted": r.drafted}
+        # greedy decode of the target alone, same device loop
+        t0 = time.perf_counter()
+        target.generate(prompt, args.new)
+        sweep["greedy (no draft) e2e tok/s"] = args.new / (time.perf_counter() - t0)
+        line["sweep"] = sweep
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(J, O, target, draft, prompt, greedy, args, args.cpu_seconds)
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

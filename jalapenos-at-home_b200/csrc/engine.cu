@@ -1,0 +1,976 @@
+// Forward passes, greedy generation and speculative decoding.
+//
+//  * predict / hidden / next_token follow engine/src/model.rs:143-240 with
+//    one host sync per call (the reference's gpu_finish, gpu.m:114-128).
+//  * generate (model.rs:268-285) and generate_speculative (speculative.rs:
+//    43-143) run on the device: the whole loop is one CUDA graph whose WHILE
+//    node repeats a round and whose IF nodes skip draft passes past the
+//    budget or an end-of-sequence.  Acceptance, KV rollback (a length
+//    update) and the draft catch-up are small kernels between the passes,
+//    so a generation costs one host synchronisation.
+//  * JL_SPEC_HOST keeps the reference's host-side control flow for
+//    comparison.
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+
+#include "jl_internal.h"
+#include "kernels.cuh"
+
+namespace jl {
+
+namespace {
+
+constexpr int HEAD_CAP = 512;  // predicted rows per pass (longer all=true calls are chunked)
+
+__host__ __device__ inline void philox10_hd(uint32_t c[4], uint32_t k0, uint32_t k1) {
+    for (int r = 0; r < 10; ++r) {
+        if (r) { k0 += 0x9E3779B9u; k1 += 0xBB67AE85u; }
+        const uint64_t p0 = (uint64_t)0xD2511F53u * c[0];
+        const uint64_t p1 = (uint64_t)0xCD9E8D57u * c[2];
+        const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0, n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+        c[0] = n0; c[1] = (uint32_t)p1; c[2] = n2; c[3] = (uint32_t)p0;
+    }
+}
+
+// Oracle-draft proposal for `position`: the scripted stream's token, or with
+// probability p a uniform id, both drawn from one Philox block keyed by the
+// seed and the position.  `own` is the draft model's prediction.
+struct Oracle {
+    const uint32_t* stream;  // device or host, matching the caller
+    int32_t len;
+    double p;
+    uint64_t seed;
+    int32_t vocab;
+};
+
+__host__ __device__ inline uint32_t oracle_token(const Oracle& o, int32_t position, uint32_t own) {
+    if (!o.stream || position >= o.len) return own;
+    uint32_t c[4] = {(uint32_t)position, 0u, 0u, 0x6f726163u};
+    philox10_hd(c, (uint32_t)o.seed, 0x64726166u);
+    if ((double)c[0] + 0.5 < o.p * 4294967296.0) return c[1] % (uint32_t)o.vocab;
+    return o.stream[position];
+}
+
+// ---------------------------------------------------------------------------
+// device-side state of the generation loops
+
+struct SpecState {
+    int32_t n_tokens, limit, eos, start;
+    int32_t gamma, max_gamma, adaptive, budget;
+    int32_t n_proposed, pending, first_pred, draft_next;
+    int32_t target_len, draft_len, done, catch_rows;
+    int32_t drafted, accepted, rounds, draft_passes, verify_passes;
+    int32_t iterations;  // loop bodies entered; every round adds >= 1 token, so <= limit
+    int32_t fault;       // set when a guard stopped the loop
+    int32_t proposed[MAX_GAMMA];
+};
+
+__device__ inline void set_row(PassBuf pb, int i, uint32_t token, int32_t pos) {
+    RowDesc r;
+    r.token = token;
+    r.seq = 0;
+    r.pos = pos;
+    r.pad = 0;
+    pb.row[i] = r;
+}
+
+// Conditional handles of one round: IF nodes of draft steps 1..G-1.  Their
+// values persist across WHILE iterations, so every round clears them first.
+struct StepHandles {
+    cudaGraphConditionalHandle h[MAX_GAMMA];
+    int n;
+};
+
+// speculative.rs:79-93, first iteration: propose draft_next, then decide
+// whether the draft runs again.
+__global__ void k_round_begin(SpecState* st, PassBuf draft, cudaGraphConditionalHandle loop,
+                              StepHandles steps, cudaGraphConditionalHandle catchup) {
+    SpecState& s = *st;
+    cudaGraphSetConditional(catchup, 0);
+    for (int i = 1; i < steps.n; ++i) cudaGraphSetConditional(steps.h[i], 0);
+    s.iterations += 1;
+    if (s.iterations > s.limit + 1) s.fault = 1;  // cannot happen: each round adds a token
+    if (s.done || s.fault || s.n_tokens >= s.limit) {
+        s.done = 1;
+        cudaGraphSetConditional(loop, 0);
+        return;
+    }
+    s.start = s.n_tokens;
+    s.budget = min(s.gamma, s.limit - s.start);
+    s.proposed[0] = s.draft_next;
+    s.n_proposed = 1;
+    const bool more = !(s.budget == 1 || s.draft_next == s.eos);
+    if (more) {
+        draft.hdr->rows = 1;
+        draft.hdr->head_rows = 1;
+        draft.head_row[0] = 0;
+        set_row(draft, 0, (uint32_t)s.draft_next, s.draft_len);
+    }
+    if (steps.n > 1) cudaGraphSetConditional(steps.h[1], more ? 1 : 0);
+}
+
+// After draft pass i of a round (speculative.rs:84-92).
+__global__ void k_draft_step(SpecState* st, PassBuf draft, Oracle o, int i,
+                             cudaGraphConditionalHandle next) {
+    SpecState& s = *st;
+    s.draft_len += 1;
+    s.draft_passes += 1;
+    const uint32_t tok = oracle_token(o, s.draft_len, draft.out_ids[0]);
+    s.draft_next = (int32_t)tok;
+    s.proposed[i] = (int32_t)tok;
+    s.n_proposed = i + 1;
+    const bool more = !(i + 1 == s.budget || (int32_t)tok == s.eos);
+    if (more) set_row(draft, 0, tok, s.draft_len);
+    if (next) cudaGraphSetConditional(next, more ? 1 : 0);
+}
+
+// speculative.rs:95-97: [pending correction] + proposals, predict after every row.
+__global__ void k_verify_setup(SpecState* st, PassBuf target) {
+    SpecState& s = *st;
+    int rows = 0;
+    if (s.pending >= 0) set_row(target, rows++, (uint32_t)s.pending, s.target_len);
+    for (int j = 0; j < s.n_proposed; ++j) {
+        set_row(target, rows, (uint32_t)s.proposed[j], s.target_len + rows);
+        ++rows;
+    }
+    target.hdr->rows = rows;
+    target.hdr->head_rows = rows;
+    for (int j = 0; j < rows; ++j) target.head_row[j] = j;
+}
+
+// speculative.rs:99-140: greedy acceptance, schedule feedback, rollback by
+// length, correction / bonus token and the draft catch-up rows.
+__global__ void k_accept(SpecState* st, PassBuf target, PassBuf draft, uint32_t* tokens,
+                         jl_round_stats* rounds, int32_t rounds_cap,
+                         cudaGraphConditionalHandle loop, cudaGraphConditionalHandle catchup) {
+    SpecState& s = *st;
+    const int rows = target.hdr->rows;
+    s.target_len += rows;
+    s.verify_passes += 1;
+    int32_t preds[MAX_GAMMA + 2];
+    int np = 0;
+    if (s.first_pred >= 0) preds[np++] = s.first_pred;
+    for (int j = 0; j < rows; ++j) preds[np++] = (int32_t)target.out_ids[j];
+    s.first_pred = -1;
+    s.pending = -1;
+    int accepted = 0;
+    int32_t next = preds[0];
+    while (accepted < s.n_proposed && s.proposed[accepted] == next) {
+        ++accepted;
+        next = preds[accepted];
+    }
+    // DraftSchedule::observe (scheduler.rs:33-44)
+    const int gamma = s.gamma, drafted = s.n_proposed;
+    if (s.adaptive && drafted == s.gamma) {
+        if (accepted == drafted) s.gamma = min(s.gamma + 1, s.max_gamma);
+        else if (accepted < (drafted + 1) / 2) s.gamma = max(s.gamma / 2, 1);
+    }
+    if (s.rounds < rounds_cap) {
+        jl_round_stats r;
+        r.gamma = (uint32_t)gamma;
+        r.drafted = (uint32_t)drafted;
+        r.accepted = (uint32_t)accepted;
+        r.next_gamma = (uint32_t)s.gamma;
+        rounds[s.rounds] = r;
+    }
+    s.rounds += 1;
+    s.drafted += drafted;
+    s.accepted += accepted;
+    // budget <= limit - start keeps n_tokens <= limit; the guards only bound writes
+    for (int j = 0; j < accepted && s.n_tokens < s.limit; ++j) tokens[s.n_tokens++] = (uint32_t)s.proposed[j];
+    bool stop = (accepted > 0 && (int32_t)tokens[s.n_tokens - 1] == s.eos) || s.n_tokens >= s.limit;
+    if (!stop) {
+        s.target_len = s.start + accepted;
+        s.draft_len = min(s.start + accepted, s.draft_len);
+        tokens[s.n_tokens++] = (uint32_t)next;
+        stop = next == s.eos || s.n_tokens >= s.limit;
+    }
+    if (stop) {
+        s.done = 1;
+        cudaGraphSetConditional(loop, 0);
+        cudaGraphSetConditional(catchup, 0);
+        return;
+    }
+    s.pending = next;
+    // The last accepted proposal may not be in the draft cache yet: feed it
+    // together with the bonus token (speculative.rs:134-138).
+    const int tail = s.n_tokens - s.draft_len;
+    if (tail < 1 || tail > 2) {  // cannot happen; stop rather than run a malformed pass
+        s.fault = 1;
+        s.done = 1;
+        cudaGraphSetConditional(loop, 0);
+        cudaGraphSetConditional(catchup, 0);
+        return;
+    }
+    s.catch_rows = tail;
+    for (int j = 0; j < tail; ++j) set_row(draft, j, tokens[s.draft_len + j], s.draft_len + j);
+    draft.hdr->rows = tail;
+    draft.hdr->head_rows = 1;
+    draft.head_row[0] = tail - 1;
+    cudaGraphSetConditional(catchup, 1);
+}
+
+__global__ void k_catchup_done(SpecState* st, PassBuf draft, Oracle o) {
+    SpecState& s = *st;
+    s.draft_len += s.catch_rows;
+    s.draft_passes += 1;
+    s.draft_next = (int32_t)oracle_token(o, s.draft_len, draft.out_ids[0]);
+}
+
+// Greedy loop (model.rs:277-283): after each single-row pass, append the
+// prediction and stop at eos or the count.
+__global__ void k_greedy_step(SpecState* st, PassBuf pb, uint32_t* tokens,
+                              cudaGraphConditionalHandle loop) {
+    SpecState& s = *st;
+    s.target_len += 1;
+    s.iterations += 1;
+    const uint32_t nxt = pb.out_ids[0];
+    if (s.n_tokens < s.limit) tokens[s.n_tokens++] = nxt;
+    if ((int32_t)nxt == s.eos || s.n_tokens >= s.limit || s.iterations > s.limit) {
+        s.done = 1;
+        cudaGraphSetConditional(loop, 0);
+        return;
+    }
+    set_row(pb, 0, nxt, s.target_len);
+}
+
+// ---------------------------------------------------------------------------
+
+double elapsed_ms(cudaEvent_t a, cudaEvent_t b) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, a, b);
+    return ms;
+}
+
+// Kernels record impossible states (a page id outside the pool, a position
+// outside the RoPE table) in a device flag instead of touching memory out of
+// range; surface it once the stream is idle.
+jl_status check_device_flag(jl_model* m) {
+    int flag = 0;
+    JL_CUDA(cudaMemcpy(&flag, m->counters, sizeof(int), cudaMemcpyDeviceToHost));
+    if (flag) {
+        JL_CUDA(cudaMemset(m->counters, 0, sizeof(int)));
+        set_error("kernel guard tripped (flags 0x%x): %s", flag,
+                  (flag & 1) ? "KV page id outside the pool" : "position outside the context");
+        return JL_ERR_CUDA;
+    }
+    return JL_OK;
+}
+
+jl_status check_ids(const jl_model* m, const uint32_t* ids, size_t n) {
+    for (size_t i = 0; i < n; ++i)
+        if (ids[i] >= (uint32_t)m->embed.rows) {
+            set_error("token id %u out of range (vocabulary %d)", ids[i], m->embed.rows);
+            return JL_ERR_INVALID_ARG;
+        }
+    return JL_OK;
+}
+
+// Stages one pass's rows from the host and runs it on m->stream.
+jl_status host_pass(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int head_rows,
+                    bool all, int layers) {
+    PassHdr* h = m->host_hdr;
+    h->rows = (int32_t)n;
+    h->head_rows = head_rows;
+    h->pad0 = h->pad1 = 0;
+    for (size_t i = 0; i < n; ++i) {
+        m->host_row[i].token = ids[i];
+        m->host_row[i].seq = 0;
+        m->host_row[i].pos = (int32_t)(c->len + i);
+        m->host_row[i].pad = 0;
+    }
+    for (int j = 0; j < head_rows; ++j) m->host_head_row[j] = all ? j : (int32_t)n - 1;
+    m->host_page_table[0] = c->d_pages;
+    cudaStream_t st = m->stream;
+    JL_CUDA(cudaMemcpyAsync(m->pass.hdr, h, sizeof(PassHdr), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(m->pass.row, m->host_row, n * sizeof(RowDesc), cudaMemcpyHostToDevice, st));
+    if (head_rows)
+        JL_CUDA(cudaMemcpyAsync(m->pass.head_row, m->host_head_row, head_rows * sizeof(int32_t),
+                                cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(m->pass.page_table, m->host_page_table, sizeof(int32_t*),
+                            cudaMemcpyHostToDevice, st));
+    const bool full = layers == m->layers && head_rows > 0;
+    if (full && n <= (size_t)SMALL_M) {
+        if (!m->small_graph) {
+            cudaGraph_t g;
+            JL_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            jl_status rs = record_pass(m, st, SMALL_M, m->layers, true);
+            cudaError_t ce = cudaStreamEndCapture(st, &g);
+            if (rs != JL_OK) return rs;
+            JL_CUDA(ce);
+            JL_CUDA(cudaGraphInstantiate(&m->small_graph, g, 0));
+            cudaGraphDestroy(g);
+        }
+        JL_CUDA(cudaGraphLaunch(m->small_graph, st));
+        return JL_OK;
+    }
+    PassCtx ctx{m, st, (int)n, std::max(head_rows, 1)};
+    return record_pass_ctx(ctx, layers, head_rows > 0);
+}
+
+}  // namespace
+
+jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head) {
+    const jl_model* m = c.m;
+    JL_TRY(launch_embed(c));
+    for (int l = 0; l < layers; ++l) {
+        const LayerW& L = m->lw[l];
+        JL_TRY(launch_rmsnorm(c, m->s.x, L.in_ln, m->s.xn, false));  // model.rs:174-177
+        JL_TRY(launch_qkv(c, L));                                    // lib.rs:353-355
+        JL_TRY(launch_qk_rope_kv(c, l, L));                          // lib.rs:363-396
+        JL_TRY(launch_attention(c, l));                              // lib.rs:401-441
+        JL_TRY(launch_o(c, L));                                      // lib.rs:444-449 + residual
+        JL_TRY(launch_rmsnorm(c, m->s.x, L.post_ln, m->s.xn, false));
+        JL_TRY(launch_gateup(c, L));                                 // lib.rs:459-463
+        JL_TRY(launch_down(c, L));                                   // lib.rs:464-467 + residual
+    }
+    if (with_head) {
+        JL_TRY(launch_rmsnorm(c, m->s.x, m->final_norm, m->s.xh, true));  // model.rs:228
+        JL_TRY(launch_head(c));                                           // model.rs:229-234
+        JL_TRY(launch_argmax(c));                                         // model.rs:235-239
+    }
+    return JL_OK;
+}
+
+jl_status record_pass(jl_model* m, cudaStream_t stream, int rows_cap, int layers, bool with_head) {
+    PassCtx c{m, stream, rows_cap, rows_cap};
+    return record_pass_ctx(c, layers, with_head);
+}
+
+jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool all,
+                  uint32_t* out_ids, float* out_logits) {
+    if (n == 0 || c->len + n > (size_t)m->max_positions) {  // model.rs:212
+        set_error("predict needs 1..%zu tokens, got %zu", (size_t)m->max_positions - c->len, n);
+        return JL_ERR_INVALID_ARG;
+    }
+    JL_TRY(check_ids(m, ids, n));
+    JL_CUDA(cudaSetDevice(m->device));
+    JL_TRY(cache_reserve(c, c->len + n, m->stream));
+    const size_t chunk = all ? std::min<size_t>(m->max_rows, HEAD_CAP) : (size_t)m->max_rows;
+    size_t done = 0;
+    while (done < n) {
+        const size_t take = std::min(chunk, n - done);
+        const bool last = done + take == n;
+        const int head_rows = all ? (int)take : (last ? 1 : 0);
+        JL_TRY(host_pass(m, c, ids + done, take, head_rows, all, m->layers));
+        if (head_rows) {
+            const size_t first = all ? done : 0;
+            JL_CUDA(cudaMemcpyAsync(m->host_out, m->pass.out_ids, head_rows * sizeof(uint32_t),
+                                    cudaMemcpyDeviceToHost, m->stream));
+            if (out_logits)
+                JL_CUDA(cudaMemcpyAsync(out_logits + first * m->vocab, m->s.logits,
+                                        (size_t)head_rows * m->vocab * sizeof(float),
+                                        cudaMemcpyDeviceToHost, m->stream));
+            JL_CUDA(cudaStreamSynchronize(m->stream));
+            memcpy(out_ids + first, m->host_out, head_rows * sizeof(uint32_t));
+        }
+        c->len += take;
+        done += take;
+    }
+    JL_CUDA(cudaStreamSynchronize(m->stream));
+    return check_device_flag(m);
+}
+
+jl_status time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t rows, size_t reps,
+                    double* wall_ms, double* gpu_ms) {
+    // model.rs:245-266
+    if (rows == 0 || reps == 0 || n + rows > (size_t)m->max_positions) {
+        set_error("time_pass needs rows > 0, reps > 0 and prompt + rows within the context");
+        return JL_ERR_INVALID_ARG;
+    }
+    jl_cache* c = nullptr;
+    JL_TRY(cache_create(m, &c));
+    std::unique_ptr<jl_cache, void (*)(jl_cache*)> guard(c, cache_free);
+    uint32_t first = 0;
+    JL_TRY(predict(m, c, prompt, n, false, &first, nullptr));
+    std::vector<uint32_t> tokens(rows), out(rows);
+    for (size_t i = 0; i < rows; ++i) tokens[i] = prompt[i % n];
+    std::vector<double> wall, busy;
+    for (size_t r = 0; r < reps + 2; ++r) {
+        const auto t0 = std::chrono::steady_clock::now();
+        JL_CUDA(cudaEventRecord(m->ev0, m->stream));
+        JL_TRY(predict(m, c, tokens.data(), rows, rows > 1, out.data(), nullptr));
+        JL_CUDA(cudaEventRecord(m->ev1, m->stream));
+        JL_CUDA(cudaEventSynchronize(m->ev1));
+        wall.push_back(std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
+        busy.push_back(elapsed_ms(m->ev0, m->ev1));
+        c->len = n;  // cache.truncate(prompt.len())
+    }
+    auto median = [](std::vector<double>& v) {
+        v.erase(v.begin(), v.begin() + 2);
+        std::sort(v.begin(), v.end());
+        return v[v.size() / 2];
+    };
+    *wall_ms = median(wall);
+    *gpu_ms = median(busy);
+    return JL_OK;
+}
+
+jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters, double* ms,
+                          size_t* bytes) {
+    if (layer < 0 || layer >= m->layers || which < 0 || which > 4 || rows < 1 ||
+        rows > m->max_rows || iters < 1) {
+        set_error("time_projection: bad layer, projection, rows or iters");
+        return JL_ERR_INVALID_ARG;
+    }
+    JL_CUDA(cudaSetDevice(m->device));
+    const LayerW& L = m->lw[layer];
+    PassHdr h{rows, which == 4 ? rows : 0, 0, 0};
+    *m->host_hdr = h;
+    JL_CUDA(cudaMemcpyAsync(m->pass.hdr, m->host_hdr, sizeof(PassHdr), cudaMemcpyHostToDevice, m->stream));
+    const int cap = rows <= SMALL_M ? SMALL_M : rows;
+    PassCtx c{m, m->stream, cap, cap};
+    auto launch = [&]() -> jl_status {
+        switch (which) {
+            case 0: return launch_qkv(c, L);
+            case 1: return launch_o(c, L);
+            case 2: return launch_gateup(c, L);
+            case 3: return launch_down(c, L);
+            default: return launch_head(c);
+        }
+    };
+    JL_TRY(launch());  // warm up
+    JL_CUDA(cudaEventRecord(m->ev0, m->stream));
+    for (int i = 0; i < iters; ++i) JL_TRY(launch());
+    JL_CUDA(cudaEventRecord(m->ev1, m->stream));
+    JL_CUDA(cudaEventSynchronize(m->ev1));
+    *ms = elapsed_ms(m->ev0, m->ev1) / iters;
+    switch (which) {
+        case 0: *bytes = L.q.bytes() + L.k.bytes() + L.v.bytes(); break;
+        case 1: *bytes = L.o.bytes(); break;
+        case 2: *bytes = L.gate.bytes() + L.up.bytes(); break;
+        case 3: *bytes = L.down.bytes(); break;
+        default: *bytes = m->head.bytes();
+    }
+    return JL_OK;
+}
+
+jl_status hidden(jl_model* m, const uint32_t* ids, size_t n, size_t layers, float* out) {
+    if (n == 0 || n > (size_t)m->max_positions || layers > (size_t)m->layers) {
+        set_error("hidden needs 1..%d tokens and at most %d layers", m->max_positions, m->layers);
+        return JL_ERR_INVALID_ARG;
+    }
+    JL_TRY(check_ids(m, ids, n));
+    JL_CUDA(cudaSetDevice(m->device));
+    jl_cache* c = nullptr;
+    JL_TRY(cache_create(m, &c));
+    std::unique_ptr<jl_cache, void (*)(jl_cache*)> guard(c, cache_free);
+    JL_TRY(cache_reserve(c, n, m->stream));
+    size_t done = 0;
+    while (done < n) {
+        const size_t take = std::min((size_t)m->max_rows, n - done);
+        JL_TRY(host_pass(m, c, ids + done, take, 0, false, (int)layers));
+        JL_CUDA(cudaMemcpyAsync(out + done * m->hidden, m->s.x, take * m->hidden * sizeof(float),
+                                cudaMemcpyDeviceToHost, m->stream));
+        JL_CUDA(cudaStreamSynchronize(m->stream));
+        c->len += take;
+        done += take;
+    }
+    return JL_OK;
+}
+
+// ---------------------------------------------------------------------------
+// device-resident loops
+
+struct SpecGraph {
+    jl_model* target = nullptr;
+    jl_model* draft = nullptr;  // null for the greedy loop
+    int G = 0;
+    cudaGraphExec_t exec = nullptr;
+    SpecState* st = nullptr;
+    uint32_t* tokens = nullptr;
+    jl_round_stats* rounds = nullptr;
+    int32_t cap = 0;
+    uint32_t* oracle = nullptr;
+    int32_t oracle_cap = 0;
+    Oracle oracle_args{};
+    SpecState* host_st = nullptr;
+};
+
+void spec_graph_free(SpecGraph* g) {
+    if (!g) return;
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    cudaFree(g->st);
+    cudaFree(g->tokens);
+    cudaFree(g->rounds);
+    cudaFree(g->oracle);
+    cudaFreeHost(g->host_st);
+    delete g;
+}
+
+namespace {
+
+jl_status add_conditional(cudaGraph_t graph, cudaGraphNode_t* deps, size_t ndeps,
+                          cudaGraphConditionalHandle h, cudaGraphConditionalNodeType type,
+                          cudaGraphNode_t* node, cudaGraph_t* body) {
+    cudaGraphNodeParams p = {};
+    p.type = cudaGraphNodeTypeConditional;
+    p.conditional.handle = h;
+    p.conditional.type = type;
+    p.conditional.size = 1;
+    JL_CUDA(cudaGraphAddNode(node, graph, deps, ndeps, &p));
+    *body = p.conditional.phGraph_out[0];
+    return JL_OK;
+}
+
+// Captures the kernels that `fn` launches on `stream` into `graph`, after
+// `dep` (or as roots when dep is null); returns the capture's last nodes.
+template <class F>
+jl_status capture_into(cudaGraph_t graph, cudaStream_t stream, cudaGraphNode_t* dep, F fn,
+                       std::vector<cudaGraphNode_t>* tail) {
+    JL_CUDA(cudaStreamBeginCaptureToGraph(stream, graph, dep, nullptr, dep ? 1 : 0,
+                                          cudaStreamCaptureModeThreadLocal));
+    jl_status rs = fn();
+    if (rs == JL_OK && tail) {
+        cudaStreamCaptureStatus cs;
+        const cudaGraphNode_t* deps = nullptr;
+        size_t nd = 0;
+        cudaError_t e = cudaStreamGetCaptureInfo(stream, &cs, nullptr, nullptr, &deps, &nd);
+        if (e == cudaSuccess) tail->assign(deps, deps + nd);
+    }
+    cudaGraph_t out;
+    cudaError_t ce = cudaStreamEndCapture(stream, &out);
+    if (rs != JL_OK) return rs;
+    JL_CUDA(ce);
+    return JL_OK;
+}
+
+jl_status build_spec_graph(SpecGraph* g) {
+    jl_model* T = g->target;
+    jl_model* D = g->draft;
+    cudaStream_t st = T->stream;
+    cudaGraph_t top;
+    JL_CUDA(cudaGraphCreate(&top, 0));
+    std::unique_ptr<CUgraph_st, cudaError_t (*)(cudaGraph_t)> top_guard(top, cudaGraphDestroy);
+    cudaGraphConditionalHandle h_loop;
+    JL_CUDA(cudaGraphConditionalHandleCreate(&h_loop, top, 1, cudaGraphCondAssignDefault));
+    cudaGraphNode_t loop_node;
+    cudaGraph_t body;
+    JL_TRY(add_conditional(top, nullptr, 0, h_loop, cudaGraphCondTypeWhile, &loop_node, &body));
+
+    const int G = g->G;
+    std::vector<cudaGraphConditionalHandle> h_step(G + 1, 0);
+    for (int i = 1; i < G; ++i)
+        JL_CUDA(cudaGraphConditionalHandleCreate(&h_step[i], body, 0, 0));
+    cudaGraphConditionalHandle h_catch;
+    JL_CUDA(cudaGraphConditionalHandleCreate(&h_catch, body, 0, 0));
+
+    StepHandles steps{};
+    steps.n = G;
+    for (int i = 1; i < G; ++i) steps.h[i] = h_step[i];
+    std::vector<cudaGraphNode_t> tail;
+    // round begin
+    JL_TRY(capture_into(body, st, nullptr, [&]() -> jl_status {
+        k_round_begin<<<1, 1, 0, st>>>(g->st, D->pass, h_loop, steps, h_catch);
+        JL_CUDA(cudaGetLastError());
+        return JL_OK;
+    }, &tail));
+    cudaGraphNode_t prev = tail.at(0);
+    // draft steps 1..G-1, each behind an IF node
+    for (int i = 1; i < G; ++i) {
+        cudaGraphNode_t ifn;
+        cudaGraph_t ifb;
+        JL_TRY(add_conditional(body, &prev, 1, h_step[i], cudaGraphCondTypeIf, &ifn, &ifb));
+        const cudaGraphConditionalHandle nxt = i + 1 < G ? h_step[i + 1] : 0;
+        JL_TRY(capture_into(ifb, st, nullptr, [&]() -> jl_status {
+            PassCtx c{D, st, 1, 1};
+            JL_TRY(record_pass_ctx(c, D->layers, true));
+            k_draft_step<<<1, 1, 0, st>>>(g->st, D->pass, g->oracle_args, i, nxt);
+            JL_CUDA(cudaGetLastError());
+            return JL_OK;
+        }, nullptr));
+        prev = ifn;
+    }
+    // verify + accept
+    JL_TRY(capture_into(body, st, &prev, [&]() -> jl_status {
+        k_verify_setup<<<1, 1, 0, st>>>(g->st, T->pass);
+        JL_CUDA(cudaGetLastError());
+        PassCtx c{T, st, G + 1, G + 1};
+        JL_TRY(record_pass_ctx(c, T->layers, true));
+        k_accept<<<1, 1, 0, st>>>(g->st, T->pass, D->pass, g->tokens, g->rounds, g->cap, h_loop, h_catch);
+        JL_CUDA(cudaGetLastError());
+        return JL_OK;
+    }, &tail));
+    prev = tail.at(0);
+    // draft catch-up behind an IF node
+    {
+        cudaGraphNode_t ifn;
+        cudaGraph_t ifb;
+        JL_TRY(add_conditional(body, &prev, 1, h_catch, cudaGraphCondTypeIf, &ifn, &ifb));
+        JL_TRY(capture_into(ifb, st, nullptr, [&]() -> jl_status {
+            PassCtx c{D, st, 2, 1};
+            JL_TRY(record_pass_ctx(c, D->layers, true));
+            k_catchup_done<<<1, 1, 0, st>>>(g->st, D->pass, g->oracle_args);
+            JL_CUDA(cudaGetLastError());
+            return JL_OK;
+        }, nullptr));
+    }
+    JL_CUDA(cudaGraphInstantiate(&g->exec, top, 0));
+    return JL_OK;
+}
+
+jl_status build_greedy_graph(SpecGraph* g) {
+    jl_model* T = g->target;
+    cudaStream_t st = T->stream;
+    cudaGraph_t top;
+    JL_CUDA(cudaGraphCreate(&top, 0));
+    std::unique_ptr<CUgraph_st, cudaError_t (*)(cudaGraph_t)> top_guard(top, cudaGraphDestroy);
+    cudaGraphConditionalHandle h_loop;
+    JL_CUDA(cudaGraphConditionalHandleCreate(&h_loop, top, 1, cudaGraphCondAssignDefault));
+    cudaGraphNode_t loop_node;
+    cudaGraph_t body;
+    JL_TRY(add_conditional(top, nullptr, 0, h_loop, cudaGraphCondTypeWhile, &loop_node, &body));
+    JL_TRY(capture_into(body, st, nullptr, [&]() -> jl_status {
+        PassCtx c{T, st, 1, 1};
+        JL_TRY(record_pass_ctx(c, T->layers, true));
+        k_greedy_step<<<1, 1, 0, st>>>(g->st, T->pass, g->tokens, h_loop);
+        JL_CUDA(cudaGetLastError());
+        return JL_OK;
+    }, nullptr));
+    JL_CUDA(cudaGraphInstantiate(&g->exec, top, 0));
+    return JL_OK;
+}
+
+jl_status get_graph(jl_model* target, jl_model* draft, int G, SpecGraph** out) {
+    for (auto* g : target->spec_graphs)
+        if (g->draft == draft && g->G == G) {
+            *out = g;
+            return JL_OK;
+        }
+    std::unique_ptr<SpecGraph> g(new SpecGraph());
+    g->target = target;
+    g->draft = draft;
+    g->G = G;
+    g->cap = target->max_positions + 2 * MAX_GAMMA + 8;
+    JL_CUDA(cudaMalloc(&g->st, sizeof(SpecState)));
+    JL_CUDA(cudaMalloc(&g->tokens, (size_t)g->cap * sizeof(uint32_t)));
+    JL_CUDA(cudaMalloc(&g->rounds, (size_t)g->cap * sizeof(jl_round_stats)));
+    JL_CUDA(cudaMallocHost(&g->host_st, sizeof(SpecState)));
+    if (draft) {
+        g->oracle_cap = g->cap;
+        JL_CUDA(cudaMalloc(&g->oracle, (size_t)g->oracle_cap * sizeof(uint32_t)));
+        g->oracle_args = Oracle{nullptr, 0, 0.0, 0, target->vocab};
+        // The kernels read oracle settings from a device copy refreshed per call.
+    }
+    jl_status s = draft ? build_spec_graph(g.get()) : build_greedy_graph(g.get());
+    if (s != JL_OK) {
+        spec_graph_free(g.release());
+        return s;
+    }
+    *out = g.get();
+    target->spec_graphs.push_back(g.release());
+    return JL_OK;
+}
+
+}  // namespace
+
+jl_status generate(jl_model* m, const uint32_t* prompt, size_t n, size_t count, uint32_t* out,
+                   size_t cap, size_t* out_len) {
+    // model.rs:268-285
+    if (n == 0) {
+        set_error("prompt is empty");
+        return JL_ERR_INVALID_ARG;
+    }
+    const size_t limit_room = n < (size_t)m->max_positions ? (size_t)m->max_positions - n : 0;
+    count = std::min(count, limit_room);
+    if (cap < n + count) {
+        set_error("output capacity %zu is below prompt + count = %zu", cap, n + count);
+        return JL_ERR_INVALID_ARG;
+    }
+    JL_TRY(check_ids(m, prompt, n));
+    memcpy(out, prompt, n * sizeof(uint32_t));
+    *out_len = n;
+    if (count == 0) return JL_OK;
+    JL_CUDA(cudaSetDevice(m->device));
+    jl_cache* c = nullptr;
+    JL_TRY(cache_create(m, &c));
+    std::unique_ptr<jl_cache, void (*)(jl_cache*)> guard(c, cache_free);
+    uint32_t next = 0;
+    JL_TRY(predict(m, c, prompt, n, false, &next, nullptr));
+    out[n] = next;
+    *out_len = n + 1;
+    if ((int32_t)next == m->eos || count == 1) return JL_OK;
+    // the rest of the loop runs on the device
+    SpecGraph* g = nullptr;
+    JL_TRY(get_graph(m, nullptr, 0, &g));
+    JL_TRY(cache_reserve(c, n + count, m->stream));
+    SpecState* s = g->host_st;
+    memset(s, 0, sizeof(SpecState));
+    s->n_tokens = (int32_t)(n + 1);
+    s->limit = (int32_t)(n + count);
+    s->eos = m->eos;
+    s->target_len = (int32_t)c->len;
+    cudaStream_t st = m->stream;
+    JL_CUDA(cudaMemcpyAsync(g->st, s, sizeof(SpecState), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(g->tokens, out, (n + 1) * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+    PassHdr* h = m->host_hdr;
+    h->rows = 1;
+    h->head_rows = 1;
+    m->host_row[0] = RowDesc{next, 0, (int32_t)c->len, 0};
+    m->host_head_row[0] = 0;
+    m->host_page_table[0] = c->d_pages;
+    JL_CUDA(cudaMemcpyAsync(m->pass.hdr, h, sizeof(PassHdr), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(m->pass.row, m->host_row, sizeof(RowDesc), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(m->pass.head_row, m->host_head_row, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(m->pass.page_table, m->host_page_table, sizeof(int32_t*),
+                            cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaGraphLaunch(g->exec, st));
+    JL_CUDA(cudaMemcpyAsync(s, g->st, sizeof(SpecState), cudaMemcpyDeviceToHost, st));
+    JL_CUDA(cudaStreamSynchronize(st));
+    JL_TRY(check_device_flag(m));
+    if (s->n_tokens < (int32_t)n + 1 || s->n_tokens > (int32_t)(n + count)) {
+        set_error("greedy loop ended in an inconsistent state (%d tokens)", s->n_tokens);
+        return JL_ERR_CUDA;
+    }
+    JL_CUDA(cudaMemcpy(out, g->tokens, (size_t)s->n_tokens * sizeof(uint32_t), cudaMemcpyDeviceToHost));
+    c->len = (size_t)s->target_len;
+    *out_len = (size_t)s->n_tokens;
+    return JL_OK;
+}
+
+namespace {
+
+double now_ms() {
+    return std::chrono::duration<double, std::milli>(
+               std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+// speculative.rs:43-143 with one host synchronisation per pass.
+jl_status spec_host(jl_model* T, jl_model* D, const uint32_t* prompt, size_t n, size_t limit,
+                    const jl_schedule& sched, const Oracle& o, jl_spec_result* r) {
+    jl_cache *tc = nullptr, *dc = nullptr;
+    JL_TRY(cache_create(T, &tc));
+    std::unique_ptr<jl_cache, void (*)(jl_cache*)> g1(tc, cache_free);
+    JL_TRY(cache_create(D, &dc));
+    std::unique_ptr<jl_cache, void (*)(jl_cache*)> g2(dc, cache_free);
+    std::vector<uint32_t> tokens(prompt, prompt + n);
+    uint32_t gamma = sched.gamma;
+    double t0 = now_ms();
+    uint32_t first = 0, dnext = 0;
+    JL_TRY(predict(T, tc, prompt, n, false, &first, nullptr));
+    JL_TRY(predict(D, dc, prompt, n, false, &dnext, nullptr));
+    dnext = oracle_token(o, (int32_t)dc->len, dnext);
+    int64_t first_pred = first;
+    r->prefill_passes = 2;
+    r->prefill_ms = now_ms() - t0;
+    const double decode0 = now_ms();
+    int64_t pending = -1;
+    std::vector<uint32_t> proposed, verification, checked(MAX_GAMMA + 2);
+    while (tokens.size() < limit) {
+        const size_t start = tokens.size();
+        const size_t budget = std::min<size_t>(gamma, limit - start);
+        proposed.clear();
+        double t = now_ms();
+        for (size_t i = 0; i < budget; ++i) {
+            proposed.push_back(dnext);
+            if (i + 1 == budget || (int32_t)dnext == T->eos) break;
+            uint32_t nx = 0;
+            JL_TRY(predict(D, dc, &dnext, 1, false, &nx, nullptr));
+            dnext = oracle_token(o, (int32_t)dc->len, nx);
+            r->draft_passes++;
+        }
+        r->draft_ms += now_ms() - t;
+        verification.clear();
+        if (pending >= 0) verification.push_back((uint32_t)pending);
+        verification.insert(verification.end(), proposed.begin(), proposed.end());
+        pending = -1;
+        t = now_ms();
+        checked.resize(verification.size());
+        JL_TRY(predict(T, tc, verification.data(), verification.size(), true, checked.data(), nullptr));
+        r->verify_passes++;
+        r->verify_ms += now_ms() - t;
+        std::vector<uint32_t> preds;
+        if (first_pred >= 0) preds.push_back((uint32_t)first_pred);
+        preds.insert(preds.end(), checked.begin(), checked.end());
+        first_pred = -1;
+        size_t accepted = 0;
+        uint32_t next = preds[0];
+        while (accepted < proposed.size() && proposed[accepted] == next) next = preds[++accepted];
+        const uint32_t g_before = gamma;
+        if (sched.adaptive && proposed.size() == gamma) {
+            if (accepted == proposed.size()) gamma = std::min(gamma + 1, sched.max_gamma);
+            else if (accepted < (proposed.size() + 1) / 2) gamma = std::max<uint32_t>(gamma / 2, 1);
+        }
+        if (r->rounds_out && r->rounds < r->rounds_cap)
+            r->rounds_out[r->rounds] = jl_round_stats{g_before, (uint32_t)proposed.size(),
+                                                      (uint32_t)accepted, gamma};
+        r->rounds++;
+        r->drafted += proposed.size();
+        r->accepted += accepted;
+        tokens.insert(tokens.end(), proposed.begin(), proposed.begin() + accepted);
+        if ((accepted > 0 && (int32_t)tokens.back() == T->eos) || tokens.size() == limit) break;
+        tc->len = start + accepted;                     // speculative.rs:127
+        dc->len = std::min(start + accepted, dc->len);  // speculative.rs:128
+        tokens.push_back(next);
+        if ((int32_t)next == T->eos || tokens.size() == limit) break;
+        pending = next;
+        const size_t tail = tokens.size() - dc->len;
+        t = now_ms();
+        uint32_t nx = 0;
+        JL_TRY(predict(D, dc, tokens.data() + dc->len, tail, false, &nx, nullptr));
+        dnext = oracle_token(o, (int32_t)dc->len, nx);
+        r->draft_passes++;
+        r->draft_ms += now_ms() - t;
+    }
+    r->decode_ms = now_ms() - decode0;
+    r->n_tokens = tokens.size();
+    memcpy(r->tokens, tokens.data(), tokens.size() * sizeof(uint32_t));
+    return JL_OK;
+}
+
+}  // namespace
+
+jl_status generate_speculative(jl_model* T, jl_model* D, const uint32_t* prompt, size_t n,
+                               size_t count, const jl_schedule& sched,
+                               const jl_spec_options& opts, jl_spec_result* r) {
+    if (n == 0) {
+        set_error("prompt is empty");
+        return JL_ERR_INVALID_ARG;
+    }
+    if (sched.gamma == 0 || sched.max_gamma < sched.gamma) {
+        set_error("gamma must be positive and no greater than max gamma");
+        return JL_ERR_INVALID_ARG;
+    }
+    if (T->vocab != D->vocab || T->eos != D->eos) {
+        // speculative.rs:42: both models must share token ids
+        set_error("target and draft must share the vocabulary");
+        return JL_ERR_INVALID_ARG;
+    }
+    if (T->device != D->device) {
+        set_error("target and draft must live on the same GPU");
+        return JL_ERR_INVALID_ARG;
+    }
+    if (T == D) {
+        set_error("use two model handles for target and draft (each owns its pass buffers)");
+        return JL_ERR_INVALID_ARG;
+    }
+    // speculative.rs:60-67
+    const size_t limit = std::min({n + count, (size_t)T->max_positions, (size_t)D->max_positions});
+    if (r->tokens_cap < std::max(limit, n)) {
+        set_error("tokens capacity %zu is below %zu", r->tokens_cap, std::max(limit, n));
+        return JL_ERR_INVALID_ARG;
+    }
+    JL_TRY(check_ids(T, prompt, n));
+    if (opts.oracle_stream && opts.oracle_p > 0) {
+        if (opts.oracle_p > 1.0) {
+            set_error("oracle_p must lie in [0, 1]");
+            return JL_ERR_INVALID_ARG;
+        }
+    }
+    if (opts.oracle_stream) JL_TRY(check_ids(T, opts.oracle_stream, opts.oracle_len));
+    const size_t keep_tokens_cap = r->tokens_cap, keep_rounds_cap = r->rounds_cap;
+    uint32_t* keep_tokens = r->tokens;
+    jl_round_stats* keep_rounds = r->rounds_out;
+    memset(r, 0, sizeof(*r));
+    r->tokens = keep_tokens;
+    r->tokens_cap = keep_tokens_cap;
+    r->rounds_out = keep_rounds;
+    r->rounds_cap = keep_rounds_cap;
+    memcpy(r->tokens, prompt, n * sizeof(uint32_t));
+    r->n_tokens = n;
+    if (n >= limit) return JL_OK;
+    JL_CUDA(cudaSetDevice(T->device));
+    Oracle host_oracle{opts.oracle_stream, (int32_t)std::min(opts.oracle_len, (size_t)INT32_MAX),
+                       opts.oracle_p, opts.oracle_seed, T->vocab};
+    if (opts.mode == JL_SPEC_HOST)
+        return spec_host(T, D, prompt, n, limit, sched, host_oracle, r);
+
+    const int G = (int)sched.max_gamma;
+    if (G > MAX_GAMMA) {
+        set_error("max gamma %d exceeds %d for the device loop", G, MAX_GAMMA);
+        return JL_ERR_INVALID_ARG;
+    }
+    jl_cache *tc = nullptr, *dc = nullptr;
+    JL_TRY(cache_create(T, &tc));
+    std::unique_ptr<jl_cache, void (*)(jl_cache*)> g1(tc, cache_free);
+    JL_TRY(cache_create(D, &dc));
+    std::unique_ptr<jl_cache, void (*)(jl_cache*)> g2(dc, cache_free);
+    cudaStream_t st = T->stream;
+    // prefill both models (speculative.rs:69-75)
+    JL_CUDA(cudaEventRecord(T->ev0, st));
+    uint32_t first = 0, dnext = 0;
+    JL_TRY(predict(T, tc, prompt, n, false, &first, nullptr));
+    JL_TRY(predict(D, dc, prompt, n, false, &dnext, nullptr));
+    JL_CUDA(cudaEventRecord(T->ev1, st));
+    JL_CUDA(cudaEventSynchronize(T->ev1));
+    r->prefill_ms = elapsed_ms(T->ev0, T->ev1);
+    r->prefill_passes = 2;
+    dnext = oracle_token(host_oracle, (int32_t)dc->len, dnext);
+
+    SpecGraph* g = nullptr;
+    JL_TRY(get_graph(T, D, G, &g));
+    // pages for every position the loop can reach
+    JL_TRY(cache_reserve(tc, limit + G + 1, st));
+    JL_TRY(cache_reserve(dc, limit + G + 1, st));
+    // oracle stream to the device
+    Oracle dev_oracle{nullptr, 0, opts.oracle_p, opts.oracle_seed, T->vocab};
+    if (opts.oracle_stream) {
+        const size_t len = std::min(opts.oracle_len, (size_t)g->oracle_cap);
+        JL_CUDA(cudaMemcpyAsync(g->oracle, opts.oracle_stream, len * sizeof(uint32_t),
+                                cudaMemcpyHostToDevice, st));
+        dev_oracle.stream = g->oracle;
+        dev_oracle.len = (int32_t)len;
+    }
+    if (memcmp(&dev_oracle, &g->oracle_args, sizeof(Oracle)) != 0) {
+        // oracle settings are kernel arguments: rebuild the graph when they change
+        g->oracle_args = dev_oracle;
+        if (g->exec) cudaGraphExecDestroy(g->exec);
+        g->exec = nullptr;
+        JL_TRY(build_spec_graph(g));
+    }
+    SpecState* s = g->host_st;
+    memset(s, 0, sizeof(SpecState));
+    s->n_tokens = (int32_t)n;
+    s->limit = (int32_t)limit;
+    s->eos = T->eos;
+    s->gamma = (int32_t)sched.gamma;
+    s->max_gamma = (int32_t)sched.max_gamma;
+    s->adaptive = sched.adaptive ? 1 : 0;
+    s->pending = -1;
+    s->first_pred = (int32_t)first;
+    s->draft_next = (int32_t)dnext;
+    s->target_len = (int32_t)tc->len;
+    s->draft_len = (int32_t)dc->len;
+    JL_CUDA(cudaMemcpyAsync(g->st, s, sizeof(SpecState), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(g->tokens, prompt, n * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+    // both models read sequence 0 from their own cache's page table
+    T->host_page_table[0] = tc->d_pages;
+    D->host_page_table[0] = dc->d_pages;
+    JL_CUDA(cudaMemcpyAsync(T->pass.page_table, T->host_page_table, sizeof(int32_t*),
+                            cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(D->pass.page_table, D->host_page_table, sizeof(int32_t*),
+                            cudaMemcpyHostToDevice, st));
+    // the draft's stream must not still be using its pass buffers
+    JL_CUDA(cudaStreamSynchronize(D->stream));
+    JL_CUDA(cudaEventRecord(T->ev0, st));
+    JL_CUDA(cudaGraphLaunch(g->exec, st));
+    JL_CUDA(cudaEventRecord(T->ev1, st));
+    JL_CUDA(cudaMemcpyAsync(s, g->st, sizeof(SpecState), cudaMemcpyDeviceToHost, st));
+    JL_CUDA(cudaStreamSynchronize(st));
+    r->decode_ms = elapsed_ms(T->ev0, T->ev1);
+    JL_TRY(check_device_flag(T));
+    JL_TRY(check_device_flag(D));
+    if (s->fault || s->n_tokens < (int32_t)n || s->n_tokens > (int32_t)limit) {
+        set_error("device loop ended in an inconsistent state (%d tokens)", s->n_tokens);
+        return JL_ERR_CUDA;
+    }
+    JL_CUDA(cudaMemcpy(r->tokens, g->tokens, (size_t)s->n_tokens * sizeof(uint32_t),
+                       cudaMemcpyDeviceToHost));
+    if (r->rounds_out && r->rounds_cap)
+        JL_CUDA(cudaMemcpy(r->rounds_out, g->rounds,
+                           std::min((size_t)s->rounds, r->rounds_cap) * sizeof(jl_round_stats),
+                           cudaMemcpyDeviceToHost));
+    r->n_tokens = (size_t)s->n_tokens;
+    r->drafted = (size_t)s->drafted;
+    r->accepted = (size_t)s->accepted;
+    r->rounds = (size_t)s->rounds;
+    r->draft_passes = (size_t)s->draft_passes;
+    r->verify_passes = (size_t)s->verify_passes;
+    tc->len = (size_t)s->target_len;
+    dc->len = (size_t)s->draft_len;
+    return JL_OK;
+}
+
+}  // namespace jl

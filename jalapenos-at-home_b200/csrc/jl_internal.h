@@ -1,0 +1,254 @@
+// Internal declarations of the B200 Qwen3 decode engine.
+//
+// Data layout in HBM (one CUDA context per GPU, one model per handle):
+//  * Weights live in one arena.  A projection is row-major [out, in]:
+//    bf16 as u16[out*in]; MXFP4 exactly as the reference checkpoint stores it
+//    (python/quantize_mxfp4.py:37-38): packed u8[out, in/2] with the even
+//    element in the low nibble, and E8M0 scales u8[out, in/32].
+//  * The KV cache is a pool of pages of PAGE tokens shared by every cache of a
+//    model: [layer][K|V][page][kv_head][PAGE][128], bf16 or f32.  A cache is a
+//    page table plus a length; truncation (KvCache::truncate,
+//    engine/src/model.rs:45-51) only moves the length.
+//  * A forward pass reads its rows (token, sequence, position) from a
+//    device-resident PassBuf, so one captured CUDA graph serves any row count
+//    up to the bucket it was captured for.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/jalapeno.h"
+
+namespace jl {
+
+constexpr int HEAD = 128;        // head_dim of every Qwen3 model (engine/src/lib.rs:24)
+constexpr int HALF = 64;         // RoPE rotates (i, i + 64) pairs (engine/src/lib.rs:297)
+constexpr int PAGE = 64;         // tokens per KV page
+constexpr int SMALL_M = 32;      // passes up to this many rows use the skinny kernels
+constexpr int MAX_SEQS = 64;     // sequences one pass may touch
+constexpr int MAX_GAMMA = 16;    // largest draft length of the device-resident loop
+
+// ---- errors --------------------------------------------------------------
+
+void set_error(const char* fmt, ...) __attribute__((format(printf, 1, 2)));
+const char* last_error();
+
+struct Status {
+    jl_status code = JL_OK;
+    bool ok() const { return code == JL_OK; }
+};
+
+#define JL_TRY(expr)                                   \
+    do {                                               \
+        jl_status _s = (expr);                         \
+        if (_s != JL_OK) return _s;                    \
+    } while (0)
+
+jl_status cuda_fail(cudaError_t e, const char* what, const char* file, int line);
+#define JL_CUDA(call)                                                          \
+    do {                                                                       \
+        cudaError_t _e = (call);                                               \
+        if (_e != cudaSuccess) return ::jl::cuda_fail(_e, #call, __FILE__, __LINE__); \
+    } while (0)
+
+// ---- host weights (engine::load) -------------------------------------------
+
+struct HostTensor {
+    std::string name;
+    jl_dtype dtype = JL_BF16;
+    std::vector<size_t> shape;       // logical shape
+    std::vector<uint16_t> bf16;      // JL_BF16
+    std::vector<uint8_t> packed;     // JL_MXFP4
+    std::vector<uint8_t> scales;     // JL_MXFP4
+};
+
+struct HostConfig {
+    int layers = 0, max_positions = 0, eos = 0;
+};
+
+}  // namespace jl
+
+struct jl_weights {
+    std::map<std::string, jl::HostTensor> tensors;
+};
+
+namespace jl {
+
+jl_status load_weights(const std::string& dir, jl_weights* out);
+jl_status load_config(const std::string& dir, HostConfig* out);
+
+// ---- device structures -------------------------------------------------------
+
+enum MatKind : int { MAT_BF16 = 0, MAT_MXFP4 = 1 };
+
+struct Mat {
+    int kind = MAT_BF16;
+    int rows = 0, cols = 0;
+    const void* data = nullptr;      // bf16 [rows][cols] or packed [rows][cols/2]
+    const uint8_t* scales = nullptr; // [rows][cols/32] for MXFP4
+    size_t bytes() const {
+        return kind == MAT_MXFP4 ? (size_t)rows * cols / 2 + (size_t)rows * cols / 32
+                                 : (size_t)rows * cols * 2;
+    }
+};
+
+struct LayerW {
+    Mat q, k, v, o, gate, up, down;
+    const uint16_t* in_ln = nullptr;
+    const uint16_t* post_ln = nullptr;
+    const uint16_t* q_norm = nullptr;
+    const uint16_t* k_norm = nullptr;
+};
+
+struct RowDesc {
+    uint32_t token;
+    int32_t seq;   // index into PassBuf::page_table
+    int32_t pos;   // absolute position of this token in its sequence
+    int32_t pad;
+};
+
+struct PassHdr {
+    int32_t rows;       // active rows of this pass
+    int32_t head_rows;  // rows whose next token is predicted
+    int32_t pad0, pad1;
+};
+
+// Device pointers describing one pass; written by the host (jl_predict) or by
+// the speculative-loop kernels, read by every pass kernel.
+struct PassBuf {
+    PassHdr* hdr = nullptr;
+    RowDesc* row = nullptr;            // [max_rows]
+    int32_t* head_row = nullptr;       // [max_rows] row index of each predicted row
+    const int32_t** page_table = nullptr;  // [MAX_SEQS]
+    uint32_t* out_ids = nullptr;       // [max_rows]
+};
+
+struct Scratch {
+    float* x = nullptr;       // [rows, hidden] residual stream
+    float* xn = nullptr;      // [rows, max(hidden, q_width)] normalised input
+    float* qkv = nullptr;     // [rows, q_width + 2*kv_width]
+    float* attn = nullptr;    // [rows, q_width]
+    float* act = nullptr;     // [rows, inter] silu(gate) * up
+    float* xh = nullptr;      // [rows, hidden] final-norm rows to predict
+    float* logits = nullptr;  // [rows, vocab]
+};
+
+struct KvPool {
+    jl_kv_dtype dtype = JL_KV_BF16;
+    int elem = 2;
+    size_t pages = 0;
+    void* base = nullptr;                 // [layers][2][pages][kv_heads][PAGE][HEAD]
+    std::vector<int32_t> free_list;
+    size_t page_elems = 0;                // kv_heads * PAGE * HEAD
+};
+
+struct SpecGraph;  // device-resident speculative loop (engine.cu)
+
+}  // namespace jl
+
+struct jl_model {
+    int device = 0;
+    int layers = 0, hidden = 0, q_heads = 0, kv_heads = 0, inter = 0, vocab = 0;
+    int max_positions = 0, eos = 0;
+    bool tied = false;
+    jl::Mat embed, head;
+    const uint16_t* final_norm = nullptr;
+    std::vector<jl::LayerW> lw;
+    void* arena = nullptr;
+    size_t arena_bytes = 0;
+    float2* rope = nullptr;               // [max_positions][HALF] (cos, sin)
+    jl::KvPool kv;
+    int max_rows = 0;
+    jl::PassBuf pass;                     // device
+    jl::PassHdr* host_hdr = nullptr;      // pinned staging for jl_predict
+    jl::RowDesc* host_row = nullptr;
+    int32_t* host_head_row = nullptr;
+    const int32_t** host_page_table = nullptr;
+    uint32_t* host_out = nullptr;
+    float* host_logits = nullptr;
+    jl::Scratch s;
+    void* scratch_arena = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    cudaGraphExec_t small_graph = nullptr;  // full pass, rows <= SMALL_M
+    std::vector<jl::SpecGraph*> spec_graphs;  // owned; freed by model_free
+    int* counters = nullptr;              // zeroed split-K / reduction counters
+    std::map<std::string, std::pair<const void*, size_t>> tensor_index;  // name -> device bytes
+};
+
+struct jl_cache {
+    jl_model* m = nullptr;
+    std::vector<int32_t> pages;
+    int32_t* d_pages = nullptr;           // device page table [max_pages]
+    int32_t* h_pages = nullptr;           // pinned mirror
+    size_t max_pages = 0;
+    size_t len = 0;
+};
+
+namespace jl {
+
+// ---- model construction (model.cu) --------------------------------------------
+jl_status model_from_weights(jl_weights* w, const HostConfig& cfg, const jl_model_options& o,
+                             jl_model** out);
+jl_status model_synthesize(const jl_synth_config& c, const jl_model_options& o, jl_model** out);
+void model_free(jl_model* m);
+jl_status cache_create(jl_model* m, jl_cache** out);
+void cache_free(jl_cache* c);
+jl_status cache_reserve(jl_cache* c, size_t tokens, cudaStream_t stream);
+
+// ---- passes and generation (engine.cu) ---------------------------------------
+// Records the kernels of one forward pass on `stream`.  rows_cap bounds the
+// rows the pass may have; `layers` < m->layers stops early (Model::hidden);
+// with_head adds final norm, lm_head and argmax.
+jl_status record_pass(jl_model* m, cudaStream_t stream, int rows_cap, int layers, bool with_head);
+struct PassCtx;
+jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head);
+// Sets kernel attributes once per device, before any stream capture.
+jl_status configure_kernels();
+jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool all,
+                  uint32_t* out_ids, float* out_logits);
+jl_status hidden(jl_model* m, const uint32_t* ids, size_t n, size_t layers, float* out);
+jl_status time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t rows, size_t reps,
+                    double* wall_ms, double* gpu_ms);
+jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters, double* ms,
+                          size_t* bytes);
+jl_status generate(jl_model* m, const uint32_t* prompt, size_t n, size_t count, uint32_t* out,
+                   size_t cap, size_t* out_len);
+jl_status generate_speculative(jl_model* target, jl_model* draft, const uint32_t* prompt,
+                               size_t n, size_t count, const jl_schedule& sched,
+                               const jl_spec_options& opts, jl_spec_result* res);
+void spec_graph_free(SpecGraph* g);
+
+// ---- kernel launchers (kernels.cu) ---------------------------------------------
+struct PassCtx {
+    const jl_model* m;
+    cudaStream_t stream;
+    int rows_cap;   // rows the pass may hold
+    int head_cap;   // predicted rows the pass may hold
+};
+jl_status launch_embed(const PassCtx& c);
+jl_status launch_rmsnorm(const PassCtx& c, const float* x, const uint16_t* w, float* out,
+                         bool head_rows);
+jl_status launch_qkv(const PassCtx& c, const LayerW& L);
+jl_status launch_qk_rope_kv(const PassCtx& c, int layer, const LayerW& L);
+jl_status launch_attention(const PassCtx& c, int layer);
+jl_status launch_o(const PassCtx& c, const LayerW& L);
+jl_status launch_gateup(const PassCtx& c, const LayerW& L);
+jl_status launch_down(const PassCtx& c, const LayerW& L);
+jl_status launch_head(const PassCtx& c);
+jl_status launch_argmax(const PassCtx& c);
+
+jl_status launch_synth_bf16(uint64_t seed, uint32_t tensor_index, size_t n, uint16_t* out,
+                            cudaStream_t stream);
+jl_status launch_fill_u16(uint16_t* out, size_t n, uint16_t value, cudaStream_t stream);
+jl_status launch_quantize_mxfp4(const uint16_t* bf16, int rows, int cols, uint8_t* packed,
+                                uint8_t* scales, cudaStream_t stream);
+
+}  // namespace jl

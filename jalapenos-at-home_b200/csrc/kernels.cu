@@ -1,0 +1,848 @@
+// Forward-pass kernels for sm_100a, first generation (CUDA cores).
+//
+// Every kernel reads its row count from the device PassHdr, so a pass
+// recorded once into a CUDA graph replays for any number of rows.  Every
+// output value is computed by one warp in a fixed order that does not depend
+// on how many rows the pass holds: a token's logits are bit-identical whether
+// it is decoded alone, verified among k+1 draft tokens, or fed in a two-row
+// draft catch-up.  That is what makes speculative output equal greedy output
+// exactly (engine/tests/generation.rs:69-92 asserts it on the reference).
+#include <cstdio>
+
+#include "jl_internal.h"
+#include "kernels.cuh"
+
+namespace jl {
+
+namespace {
+
+enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+
+// Up to three matrices stacked along the output dimension (q, k, v), or the
+// (gate, up) pair of EPI_SWIGLU.  All share the input width K and kind.
+struct Proj {
+    const void* w[3];
+    const uint8_t* s[3];
+    int n[3];
+    int K;
+    int total;  // output columns (EPI_SWIGLU: rows of one matrix)
+};
+
+__device__ __forceinline__ void pick(const Proj& p, int r, int& mat, int& local) {
+    if (r < p.n[0]) { mat = 0; local = r; }
+    else if (r < p.n[0] + p.n[1]) { mat = 1; local = r - p.n[0]; }
+    else { mat = 2; local = r - p.n[0] - p.n[1]; }
+}
+
+// Shared-memory slot of 16-byte x chunk c.  MXFP4 lanes read the eight
+// chunks of one 32-element block each; bf16 lanes read two adjacent chunks.
+// The XOR swizzles keep every 8-lane phase of an LDS.128 on distinct banks.
+__device__ __forceinline__ int swz_mx(int c) { return c ^ ((c >> 3) & 7); }
+__device__ __forceinline__ int swz_bf(int c) { return c ^ ((c >> 3) & 1); }
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    // lib.rs:462: (gate / (1 + exp(-gate))) * up
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+// ---------------------------------------------------------------------------
+// Skinny projection: y[m, r] (op)= sum_k x[m, k] * W[r, k] for M <= SMALL_M.
+// CTA = 8 warps; a warp owns R output rows at a time, its lanes split K;
+// MR input rows are staged in shared memory per sweep over the weights.
+
+template <int KIND, int EPI, int R, int MR>
+__global__ void __launch_bounds__(256) k_skinny(const PassHdr* __restrict__ hdr, int use_head,
+                                                int max_m, const float* __restrict__ x, int ldx, Proj p,
+                                                float* __restrict__ y, int ldy) {
+    extern __shared__ float4 xs4[];
+    const int M = min(use_head ? hdr->head_rows : hdr->rows, max_m);  // never past the buffers
+    const int K = p.K, K4 = K >> 2;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int groups = (p.total + R - 1) / R;
+    constexpr int NV = EPI == EPI_SWIGLU ? 2 : 1;  // dot products per output
+    for (int m0 = 0; m0 < M; m0 += MR) {
+        const int mr = min(MR, M - m0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < MR * K4; i += blockDim.x) {
+            const int m = i / K4, c = i - m * K4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (m < mr) v = reinterpret_cast<const float4*>(x + (size_t)(m0 + m) * ldx)[c];
+            xs4[m * K4 + (KIND == MAT_MXFP4 ? swz_mx(c) : swz_bf(c))] = v;
+        }
+        __syncthreads();
+        for (int g = blockIdx.x * 8 + warp; g < groups; g += gridDim.x * 8) {
+            const uint8_t* wrow[R][NV];
+            const uint8_t* srow[R][NV];
+            bool valid[R];
+#pragma unroll
+            for (int j = 0; j < R; ++j) {
+                const int r = g * R + j;
+                valid[j] = r < p.total;
+                const int rr = valid[j] ? r : 0;
+#pragma unroll
+                for (int v = 0; v < NV; ++v) {
+                    int mat, local;
+                    if (EPI == EPI_SWIGLU) { mat = v; local = rr; }
+                    else pick(p, rr, mat, local);
+                    if (KIND == MAT_MXFP4) {
+                        wrow[j][v] = (const uint8_t*)p.w[mat] + (size_t)local * (K >> 1);
+                        srow[j][v] = p.s[mat] + (size_t)local * (K >> 5);
+                    } else {
+                        wrow[j][v] = (const uint8_t*)p.w[mat] + (size_t)local * K * 2;
+                        srow[j][v] = nullptr;
+                    }
+                }
+            }
+            float acc[R][NV][MR];
+#pragma unroll
+            for (int j = 0; j < R; ++j)
+#pragma unroll
+                for (int v = 0; v < NV; ++v)
+#pragma unroll
+                    for (int m = 0; m < MR; ++m) acc[j][v][m] = 0.f;
+
+            if (KIND == MAT_MXFP4) {
+                const int nb = K >> 5;
+                for (int b = lane; b < nb; b += 32) {
+                    uint4 wv[R][NV];
+                    uint32_t sb[R][NV];
+#pragma unroll
+                    for (int j = 0; j < R; ++j)
+#pragma unroll
+                        for (int v = 0; v < NV; ++v) {
+                            wv[j][v] = valid[j] ? ldg_stream(wrow[j][v] + (size_t)b * 16)
+                                                : make_uint4(0, 0, 0, 0);
+                            sb[j][v] = valid[j] ? srow[j][v][b] : 127u;
+                        }
+                    float part[R][NV][MR];
+#pragma unroll
+                    for (int j = 0; j < R; ++j)
+#pragma unroll
+                        for (int v = 0; v < NV; ++v)
+#pragma unroll
+                            for (int m = 0; m < MR; ++m) part[j][v][m] = 0.f;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        float4 xv[MR];
+#pragma unroll
+                        for (int m = 0; m < MR; ++m) xv[m] = xs4[m * K4 + b * 8 + (q ^ (b & 7))];
+#pragma unroll
+                        for (int j = 0; j < R; ++j)
+#pragma unroll
+                            for (int v = 0; v < NV; ++v) {
+                                const uint32_t w4 = q < 2 ? wv[j][v].x : q < 4 ? wv[j][v].y
+                                                  : q < 6 ? wv[j][v].z : wv[j][v].w;
+                                const uint32_t word = w4 >> ((q & 1) * 16);
+                                const float l0 = e2m1(word), l1 = e2m1(word >> 4);
+                                const float l2 = e2m1(word >> 8), l3 = e2m1(word >> 12);
+#pragma unroll
+                                for (int m = 0; m < MR; ++m) {
+                                    float a = part[j][v][m];
+                                    a = fmaf(l0, xv[m].x, a);
+                                    a = fmaf(l1, xv[m].y, a);
+                                    a = fmaf(l2, xv[m].z, a);
+                                    a = fmaf(l3, xv[m].w, a);
+                                    part[j][v][m] = a;
+                                }
+                            }
+                    }
+#pragma unroll
+                    for (int j = 0; j < R; ++j)
+#pragma unroll
+                        for (int v = 0; v < NV; ++v) {
+                            const float sc = e8m0(sb[j][v]);
+#pragma unroll
+                            for (int m = 0; m < MR; ++m)
+                                acc[j][v][m] = fmaf(part[j][v][m], sc, acc[j][v][m]);
+                        }
+                }
+            } else {
+                for (int e0 = lane * 8; e0 < K; e0 += 256) {
+                    uint4 wv[R][NV];
+#pragma unroll
+                    for (int j = 0; j < R; ++j)
+#pragma unroll
+                        for (int v = 0; v < NV; ++v)
+                            wv[j][v] = valid[j] ? ldg_stream(wrow[j][v] + (size_t)e0 * 2)
+                                                : make_uint4(0, 0, 0, 0);
+                    const int c = e0 >> 2;
+                    float4 xa[MR], xb[MR];
+#pragma unroll
+                    for (int m = 0; m < MR; ++m) {
+                        xa[m] = xs4[m * K4 + swz_bf(c)];
+                        xb[m] = xs4[m * K4 + swz_bf(c + 1)];
+                    }
+#pragma unroll
+                    for (int j = 0; j < R; ++j)
+#pragma unroll
+                        for (int v = 0; v < NV; ++v) {
+                            const uint4 w = wv[j][v];
+                            const float w0 = __uint_as_float(w.x << 16), w1 = __uint_as_float(w.x & 0xffff0000u);
+                            const float w2 = __uint_as_float(w.y << 16), w3 = __uint_as_float(w.y & 0xffff0000u);
+                            const float w4 = __uint_as_float(w.z << 16), w5 = __uint_as_float(w.z & 0xffff0000u);
+                            const float w6 = __uint_as_float(w.w << 16), w7 = __uint_as_float(w.w & 0xffff0000u);
+#pragma unroll
+                            for (int m = 0; m < MR; ++m) {
+                                float a = acc[j][v][m];
+                                a = fmaf(w0, xa[m].x, a);
+                                a = fmaf(w1, xa[m].y, a);
+                                a = fmaf(w2, xa[m].z, a);
+                                a = fmaf(w3, xa[m].w, a);
+                                a = fmaf(w4, xb[m].x, a);
+                                a = fmaf(w5, xb[m].y, a);
+                                a = fmaf(w6, xb[m].z, a);
+                                a = fmaf(w7, xb[m].w, a);
+                                acc[j][v][m] = a;
+                            }
+                        }
+                }
+            }
+            // fixed-order reduction across the 32 lanes
+#pragma unroll
+            for (int j = 0; j < R; ++j)
+#pragma unroll
+                for (int v = 0; v < NV; ++v)
+#pragma unroll
+                    for (int m = 0; m < MR; ++m) acc[j][v][m] = warp_sum(acc[j][v][m]);
+            if (lane == 0) {
+#pragma unroll
+                for (int j = 0; j < R; ++j) {
+                    if (!valid[j]) continue;
+                    const int r = g * R + j;
+#pragma unroll
+                    for (int m = 0; m < MR; ++m) {
+                        if (m >= mr) continue;
+                        float* out = y + (size_t)(m0 + m) * ldy + r;
+                        if (EPI == EPI_STORE) *out = acc[j][0][m];
+                        else if (EPI == EPI_ADD) *out = __fadd_rn(*out, acc[j][0][m]);
+                        else *out = silu_mul(acc[j][0][m], acc[j][NV - 1][m]);
+                    }
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Tiled projection for long prompts (M > SMALL_M): 64 tokens x 64 outputs per
+// CTA, weights decoded to exact f32 in shared memory.
+
+template <int KIND, int EPI>
+__global__ void __launch_bounds__(256) k_gemm(const PassHdr* __restrict__ hdr, int use_head,
+                                              int max_m, const float* __restrict__ x, int ldx, Proj p,
+                                              float* __restrict__ y, int ldy) {
+    constexpr int BM = 64, BN = 64, BK = 32;
+    constexpr int NV = EPI == EPI_SWIGLU ? 2 : 1;
+    __shared__ float xs[BK][BM + 4];
+    __shared__ float ws[NV][BK][BN + 4];
+    const int M = min(use_head ? hdr->head_rows : hdr->rows, max_m);  // never past the buffers
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    if (m0 >= M || n0 >= p.total) return;
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int K = p.K;
+    float acc[NV][4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += BK) {
+        // x tile: 64 rows x 32 k, transposed into xs[k][m]
+        for (int i = tid; i < BM * BK / 4; i += 256) {
+            const int m = i / (BK / 4), c = i % (BK / 4);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (m0 + m < M) v = *reinterpret_cast<const float4*>(x + (size_t)(m0 + m) * ldx + k0 + c * 4);
+            xs[c * 4 + 0][m] = v.x;
+            xs[c * 4 + 1][m] = v.y;
+            xs[c * 4 + 2][m] = v.z;
+            xs[c * 4 + 3][m] = v.w;
+        }
+        // weight tile: 64 output rows x 32 k
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            if (KIND == MAT_MXFP4) {
+                if (tid < BN) {
+                    const int r = n0 + tid;
+                    float vals[32];
+                    if (r < p.total) {
+                        int mat, local;
+                        if (EPI == EPI_SWIGLU) { mat = v; local = r; }
+                        else pick(p, r, mat, local);
+                        const uint8_t* wr = (const uint8_t*)p.w[mat] + (size_t)local * (K >> 1) + (k0 >> 1);
+                        const uint4 wv = *reinterpret_cast<const uint4*>(wr);
+                        const float sc = e8m0(p.s[mat][(size_t)local * (K >> 5) + (k0 >> 5)]);
+                        const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            vals[e] = __fmul_rn(e2m1(words[e >> 3] >> ((e & 7) * 4)), sc);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) vals[e] = 0.f;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) ws[v][e][tid] = vals[e];
+                }
+            } else {
+                for (int i = tid; i < BN * BK / 8; i += 256) {
+                    const int n = i / (BK / 8), c = i % (BK / 8);
+                    const int r = n0 + n;
+                    uint4 wv = make_uint4(0, 0, 0, 0);
+                    if (r < p.total) {
+                        int mat, local;
+                        if (EPI == EPI_SWIGLU) { mat = v; local = r; }
+                        else pick(p, r, mat, local);
+                        wv = *reinterpret_cast<const uint4*>((const uint16_t*)p.w[mat] + (size_t)local * K + k0 + c * 8);
+                    }
+                    const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        ws[v][c * 8 + e][n] = __uint_as_float(e & 1 ? (words[e >> 1] & 0xffff0000u)
+                                                                    : (words[e >> 1] << 16));
+                }
+            }
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < BK; ++k) {
+            float a[4], b[NV][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = xs[k][ty * 4 + i];
+#pragma unroll
+            for (int v = 0; v < NV; ++v)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) b[v][i] = ws[v][k][tx * 4 + i];
+#pragma unroll
+            for (int v = 0; v < NV; ++v)
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) acc[v][i][jj] = fmaf(a[i], b[v][jj], acc[v][i][jj]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + ty * 4 + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const int n = n0 + tx * 4 + jj;
+            if (n >= p.total) continue;
+            float* out = y + (size_t)m * ldy + n;
+            if (EPI == EPI_STORE) *out = acc[0][i][jj];
+            else if (EPI == EPI_ADD) *out = __fadd_rn(*out, acc[0][i][jj]);
+            else *out = silu_mul(acc[0][i][jj], acc[NV - 1][i][jj]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+
+__global__ void k_embed(PassBuf pb, Mat e, float* __restrict__ x, int hidden) {
+    // lib.rs:213-235, model.rs:167-170
+    const int row = blockIdx.x;
+    if (row >= pb.hdr->rows) return;
+    uint32_t tok = pb.row[row].token;
+    if (tok >= (uint32_t)e.rows) tok = 0;  // ids are validated on the host
+    float* out = x + (size_t)row * hidden;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        const size_t idx = (size_t)tok * hidden + i;
+        if (e.kind == MAT_MXFP4) {
+            const uint8_t byte = ((const uint8_t*)e.data)[idx >> 1];
+            const float v = __fmul_rn(e2m1(byte >> ((idx & 1) * 4)), e8m0(e.scales[idx >> 5]));
+            out[i] = __uint_as_float(__float_as_uint(v) & 0xffff0000u);  // truncation, lib.rs:227
+        } else {
+            out[i] = bf16f(((const uint16_t*)e.data)[idx]);
+        }
+    }
+}
+
+__global__ void k_rmsnorm(PassBuf pb, const float* __restrict__ x, int ldx,
+                          const uint16_t* __restrict__ w, float* __restrict__ out, int ldo,
+                          int width, int head_rows) {
+    // lib.rs:268-290: x / sqrt(mean(x^2) + 1e-6) * w
+    __shared__ float red[32];
+    const int i = blockIdx.x;
+    const int n = head_rows ? pb.hdr->head_rows : pb.hdr->rows;
+    if (i >= n) return;
+    const int src = head_rows ? pb.head_row[i] : i;
+    const float* xr = x + (size_t)src * ldx;
+    float ss = 0.f;
+    for (int j = threadIdx.x; j < width; j += blockDim.x) ss = fmaf(xr[j], xr[j], ss);
+    ss = block_sum(ss, red);
+    const float size = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)width), 1e-6f));
+    float* o = out + (size_t)i * ldo;
+    for (int j = threadIdx.x; j < width; j += blockDim.x)
+        o[j] = __fmul_rn(__fdiv_rn(xr[j], size), bf16f(w[j]));
+}
+
+struct KvView {
+    void* k;       // this layer's K pages
+    void* v;       // this layer's V pages
+    int kv_heads;
+    int f32;       // 1: f32 elements, 0: bf16
+    int pages;     // pool size: page ids outside [0, pages) are never dereferenced
+    int max_pos;   // RoPE table rows (context limit)
+    int* err;      // device error flag: bit 0 page id out of range, bit 1 bad position
+};
+
+__device__ __forceinline__ bool page_ok(const KvView& kv, int page) {
+    if ((unsigned)page < (unsigned)kv.pages) return true;
+    atomicOr(kv.err, 1);
+    return false;
+}
+
+__device__ __forceinline__ size_t kv_index(int page, int kvh, int t, int kv_heads) {
+    return (((size_t)page * kv_heads + kvh) * PAGE + t) * HEAD;
+}
+
+// Per-head QK-RMSNorm and RoPE of q and k, then K and V appended to the cache
+// (lib.rs:363-396): one warp per head, lane owns dims {l, l+32, l+64, l+96}
+// so both RoPE pairs (i, i+64) stay in the lane.
+__global__ void __launch_bounds__(256) k_qk_rope_kv(PassBuf pb, float* __restrict__ qkv, int ld,
+                                                    int q_heads, const uint16_t* __restrict__ qn,
+                                                    const uint16_t* __restrict__ kn,
+                                                    const float2* __restrict__ rope, KvView kv) {
+    const int row = blockIdx.x;
+    if (row >= pb.hdr->rows) return;
+    const RowDesc rd = pb.row[row];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kv_heads = kv.kv_heads;
+    const int heads = q_heads + 2 * kv_heads;
+    if (rd.pos < 0 || rd.pos >= kv.max_pos || (unsigned)rd.seq >= (unsigned)MAX_SEQS) {
+        atomicOr(kv.err, 2);
+        return;
+    }
+    const int32_t* pt = pb.page_table[rd.seq];
+    const int page = pt[rd.pos / PAGE], t = rd.pos % PAGE;
+    if (!page_ok(kv, page)) return;
+    float* base = qkv + (size_t)row * ld;
+    for (int h = warp; h < heads; h += 8) {
+        float* src = base + h * HEAD;  // q heads, then k heads, then v heads
+        float a0 = src[lane], a1 = src[lane + 32], a2 = src[lane + 64], a3 = src[lane + 96];
+        if (h < q_heads + kv_heads) {
+            const uint16_t* gw = h < q_heads ? qn : kn;
+            float ss = fmaf(a0, a0, fmaf(a1, a1, fmaf(a2, a2, a3 * a3)));
+            ss = warp_sum(ss);
+            const float size = sqrtf(__fadd_rn(__fdiv_rn(ss, 128.0f), 1e-6f));
+            a0 = __fmul_rn(__fdiv_rn(a0, size), bf16f(gw[lane]));
+            a1 = __fmul_rn(__fdiv_rn(a1, size), bf16f(gw[lane + 32]));
+            a2 = __fmul_rn(__fdiv_rn(a2, size), bf16f(gw[lane + 64]));
+            a3 = __fmul_rn(__fdiv_rn(a3, size), bf16f(gw[lane + 96]));
+            // lib.rs:306-313: out[i] = a cos - b sin; out[i+64] = b cos + a sin
+            const float2 r0 = rope[(size_t)rd.pos * HALF + lane];
+            const float2 r1 = rope[(size_t)rd.pos * HALF + lane + 32];
+            const float b0 = __fsub_rn(__fmul_rn(a0, r0.x), __fmul_rn(a2, r0.y));
+            const float b2 = __fadd_rn(__fmul_rn(a2, r0.x), __fmul_rn(a0, r0.y));
+            const float b1 = __fsub_rn(__fmul_rn(a1, r1.x), __fmul_rn(a3, r1.y));
+            const float b3 = __fadd_rn(__fmul_rn(a3, r1.x), __fmul_rn(a1, r1.y));
+            a0 = b0; a1 = b1; a2 = b2; a3 = b3;
+        }
+        if (h < q_heads) {
+            src[lane] = a0; src[lane + 32] = a1; src[lane + 64] = a2; src[lane + 96] = a3;
+        } else {
+            const bool is_k = h < q_heads + kv_heads;
+            const int kvh = is_k ? h - q_heads : h - q_heads - kv_heads;
+            const size_t idx = kv_index(page, kvh, t, kv_heads);
+            if (kv.f32) {
+                float* d = (float*)(is_k ? kv.k : kv.v) + idx;
+                d[lane] = a0; d[lane + 32] = a1; d[lane + 64] = a2; d[lane + 96] = a3;
+            } else {
+                uint16_t* d = (uint16_t*)(is_k ? kv.k : kv.v) + idx;
+                d[lane] = f2bf16(a0); d[lane + 32] = f2bf16(a1);
+                d[lane + 64] = f2bf16(a2); d[lane + 96] = f2bf16(a3);
+            }
+        }
+    }
+}
+
+template <int F32>
+__device__ __forceinline__ float kv_load(const void* base, size_t idx) {
+    if (F32) return ((const float*)base)[idx];
+    return bf16f(((const uint16_t*)base)[idx]);
+}
+
+// Causal GQA attention for one (q head, row): softmax(q.k / sqrt(128)) . v
+// over positions [0, pos] of the row's sequence (lib.rs:401-441), in chunks
+// of 128 positions with a running max.
+template <int F32>
+__global__ void __launch_bounds__(128) k_attention(PassBuf pb, const float* __restrict__ qkv,
+                                                   int ld, int q_heads, int group, KvView kv,
+                                                   float* __restrict__ out) {
+    __shared__ float qs[HEAD];
+    __shared__ float pr[128];
+    __shared__ float red[32];
+    const int h = blockIdx.x, row = blockIdx.y;
+    if (row >= pb.hdr->rows) return;
+    const RowDesc rd = pb.row[row];
+    const int t = threadIdx.x;
+    const int kvh = h / group;
+    if (rd.pos < 0 || rd.pos >= kv.max_pos || (unsigned)rd.seq >= (unsigned)MAX_SEQS) {
+        if (t == 0) atomicOr(kv.err, 2);
+        out[(size_t)row * (q_heads * HEAD) + h * HEAD + t] = 0.f;
+        return;
+    }
+    const int visible = rd.pos + 1;
+    const int32_t* pt = pb.page_table[rd.seq];
+    qs[t] = qkv[(size_t)row * ld + h * HEAD + t];
+    __syncthreads();
+    const float scale = sqrtf(128.0f);
+    float m = -INFINITY, l = 0.f, acc = 0.f;
+    for (int s0 = 0; s0 < visible; s0 += 128) {
+        const int s = s0 + t;
+        float sc = -INFINITY;
+        if (s < visible && page_ok(kv, pt[s / PAGE])) {
+            const size_t idx = kv_index(pt[s / PAGE], kvh, s % PAGE, kv.kv_heads);
+            float dot = 0.f;
+            if (F32) {
+                const float4* kr = (const float4*)((const float*)kv.k + idx);
+#pragma unroll 8
+                for (int i = 0; i < 32; ++i) {
+                    const float4 k4 = kr[i];
+                    dot = fmaf(qs[4 * i], k4.x, dot);
+                    dot = fmaf(qs[4 * i + 1], k4.y, dot);
+                    dot = fmaf(qs[4 * i + 2], k4.z, dot);
+                    dot = fmaf(qs[4 * i + 3], k4.w, dot);
+                }
+            } else {
+                const uint4* kr = (const uint4*)((const uint16_t*)kv.k + idx);
+#pragma unroll 4
+                for (int i = 0; i < 16; ++i) {
+                    const uint4 k8 = kr[i];
+                    const uint32_t w[4] = {k8.x, k8.y, k8.z, k8.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        dot = fmaf(qs[8 * i + 2 * e], __uint_as_float(w[e] << 16), dot);
+                        dot = fmaf(qs[8 * i + 2 * e + 1], __uint_as_float(w[e] & 0xffff0000u), dot);
+                    }
+                }
+            }
+            sc = __fdiv_rn(dot, scale);
+        }
+        const float cmax = block_max(sc, red);
+        const float nm = fmaxf(m, cmax);
+        const float corr = expf(m - nm);
+        const float e = s < visible ? expf(sc - nm) : 0.f;
+        pr[t] = e;
+        const float esum = block_sum(e, red);  // also orders pr[] writes before reads
+        l = fmaf(l, corr, esum);
+        acc *= corr;
+        const int n = min(128, visible - s0);
+        for (int j = 0; j < n; ++j) {
+            const int sp = s0 + j;
+            const int page = pt[sp / PAGE];
+            if ((unsigned)page >= (unsigned)kv.pages) continue;  // flagged in the score loop
+            const size_t idx = kv_index(page, kvh, sp % PAGE, kv.kv_heads) + t;
+            acc = fmaf(pr[j], kv_load<F32>(kv.v, idx), acc);
+        }
+        m = nm;
+        __syncthreads();
+    }
+    out[(size_t)row * (q_heads * HEAD) + h * HEAD + t] = __fdiv_rn(acc, l);
+}
+
+// First maximum of each predicted row, ties to the lower index
+// (model.rs:288-296, gpu.metal:176-212).
+__global__ void __launch_bounds__(1024) k_argmax(PassBuf pb, const float* __restrict__ logits,
+                                                 int vocab) {
+    __shared__ float bv[32];
+    __shared__ uint32_t bi[32];
+    const int r = blockIdx.x;
+    if (r >= pb.hdr->head_rows) return;
+    const float* x = logits + (size_t)r * vocab;
+    float best = -INFINITY;
+    uint32_t idx = 0xffffffffu;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+        const float v = x[i];
+        if (v > best) { best = v; idx = i; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_down_sync(0xffffffffu, best, o);
+        const uint32_t oi = __shfl_down_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) { bv[warp] = best; bi[warp] = idx; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) { best = bv[w]; idx = bi[w]; }
+        pb.out_ids[r] = idx == 0xffffffffu ? 0u : idx;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Seeded synthetic weights: Philox4x32-10 (Salmon et al., SC'11) keyed by the
+// model seed, counter (group, tensor index); Box-Muller in double precision;
+// 0.02 * z rounded to f32, then to bf16.
+
+__device__ __forceinline__ void philox10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        if (r) { k0 += 0x9E3779B9u; k1 += 0xBB67AE85u; }
+        const uint32_t hi0 = __umulhi(0xD2511F53u, c[0]), lo0 = 0xD2511F53u * c[0];
+        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c[2]), lo1 = 0xCD9E8D57u * c[2];
+        const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+        c[0] = n0; c[1] = lo1; c[2] = n2; c[3] = lo0;
+    }
+}
+
+__global__ void k_synth(uint64_t seed, uint32_t tensor, size_t n, uint16_t* __restrict__ out) {
+    const double two_pi = 6.283185307179586476925286766559;
+    const double inv32 = 1.0 / 4294967296.0;
+    const uint32_t k0 = (uint32_t)seed ^ (uint32_t)(seed >> 32);
+    const size_t groups = (n + 3) / 4;
+    for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < groups;
+         g += (size_t)gridDim.x * blockDim.x) {
+        uint32_t c[4] = {(uint32_t)g, (uint32_t)(g >> 32), tensor, 0x6a616c61u};
+        philox10(c, k0, 0x70656e6fu);
+        const double u0 = ((double)c[0] + 0.5) * inv32, u1 = ((double)c[1] + 0.5) * inv32;
+        const double u2 = ((double)c[2] + 0.5) * inv32, u3 = ((double)c[3] + 0.5) * inv32;
+        const double a = sqrt(-2.0 * log(u0)), b = sqrt(-2.0 * log(u2));
+        const double z[4] = {a * cos(two_pi * u1), a * sin(two_pi * u1), b * cos(two_pi * u3),
+                             b * sin(two_pi * u3)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const size_t e = g * 4 + j;
+            if (e < n) out[e] = f2bf16((float)(0.02 * z[j]));
+        }
+    }
+}
+
+__global__ void k_fill_u16(uint16_t* out, size_t n, uint16_t v) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = v;
+}
+
+// MXFP4 quantization of bf16 weights, one 32-block per thread.  Same steps as
+// python/quantize_mxfp4.py:26-38: exponent = frexp(max|v|) - 3 clipped to
+// [-127, 127] (-127 for an all-zero block), codes by nearest level with ties
+// to the even code, sign in bit 3, even element in the low nibble.
+__global__ void k_quantize(const uint16_t* __restrict__ in, size_t blocks, uint8_t* __restrict__ packed,
+                           uint8_t* __restrict__ scales) {
+    const float mid[7] = {0.25f, 0.75f, 1.25f, 1.75f, 2.5f, 3.5f, 5.0f};
+    for (size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x; b < blocks;
+         b += (size_t)gridDim.x * blockDim.x) {
+        const uint16_t* v = in + b * 32;
+        float mx = 0.f;
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(bf16f(v[i])));
+        int e;
+        frexpf(mx, &e);
+        int ex = e - 3;
+        ex = ex < -127 ? -127 : (ex > 127 ? 127 : ex);
+        if (mx == 0.f) ex = -127;
+        uint8_t* p = packed + b * 16;
+        for (int j = 0; j < 16; ++j) {
+            uint32_t codes[2];
+            for (int h = 0; h < 2; ++h) {
+                const float f = bf16f(v[2 * j + h]);
+                const float sc = ldexpf(fabsf(f), -ex);
+                uint32_t c = 0;
+                while (c < 7 && mid[c] < sc) ++c;
+                if ((c & 1u) && sc == mid[c < 6 ? c : 6]) c += 1;
+                if (signbit(f)) c |= 8u;
+                codes[h] = c;
+            }
+            p[j] = (uint8_t)(codes[0] | (codes[1] << 4));
+        }
+        scales[b] = (uint8_t)(ex + 127);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// launch helpers
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+Proj make_proj(std::initializer_list<const Mat*> mats) {
+    Proj p{};
+    int i = 0;
+    for (const Mat* m : mats) {
+        p.w[i] = m->data;
+        p.s[i] = m->scales;
+        p.n[i] = m->rows;
+        p.K = m->cols;
+        p.total += m->rows;
+        ++i;
+    }
+    for (; i < 3; ++i) { p.w[i] = nullptr; p.s[i] = nullptr; p.n[i] = 0; }
+    return p;
+}
+
+template <int KIND, int EPI, int R, int MR>
+jl_status run_skinny(const PassCtx& c, int use_head, const float* x, int ldx, const Proj& p,
+                     float* y, int ldy) {
+    auto kern = k_skinny<KIND, EPI, R, MR>;
+    const size_t smem = (size_t)MR * p.K * sizeof(float);
+    const int groups = (p.total + R - 1) / R;
+    const int per_sm = smem <= 48 * 1024 ? 4 : (smem <= 100 * 1024 ? 2 : 1);
+    int grid = std::min((groups + 7) / 8, sm_count() * per_sm);
+    grid = std::max(grid, 1);
+    kern<<<grid, 256, smem, c.stream>>>(c.m->pass.hdr, use_head, c.m->max_rows, x, ldx, p, y, ldy);
+    JL_CUDA(cudaGetLastError());
+    return JL_OK;
+}
+
+template <int KIND, int EPI>
+jl_status run_proj_kind(const PassCtx& c, int use_head, const float* x, int ldx, const Proj& p,
+                        float* y, int ldy) {
+    const int cap = use_head ? c.head_cap : c.rows_cap;
+    if (cap <= SMALL_M) {
+        if ((size_t)4 * p.K * sizeof(float) <= 100 * 1024)
+            return run_skinny<KIND, EPI, 2, 4>(c, use_head, x, ldx, p, y, ldy);
+        return run_skinny<KIND, EPI, 2, 2>(c, use_head, x, ldx, p, y, ldy);
+    }
+    dim3 grid((p.total + 63) / 64, (cap + 63) / 64);
+    k_gemm<KIND, EPI><<<grid, 256, 0, c.stream>>>(c.m->pass.hdr, use_head, cap, x, ldx, p, y, ldy);
+    JL_CUDA(cudaGetLastError());
+    return JL_OK;
+}
+
+template <int EPI>
+jl_status run_proj(const PassCtx& c, int kind, int use_head, const float* x, int ldx,
+                   const Proj& p, float* y, int ldy) {
+    if (kind == MAT_MXFP4) return run_proj_kind<MAT_MXFP4, EPI>(c, use_head, x, ldx, p, y, ldy);
+    return run_proj_kind<MAT_BF16, EPI>(c, use_head, x, ldx, p, y, ldy);
+}
+
+KvView kv_view(const jl_model* m, int layer) {
+    KvView v;
+    const size_t bytes_layer = m->kv.pages * m->kv.page_elems * m->kv.elem;
+    char* base = (char*)m->kv.base + (size_t)layer * 2 * bytes_layer;
+    v.k = base;
+    v.v = base + bytes_layer;
+    v.kv_heads = m->kv_heads;
+    v.f32 = m->kv.dtype == JL_KV_F32;
+    v.pages = (int)m->kv.pages;
+    v.max_pos = m->max_positions;
+    v.err = m->counters;
+    return v;
+}
+
+int qkv_ld(const jl_model* m) { return (m->q_heads + 2 * m->kv_heads) * HEAD; }
+
+template <int KIND, int EPI>
+jl_status configure_skinny() {
+    JL_CUDA(cudaFuncSetAttribute(k_skinny<KIND, EPI, 2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024));
+    JL_CUDA(cudaFuncSetAttribute(k_skinny<KIND, EPI, 2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024));
+    return JL_OK;
+}
+
+}  // namespace
+
+jl_status configure_kernels() {
+    int dev = 0;
+    JL_CUDA(cudaGetDevice(&dev));
+    static bool done[64] = {};
+    if (dev < 64 && done[dev]) return JL_OK;
+    sm_count();
+    JL_TRY((configure_skinny<MAT_BF16, EPI_STORE>()));
+    JL_TRY((configure_skinny<MAT_BF16, EPI_ADD>()));
+    JL_TRY((configure_skinny<MAT_BF16, EPI_SWIGLU>()));
+    JL_TRY((configure_skinny<MAT_MXFP4, EPI_STORE>()));
+    JL_TRY((configure_skinny<MAT_MXFP4, EPI_ADD>()));
+    JL_TRY((configure_skinny<MAT_MXFP4, EPI_SWIGLU>()));
+    if (dev < 64) done[dev] = true;
+    return JL_OK;
+}
+
+jl_status launch_embed(const PassCtx& c) {
+    k_embed<<<c.rows_cap, 256, 0, c.stream>>>(c.m->pass, c.m->embed, c.m->s.x, c.m->hidden);
+    JL_CUDA(cudaGetLastError());
+    return JL_OK;
+}
+
+jl_status launch_rmsnorm(const PassCtx& c, const float* x, const uint16_t* w, float* out,
+                         bool head_rows) {
+    const int h = c.m->hidden;
+    k_rmsnorm<<<head_rows ? c.head_cap : c.rows_cap, 256, 0, c.stream>>>(c.m->pass, x, h, w, out, h, h,
+                                                                        head_rows ? 1 : 0);
+    JL_CUDA(cudaGetLastError());
+    return JL_OK;
+}
+
+jl_status launch_qkv(const PassCtx& c, const LayerW& L) {
+    Proj p = make_proj({&L.q, &L.k, &L.v});
+    return run_proj<EPI_STORE>(c, L.q.kind, 0, c.m->s.xn, c.m->hidden, p, c.m->s.qkv, qkv_ld(c.m));
+}
+
+jl_status launch_qk_rope_kv(const PassCtx& c, int layer, const LayerW& L) {
+    k_qk_rope_kv<<<c.rows_cap, 256, 0, c.stream>>>(c.m->pass, c.m->s.qkv, qkv_ld(c.m), c.m->q_heads,
+                                                   L.q_norm, L.k_norm, c.m->rope, kv_view(c.m, layer));
+    JL_CUDA(cudaGetLastError());
+    return JL_OK;
+}
+
+jl_status launch_attention(const PassCtx& c, int layer) {
+    dim3 grid(c.m->q_heads, c.rows_cap);
+    const int group = c.m->q_heads / c.m->kv_heads;
+    if (c.m->kv.dtype == JL_KV_F32)
+        k_attention<1><<<grid, 128, 0, c.stream>>>(c.m->pass, c.m->s.qkv, qkv_ld(c.m), c.m->q_heads,
+                                                   group, kv_view(c.m, layer), c.m->s.attn);
+    else
+        k_attention<0><<<grid, 128, 0, c.stream>>>(c.m->pass, c.m->s.qkv, qkv_ld(c.m), c.m->q_heads,
+                                                   group, kv_view(c.m, layer), c.m->s.attn);
+    JL_CUDA(cudaGetLastError());
+    return JL_OK;
+}
+
+jl_status launch_o(const PassCtx& c, const LayerW& L) {
+    Proj p = make_proj({&L.o});
+    return run_proj<EPI_ADD>(c, L.o.kind, 0, c.m->s.attn, c.m->q_heads * HEAD, p, c.m->s.x, c.m->hidden);
+}
+
+jl_status launch_gateup(const PassCtx& c, const LayerW& L) {
+    Proj p = make_proj({&L.gate, &L.up});
+    p.total = L.gate.rows;
+    return run_proj<EPI_SWIGLU>(c, L.gate.kind, 0, c.m->s.xn, c.m->hidden, p, c.m->s.act, c.m->inter);
+}
+
+jl_status launch_down(const PassCtx& c, const LayerW& L) {
+    Proj p = make_proj({&L.down});
+    return run_proj<EPI_ADD>(c, L.down.kind, 0, c.m->s.act, c.m->inter, p, c.m->s.x, c.m->hidden);
+}
+
+jl_status launch_head(const PassCtx& c) {
+    Proj p = make_proj({&c.m->head});
+    return run_proj<EPI_STORE>(c, c.m->head.kind, 1, c.m->s.xh, c.m->hidden, p, c.m->s.logits,
+                               c.m->vocab);
+}
+
+jl_status launch_argmax(const PassCtx& c) {
+    k_argmax<<<c.head_cap, 1024, 0, c.stream>>>(c.m->pass, c.m->s.logits, c.m->vocab);
+    JL_CUDA(cudaGetLastError());
+    return JL_OK;
+}
+
+jl_status launch_synth_bf16(uint64_t seed, uint32_t tensor_index, size_t n, uint16_t* out,
+                            cudaStream_t stream) {
+    const size_t groups = (n + 3) / 4;
+    const int grid = (int)std::min<size_t>((groups + 255) / 256, (size_t)sm_count() * 16);
+    k_synth<<<std::max(grid, 1), 256, 0, stream>>>(seed, tensor_index, n, out);
+    JL_CUDA(cudaGetLastError());
+    return JL_OK;
+}
+
+jl_status launch_fill_u16(uint16_t* out, size_t n, uint16_t value, cudaStream_t stream) {
+    const int grid = (int)std::min<size_t>((n + 255) / 256, (size_t)sm_count() * 8);
+    k_fill_u16<<<std::max(grid, 1), 256, 0, stream>>>(out, n, value);
+    JL_CUDA(cudaGetLastError());
+    return JL_OK;
+}
+
+jl_status launch_quantize_mxfp4(const uint16_t* bf16, int rows, int cols, uint8_t* packed,
+                                uint8_t* scales, cudaStream_t stream) {
+    const size_t blocks = (size_t)rows * cols / 32;
+    const int grid = (int)std::min<size_t>((blocks + 127) / 128, (size_t)sm_count() * 16);
+    k_quantize<<<std::max(grid, 1), 128, 0, stream>>>(bf16, blocks, packed, scales);
+    JL_CUDA(cudaGetLastError());
+    return JL_OK;
+}
+
+}  // namespace jl

@@ -1,0 +1,79 @@
+// Device helpers shared by the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace jl {
+
+__device__ __forceinline__ float bf16f(uint32_t bits) { return __uint_as_float(bits << 16); }
+
+// Round-to-nearest-even f32 -> bf16 bits (NaN kept quiet).
+__device__ __forceinline__ uint16_t f2bf16(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+// E8M0 scale byte -> 2^(s-127) exactly (s == 0 is the subnormal 2^-127;
+// 255 is rejected at load time).
+__device__ __forceinline__ float e8m0(uint32_t s) {
+    return s ? __uint_as_float(s << 23) : __uint_as_float(0x00400000u);
+}
+
+// One E2M1 code (low 4 bits of c) as f32: level {0,.5,1,1.5,2,3,4,6}, sign
+// in bit 3.  The magnitude bits placed at [22,25) read as level * 2^-126
+// (c == 1 lands on the subnormal 2^-127); the exact product by 2^126 restores
+// the level.
+__device__ __forceinline__ float e2m1(uint32_t c) {
+    float mag = __fmul_rn(__uint_as_float((c & 7u) << 22), 0x1p126f);
+    return __uint_as_float(__float_as_uint(mag) | ((c & 8u) << 28));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide sum for blockDim.x a multiple of 32 (<= 1024); `red` holds 32
+// floats.  Every thread gets the total.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; ++i) t += red[i];
+    return t;
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = -INFINITY;
+    for (int i = 0; i < nw; ++i) t = fmaxf(t, red[i]);
+    return t;
+}
+
+// Streaming 16-byte load of weights: read once per pass, so keep them out of L1.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+}  // namespace jl

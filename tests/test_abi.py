@@ -1,0 +1,57 @@
+"""The C-ABI library loads and exports every symbol include/jalapeno.h
+declares; host-side argument checks work without a GPU."""
+import ctypes
+import re
+
+import pytest
+
+from conftest import REPO, has_gpu
+
+import jalapeno as J
+
+
+def declared_symbols():
+    text = (REPO / "include" / "jalapeno.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(jl_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_symbols()
+    assert len(names) >= 25
+    assert sorted(J.EXPORTS) == names
+    lib = ctypes.CDLL(str(J.LIB_PATH))
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_version_and_errors():
+    assert b"sm_100a" in J.lib.jl_version()
+    with pytest.raises(J.JlError) as e:
+        J.DraftSchedule.fixed(0)
+    assert e.value.status == J.JL_ERR_INVALID_ARG
+    assert "gamma" in e.value.message
+
+
+def test_schedules_validate_like_the_reference():
+    # scheduler.rs:9-27
+    assert J.DraftSchedule.fixed(5).gamma == 5
+    assert J.DraftSchedule.adaptive(4, 5).gamma == 4
+    with pytest.raises(J.JlError):
+        J.DraftSchedule.adaptive(0, 8)
+    with pytest.raises(J.JlError):
+        J.DraftSchedule.adaptive(9, 8)
+
+
+@pytest.mark.skipif(has_gpu(), reason="checks the no-GPU error path")
+def test_no_cpu_fallback_without_a_device():
+    assert J.device_count() == 0
+    with pytest.raises(J.JlError) as e:
+        J.Model.synthesize(1, 256, 2, 1, 512, 1000, True, 0)
+    assert e.value.status == J.JL_ERR_NO_DEVICE
+
+
+def test_null_arguments_are_rejected():
+    assert J.lib.jl_weights_load(None, None) == J.JL_ERR_INVALID_ARG
+    assert J.lib.jl_model_synthesize(None, None, None) == J.JL_ERR_INVALID_ARG
+    assert J.lib.jl_cache_truncate(None, 0) == J.JL_ERR_INVALID_ARG

@@ -1,0 +1,57 @@
+"""Full-size BASELINE.json architectures on the GPU.
+
+The CPU oracle checks the first decoder layer of every architecture (its
+tensors are the same whatever the layer count) and the whole 0.6B model;
+the 8B model is checked through size-independent properties: speculative
+output equals greedy output, oracle-draft p=0 accepts every proposal,
+logits are finite.
+"""
+import numpy as np
+import pytest
+
+import jalapeno as J
+import oracle as O
+from gpu_util import HIDDEN_REL_L2, first_layers, logits_close, rel_l2
+
+pytestmark = [pytest.mark.gpu, pytest.mark.slow]
+
+PROMPT = O.prompt_ids(32, 151936, 2)
+
+
+@pytest.mark.parametrize("preset,mxfp4", [("qwen3-0.6b", True), ("qwen3-1.7b", False),
+                                          ("qwen3-1.7b", True), ("qwen3-8b", True)])
+def test_first_layer_matches_oracle(preset, mxfp4):
+    cfg = O.PRESETS[preset]
+    one = first_layers(cfg, 1)
+    seed = 1 if preset == "qwen3-0.6b" else 0
+    ref = O.Model.synthetic(one, seed, mxfp4=mxfp4)
+    m = J.Model.from_config(one, seed, mxfp4=mxfp4, kv_dtype=J.KV_F32, kv_pool_tokens=1024,
+                            max_pass_rows=64)
+    got = m.hidden(PROMPT[:8], 1)
+    assert rel_l2(got, ref.hidden(PROMPT[:8], 1)) < HIDDEN_REL_L2
+
+
+def test_qwen3_0_6b_mxfp4_logits_match_oracle():
+    cfg = O.PRESETS["qwen3-0.6b"]
+    ref = O.Model.synthetic(cfg, 1, mxfp4=True)
+    m = J.Model.from_config(cfg, 1, mxfp4=True, kv_dtype=J.KV_F32, kv_pool_tokens=1024,
+                            max_pass_rows=64)
+    prompt = PROMPT[:8]
+    ids, lg = m.predict(prompt, m.cache(), logits=True)
+    rids, rlg = ref.predict(prompt, ref.cache(), logits=True)
+    assert logits_close(lg, rlg)
+    assert rel_l2(lg, rlg) < 1e-4
+    assert ids == rids
+
+
+def test_qwen3_8b_speculative_properties():
+    target = J.Model.from_config(O.PRESETS["qwen3-8b"], 0, mxfp4=True, kv_pool_tokens=4096)
+    draft = J.Model.from_config(O.PRESETS["qwen3-0.6b"], 1, mxfp4=True, kv_pool_tokens=4096)
+    greedy = target.generate(PROMPT, 24)
+    assert len(greedy) == len(PROMPT) + 24
+    r = J.generate_speculative(target, draft, PROMPT, 24, 4)
+    assert r.tokens == greedy
+    r = J.generate_speculative(target, draft, PROMPT, 24, 4, oracle_stream=greedy)
+    assert r.tokens == greedy and r.accepted == r.drafted
+    _, lg = target.predict(PROMPT[:4], target.cache(), logits=True)
+    assert np.isfinite(lg).all()
