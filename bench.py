@@ -57,7 +57,25 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--profile", action="store_true",
+                    help="small run for ncu: one k+1-row target pass and one draft pass "
+                         "(Model::time_pass), no timing loop")
     return ap.parse_args()
+
+
+def run_profile(args, dist):
+    """The kernels of one speculative round, for a profiler's launch list: a
+    k+1-row verify pass of the target and a one-row draft pass, each through
+    the captured pass graph the decode loop replays."""
+    import jalapeno as J
+    import oracle as O
+
+    target, draft = make_models(J, dist.local)
+    prompt = O.prompt_ids(args.prompt, 151936, 2)
+    tw, tg = target.time_pass(prompt, args.gamma + 1, reps=1)
+    dw, dg = draft.time_pass(prompt, 1, reps=1)
+    print(json.dumps({"profile": True, "target_pass_ms": tg, "draft_pass_ms": dg,
+                      "target_rows": args.gamma + 1}), flush=True)
 
 
 def measured_peaks():
@@ -263,6 +281,10 @@ def main():
     dist = Dist()
     if args.impl == "reference":
         run_reference(args, dist)
+        dist.close()
+        return
+    if args.profile:
+        run_profile(args, dist)
         dist.close()
         return
     import jalapeno as J

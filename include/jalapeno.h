@@ -219,6 +219,21 @@ typedef struct jl_spec_result {
     double draft_ms, verify_ms; /* per phase (JL_SPEC_HOST only; 0 otherwise) */
 } jl_spec_result;
 
+/* The projections of one layer as the forward pass runs them: the
+ * reference's public matmul (engine/src/lib.rs:240-266, y = x . W^T) applied
+ * to `rows` f32 input rows, in the fused forms this engine uses.
+ *   JL_PROJ_QKV     y = [x.Wq^T | x.Wk^T | x.Wv^T]   (q_width + 2*kv_width)
+ *   JL_PROJ_O       y = x . Wo^T                      (hidden)
+ *   JL_PROJ_GATE_UP y = silu(x.Wgate^T) * (x.Wup^T)   (intermediate, lib.rs:459-463)
+ *   JL_PROJ_DOWN    y = x . Wdown^T                   (hidden)
+ *   JL_PROJ_HEAD    y = x . Whead^T                   (vocab; layer ignored)
+ * Inputs are NOT normalised first.  rows must be at most 16. */
+typedef enum jl_projection {
+    JL_PROJ_QKV = 0, JL_PROJ_O = 1, JL_PROJ_GATE_UP = 2, JL_PROJ_DOWN = 3, JL_PROJ_HEAD = 4
+} jl_projection;
+jl_status jl_project(jl_model* m, int layer, jl_projection which, const float* x, size_t rows,
+                     float* y);
+
 /* ------------------------------------------------------------------------
  * Profiling.
  * ---------------------------------------------------------------------- */
@@ -230,9 +245,6 @@ typedef struct jl_spec_result {
 jl_status jl_time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t rows, size_t reps,
                        double* wall_ms, double* gpu_ms);
 
-typedef enum jl_projection {
-    JL_PROJ_QKV = 0, JL_PROJ_O = 1, JL_PROJ_GATE_UP = 2, JL_PROJ_DOWN = 3, JL_PROJ_HEAD = 4
-} jl_projection;
 /* Launches one projection kernel of `layer` for `rows` input rows `iters`
  * times back to back on the model's stream and returns the mean device time
  * per launch (CUDA events) and the weight bytes each launch reads.  No

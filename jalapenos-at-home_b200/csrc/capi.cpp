@@ -285,6 +285,12 @@ jl_status jl_time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t row
     JL_GUARD({ return time_pass(m, prompt, n, rows, reps, wall_ms, gpu_ms); })
 }
 
+jl_status jl_project(jl_model* m, int layer, jl_projection which, const float* x, size_t rows,
+                     float* y) {
+    JL_NEED(m && x && y, "model, x and y must be non-null");
+    JL_GUARD({ return project(m, layer, (int)which, x, rows, y); })
+}
+
 jl_status jl_time_projection(jl_model* m, int layer, jl_projection which, int rows, int iters,
                              double* ms_per_launch, size_t* weight_bytes) {
     JL_NEED(m && ms_per_launch && weight_bytes, "model and outputs must be non-null");

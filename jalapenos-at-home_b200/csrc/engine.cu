@@ -293,17 +293,21 @@ jl_status host_pass(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int
                             cudaMemcpyHostToDevice, st));
     const bool full = layers == m->layers && head_rows > 0;
     if (full && n <= (size_t)SMALL_M) {
-        if (!m->small_graph) {
+        // one captured pass per row bucket 1, 2, 4, 8, 16
+        int b = 0;
+        while ((1 << b) < (int)n) ++b;
+        cudaGraphExec_t& exec = m->small_graph[b];
+        if (!exec) {
             cudaGraph_t g;
             JL_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-            jl_status rs = record_pass(m, st, SMALL_M, m->layers, true);
+            jl_status rs = record_pass(m, st, 1 << b, m->layers, true);
             cudaError_t ce = cudaStreamEndCapture(st, &g);
             if (rs != JL_OK) return rs;
             JL_CUDA(ce);
-            JL_CUDA(cudaGraphInstantiate(&m->small_graph, g, 0));
+            JL_CUDA(cudaGraphInstantiate(&exec, g, 0));
             cudaGraphDestroy(g);
         }
-        JL_CUDA(cudaGraphLaunch(m->small_graph, st));
+        JL_CUDA(cudaGraphLaunch(exec, st));
         return JL_OK;
     }
     PassCtx ctx{m, st, (int)n, std::max(head_rows, 1)};
@@ -348,7 +352,11 @@ jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool 
     JL_TRY(check_ids(m, ids, n));
     JL_CUDA(cudaSetDevice(m->device));
     JL_TRY(cache_reserve(c, c->len + n, m->stream));
-    const size_t chunk = all ? std::min<size_t>(m->max_rows, HEAD_CAP) : (size_t)m->max_rows;
+    // Up to 256 tokens go through the captured decode pass 16 rows at a time
+    // (the kernels are row-count invariant, so chunking changes no result);
+    // longer prompts use the tiled long-prompt kernels.
+    const size_t chunk = n <= 256 ? (size_t)SMALL_M
+                                  : (all ? std::min<size_t>(m->max_rows, HEAD_CAP) : (size_t)m->max_rows);
     size_t done = 0;
     while (done < n) {
         const size_t take = std::min(chunk, n - done);
@@ -408,6 +416,46 @@ jl_status time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t rows, 
     return JL_OK;
 }
 
+jl_status project(jl_model* m, int layer, int which, const float* x, size_t rows, float* y) {
+    if (rows < 1 || rows > (size_t)SMALL_M || which < 0 || which > 4 ||
+        (which != 4 && (layer < 0 || layer >= m->layers))) {
+        set_error("project: rows must be 1..%d and layer/projection valid", SMALL_M);
+        return JL_ERR_INVALID_ARG;
+    }
+    JL_CUDA(cudaSetDevice(m->device));
+    cudaStream_t st = m->stream;
+    const int QW = m->q_heads * HEAD, KVW = m->kv_heads * HEAD;
+    const LayerW* L = which == 4 ? nullptr : &m->lw[layer];
+    // (input buffer, width in, output buffer, width out)
+    float* in = nullptr;
+    float* out = nullptr;
+    int win = m->hidden, wout = m->hidden;
+    switch (which) {
+        case 0: in = m->s.xn; out = m->s.qkv; wout = QW + 2 * KVW; break;
+        case 1: in = m->s.attn; win = QW; out = m->s.x; break;
+        case 2: in = m->s.xn; out = m->s.act; wout = m->inter; break;
+        case 3: in = m->s.act; win = m->inter; out = m->s.x; break;
+        default: in = m->s.xh; out = m->s.logits; wout = m->vocab; break;
+    }
+    PassHdr h{(int32_t)rows, (int32_t)rows, 0, 0};
+    *m->host_hdr = h;
+    JL_CUDA(cudaMemcpyAsync(m->pass.hdr, m->host_hdr, sizeof(PassHdr), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(in, x, rows * win * sizeof(float), cudaMemcpyHostToDevice, st));
+    if (which == 1 || which == 3)  // these add into the residual stream: start it at zero
+        JL_CUDA(cudaMemsetAsync(out, 0, rows * wout * sizeof(float), st));
+    PassCtx c{m, st, (int)rows, (int)rows};
+    switch (which) {
+        case 0: JL_TRY(launch_qkv(c, *L)); break;
+        case 1: JL_TRY(launch_o(c, *L)); break;
+        case 2: JL_TRY(launch_gateup(c, *L)); break;
+        case 3: JL_TRY(launch_down(c, *L)); break;
+        default: JL_TRY(launch_head(c)); break;
+    }
+    JL_CUDA(cudaMemcpyAsync(y, out, rows * wout * sizeof(float), cudaMemcpyDeviceToHost, st));
+    JL_CUDA(cudaStreamSynchronize(st));
+    return check_device_flag(m);
+}
+
 jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters, double* ms,
                           size_t* bytes) {
     if (layer < 0 || layer >= m->layers || which < 0 || which > 4 || rows < 1 ||
@@ -420,8 +468,7 @@ jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters
     PassHdr h{rows, which == 4 ? rows : 0, 0, 0};
     *m->host_hdr = h;
     JL_CUDA(cudaMemcpyAsync(m->pass.hdr, m->host_hdr, sizeof(PassHdr), cudaMemcpyHostToDevice, m->stream));
-    const int cap = rows <= SMALL_M ? SMALL_M : rows;
-    PassCtx c{m, m->stream, cap, cap};
+    PassCtx c{m, m->stream, rows, rows};
     auto launch = [&]() -> jl_status {
         switch (which) {
             case 0: return launch_qkv(c, L);

@@ -31,7 +31,7 @@ namespace jl {
 constexpr int HEAD = 128;        // head_dim of every Qwen3 model (engine/src/lib.rs:24)
 constexpr int HALF = 64;         // RoPE rotates (i, i + 64) pairs (engine/src/lib.rs:297)
 constexpr int PAGE = 64;         // tokens per KV page
-constexpr int SMALL_M = 32;      // passes up to this many rows use the skinny kernels
+constexpr int SMALL_M = 16;      // passes up to this many rows use the decode kernels (tensor-core MXFP4)
 constexpr int MAX_SEQS = 64;     // sequences one pass may touch
 constexpr int MAX_GAMMA = 16;    // largest draft length of the device-resident loop
 
@@ -99,7 +99,27 @@ struct Mat {
     }
 };
 
+// An MXFP4 projection re-laid out for the tensor-core kernel (mx_mma.cu):
+// T tiles of 128 weight rows (gate/up: 64 gate + 64 up rows), S stages of 256
+// K-elements, K split into `ksplit` slices across CTAs.
+struct MxProj {
+    const uint8_t* a = nullptr;     // [T][S] swizzled 16 KB weight images
+    const uint8_t* sfa = nullptr;   // [T][S] 1 KB scale atoms
+    int T = 0, S = 0, K = 0, ksplit = 1, out_rows = 0;
+    bool swiglu = false;
+};
+
+struct MxBuffers {
+    uint8_t* bimg = nullptr;   // activation pieces, [S][N*128]
+    uint8_t* sfb = nullptr;    // their scale atoms, [S][1024]
+    float* ws = nullptr;       // split-K partials
+    int* tickets = nullptr;    // split-K arrival counters (kept at zero between launches)
+    void* arena = nullptr;     // tiled weights
+    void* scratch = nullptr;   // bimg, sfb, ws, tickets
+};
+
 struct LayerW {
+    MxProj mx_qkv, mx_o, mx_gateup, mx_down;
     Mat q, k, v, o, gate, up, down;
     const uint16_t* in_ln = nullptr;
     const uint16_t* post_ln = nullptr;
@@ -155,10 +175,13 @@ struct SpecGraph;  // device-resident speculative loop (engine.cu)
 
 struct jl_model {
     int device = 0;
+    int sms = 148;                        // streaming multiprocessors of the device
     int layers = 0, hidden = 0, q_heads = 0, kv_heads = 0, inter = 0, vocab = 0;
     int max_positions = 0, eos = 0;
     bool tied = false;
     jl::Mat embed, head;
+    jl::MxProj mx_head;                   // tensor-core copy of an MXFP4 output table
+    jl::MxBuffers mx;
     const uint16_t* final_norm = nullptr;
     std::vector<jl::LayerW> lw;
     void* arena = nullptr;
@@ -177,7 +200,7 @@ struct jl_model {
     void* scratch_arena = nullptr;
     cudaStream_t stream = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-    cudaGraphExec_t small_graph = nullptr;  // full pass, rows <= SMALL_M
+    cudaGraphExec_t small_graph[5] = {};  // full pass for rows <= 1, 2, 4, 8, 16
     std::vector<jl::SpecGraph*> spec_graphs;  // owned; freed by model_free
     int* counters = nullptr;              // zeroed split-K / reduction counters
     std::map<std::string, std::pair<const void*, size_t>> tensor_index;  // name -> device bytes
@@ -219,6 +242,7 @@ jl_status time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t rows, 
                     double* wall_ms, double* gpu_ms);
 jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters, double* ms,
                           size_t* bytes);
+jl_status project(jl_model* m, int layer, int which, const float* x, size_t rows, float* y);
 jl_status generate(jl_model* m, const uint32_t* prompt, size_t n, size_t count, uint32_t* out,
                    size_t cap, size_t* out_len);
 jl_status generate_speculative(jl_model* target, jl_model* draft, const uint32_t* prompt,
@@ -247,6 +271,18 @@ jl_status launch_argmax(const PassCtx& c);
 
 jl_status launch_synth_bf16(uint64_t seed, uint32_t tensor_index, size_t n, uint16_t* out,
                             cudaStream_t stream);
+
+// ---- tensor-core MXFP4 projections (mx_mma.cu) ---------------------------------
+enum MxEpi : int { MXE_STORE = 0, MXE_ADD = 1, MXE_SWIGLU = 2 };
+jl_status mx_configure();
+int mx_max_tokens();
+size_t mx_tile_bytes(int out_rows, int K, bool swiglu);
+jl_status mx_build(const Mat* const* mats, int nmats, bool swiglu, uint8_t* dst, int sms,
+                   MxProj* out, cudaStream_t stream);
+jl_status mx_project(const PassCtx& c, const MxProj& p, int epi, int use_head, const float* x,
+                     int ldx, const uint16_t* norm, float* y, int ldy);
+// Builds the tensor-core copies of every MXFP4 projection of `m` (model.cu).
+jl_status build_mx(jl_model* m);
 jl_status launch_fill_u16(uint16_t* out, size_t n, uint16_t value, cudaStream_t stream);
 jl_status launch_quantize_mxfp4(const uint16_t* bf16, int rows, int cols, uint8_t* packed,
                                 uint8_t* scales, cudaStream_t stream);

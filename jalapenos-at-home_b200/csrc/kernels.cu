@@ -11,6 +11,8 @@
 
 #include "jl_internal.h"
 #include "kernels.cuh"
+#include "launch.cuh"
+#include "ptx.cuh"
 
 namespace jl {
 
@@ -55,6 +57,8 @@ __global__ void __launch_bounds__(256) k_skinny(const PassHdr* __restrict__ hdr,
                                                 int max_m, const float* __restrict__ x, int ldx, Proj p,
                                                 float* __restrict__ y, int ldy) {
     extern __shared__ float4 xs4[];
+    ptx::grid_dependency_wait();  // PDL: the previous kernel's writes are visible past here
+    ptx::launch_dependents();
     const int M = min(use_head ? hdr->head_rows : hdr->rows, max_m);  // never past the buffers
     const int K = p.K, K4 = K >> 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -232,6 +236,8 @@ __global__ void __launch_bounds__(256) k_gemm(const PassHdr* __restrict__ hdr, i
                                               int max_m, const float* __restrict__ x, int ldx, Proj p,
                                               float* __restrict__ y, int ldy) {
     constexpr int BM = 64, BN = 64, BK = 32;
+    ptx::grid_dependency_wait();  // PDL: the previous kernel's writes are visible past here
+    ptx::launch_dependents();
     constexpr int NV = EPI == EPI_SWIGLU ? 2 : 1;
     __shared__ float xs[BK][BM + 4];
     __shared__ float ws[NV][BK][BN + 4];
@@ -335,6 +341,8 @@ __global__ void __launch_bounds__(256) k_gemm(const PassHdr* __restrict__ hdr, i
 
 __global__ void k_embed(PassBuf pb, Mat e, float* __restrict__ x, int hidden) {
     // lib.rs:213-235, model.rs:167-170
+    ptx::grid_dependency_wait();  // PDL: the previous kernel's writes are visible past here
+    ptx::launch_dependents();
     const int row = blockIdx.x;
     if (row >= pb.hdr->rows) return;
     uint32_t tok = pb.row[row].token;
@@ -357,6 +365,8 @@ __global__ void k_rmsnorm(PassBuf pb, const float* __restrict__ x, int ldx,
                           int width, int head_rows) {
     // lib.rs:268-290: x / sqrt(mean(x^2) + 1e-6) * w
     __shared__ float red[32];
+    ptx::grid_dependency_wait();  // PDL: the previous kernel's writes are visible past here
+    ptx::launch_dependents();
     const int i = blockIdx.x;
     const int n = head_rows ? pb.hdr->head_rows : pb.hdr->rows;
     if (i >= n) return;
@@ -398,6 +408,8 @@ __global__ void __launch_bounds__(256) k_qk_rope_kv(PassBuf pb, float* __restric
                                                     int q_heads, const uint16_t* __restrict__ qn,
                                                     const uint16_t* __restrict__ kn,
                                                     const float2* __restrict__ rope, KvView kv) {
+    ptx::grid_dependency_wait();  // PDL: the previous kernel's writes are visible past here
+    ptx::launch_dependents();
     const int row = blockIdx.x;
     if (row >= pb.hdr->rows) return;
     const RowDesc rd = pb.row[row];
@@ -467,6 +479,8 @@ __global__ void __launch_bounds__(128) k_attention(PassBuf pb, const float* __re
     __shared__ float qs[HEAD];
     __shared__ float pr[128];
     __shared__ float red[32];
+    ptx::grid_dependency_wait();  // PDL: the previous kernel's writes are visible past here
+    ptx::launch_dependents();
     const int h = blockIdx.x, row = blockIdx.y;
     if (row >= pb.hdr->rows) return;
     const RowDesc rd = pb.row[row];
@@ -542,6 +556,8 @@ __global__ void __launch_bounds__(1024) k_argmax(PassBuf pb, const float* __rest
                                                  int vocab) {
     __shared__ float bv[32];
     __shared__ uint32_t bi[32];
+    ptx::grid_dependency_wait();  // PDL: the previous kernel's writes are visible past here
+    ptx::launch_dependents();
     const int r = blockIdx.x;
     if (r >= pb.hdr->head_rows) return;
     const float* x = logits + (size_t)r * vocab;
@@ -682,9 +698,8 @@ jl_status run_skinny(const PassCtx& c, int use_head, const float* x, int ldx, co
     const int per_sm = smem <= 48 * 1024 ? 4 : (smem <= 100 * 1024 ? 2 : 1);
     int grid = std::min((groups + 7) / 8, sm_count() * per_sm);
     grid = std::max(grid, 1);
-    kern<<<grid, 256, smem, c.stream>>>(c.m->pass.hdr, use_head, c.m->max_rows, x, ldx, p, y, ldy);
-    JL_CUDA(cudaGetLastError());
-    return JL_OK;
+    return launch_pdl(kern, dim3(grid), dim3(256), smem, c.stream, (const PassHdr*)c.m->pass.hdr, use_head,
+                      c.m->max_rows, x, ldx, p, y, ldy);
 }
 
 template <int KIND, int EPI>
@@ -697,9 +712,8 @@ jl_status run_proj_kind(const PassCtx& c, int use_head, const float* x, int ldx,
         return run_skinny<KIND, EPI, 2, 2>(c, use_head, x, ldx, p, y, ldy);
     }
     dim3 grid((p.total + 63) / 64, (cap + 63) / 64);
-    k_gemm<KIND, EPI><<<grid, 256, 0, c.stream>>>(c.m->pass.hdr, use_head, cap, x, ldx, p, y, ldy);
-    JL_CUDA(cudaGetLastError());
-    return JL_OK;
+    return launch_pdl(k_gemm<KIND, EPI>, grid, dim3(256), 0, c.stream, (const PassHdr*)c.m->pass.hdr,
+                      use_head, cap, x, ldx, p, y, ldy);
 }
 
 template <int EPI>
@@ -748,76 +762,84 @@ jl_status configure_kernels() {
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_STORE>()));
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_ADD>()));
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_SWIGLU>()));
+    JL_TRY(mx_configure());
     if (dev < 64) done[dev] = true;
     return JL_OK;
 }
 
 jl_status launch_embed(const PassCtx& c) {
-    k_embed<<<c.rows_cap, 256, 0, c.stream>>>(c.m->pass, c.m->embed, c.m->s.x, c.m->hidden);
-    JL_CUDA(cudaGetLastError());
-    return JL_OK;
+    return launch_pdl(k_embed, dim3(c.rows_cap), dim3(256), 0, c.stream, c.m->pass, c.m->embed, c.m->s.x,
+                      c.m->hidden);
 }
 
 jl_status launch_rmsnorm(const PassCtx& c, const float* x, const uint16_t* w, float* out,
                          bool head_rows) {
     const int h = c.m->hidden;
-    k_rmsnorm<<<head_rows ? c.head_cap : c.rows_cap, 256, 0, c.stream>>>(c.m->pass, x, h, w, out, h, h,
-                                                                        head_rows ? 1 : 0);
-    JL_CUDA(cudaGetLastError());
-    return JL_OK;
+    return launch_pdl(k_rmsnorm, dim3(head_rows ? c.head_cap : c.rows_cap), dim3(256), 0, c.stream,
+                      c.m->pass, x, h, w, out, h, h, head_rows ? 1 : 0);
 }
 
 jl_status launch_qkv(const PassCtx& c, const LayerW& L) {
+    if (L.mx_qkv.a && c.rows_cap <= mx_max_tokens())
+        return mx_project(c, L.mx_qkv, MXE_STORE, 0, c.m->s.xn, c.m->hidden, nullptr, c.m->s.qkv,
+                          qkv_ld(c.m));
     Proj p = make_proj({&L.q, &L.k, &L.v});
     return run_proj<EPI_STORE>(c, L.q.kind, 0, c.m->s.xn, c.m->hidden, p, c.m->s.qkv, qkv_ld(c.m));
 }
 
 jl_status launch_qk_rope_kv(const PassCtx& c, int layer, const LayerW& L) {
-    k_qk_rope_kv<<<c.rows_cap, 256, 0, c.stream>>>(c.m->pass, c.m->s.qkv, qkv_ld(c.m), c.m->q_heads,
-                                                   L.q_norm, L.k_norm, c.m->rope, kv_view(c.m, layer));
-    JL_CUDA(cudaGetLastError());
-    return JL_OK;
+    return launch_pdl(k_qk_rope_kv, dim3(c.rows_cap), dim3(256), 0, c.stream, c.m->pass, c.m->s.qkv,
+                      qkv_ld(c.m), c.m->q_heads, L.q_norm, L.k_norm, (const float2*)c.m->rope,
+                      kv_view(c.m, layer));
 }
 
 jl_status launch_attention(const PassCtx& c, int layer) {
     dim3 grid(c.m->q_heads, c.rows_cap);
     const int group = c.m->q_heads / c.m->kv_heads;
     if (c.m->kv.dtype == JL_KV_F32)
-        k_attention<1><<<grid, 128, 0, c.stream>>>(c.m->pass, c.m->s.qkv, qkv_ld(c.m), c.m->q_heads,
-                                                   group, kv_view(c.m, layer), c.m->s.attn);
-    else
-        k_attention<0><<<grid, 128, 0, c.stream>>>(c.m->pass, c.m->s.qkv, qkv_ld(c.m), c.m->q_heads,
-                                                   group, kv_view(c.m, layer), c.m->s.attn);
-    JL_CUDA(cudaGetLastError());
-    return JL_OK;
+        return launch_pdl(k_attention<1>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
+                          qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn);
+    return launch_pdl(k_attention<0>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
+                      qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn);
 }
 
 jl_status launch_o(const PassCtx& c, const LayerW& L) {
+    if (L.mx_o.a && c.rows_cap <= mx_max_tokens())
+        return mx_project(c, L.mx_o, MXE_ADD, 0, c.m->s.attn, c.m->q_heads * HEAD, nullptr, c.m->s.x,
+                          c.m->hidden);
     Proj p = make_proj({&L.o});
     return run_proj<EPI_ADD>(c, L.o.kind, 0, c.m->s.attn, c.m->q_heads * HEAD, p, c.m->s.x, c.m->hidden);
 }
 
 jl_status launch_gateup(const PassCtx& c, const LayerW& L) {
+    if (L.mx_gateup.a && c.rows_cap <= mx_max_tokens())
+        return mx_project(c, L.mx_gateup, MXE_SWIGLU, 0, c.m->s.xn, c.m->hidden, nullptr, c.m->s.act,
+                          c.m->inter);
     Proj p = make_proj({&L.gate, &L.up});
     p.total = L.gate.rows;
     return run_proj<EPI_SWIGLU>(c, L.gate.kind, 0, c.m->s.xn, c.m->hidden, p, c.m->s.act, c.m->inter);
 }
 
 jl_status launch_down(const PassCtx& c, const LayerW& L) {
+    if (L.mx_down.a && c.rows_cap <= mx_max_tokens())
+        return mx_project(c, L.mx_down, MXE_ADD, 0, c.m->s.act, c.m->inter, nullptr, c.m->s.x,
+                          c.m->hidden);
     Proj p = make_proj({&L.down});
     return run_proj<EPI_ADD>(c, L.down.kind, 0, c.m->s.act, c.m->inter, p, c.m->s.x, c.m->hidden);
 }
 
 jl_status launch_head(const PassCtx& c) {
+    if (c.m->mx_head.a && c.head_cap <= mx_max_tokens())
+        return mx_project(c, c.m->mx_head, MXE_STORE, 1, c.m->s.xh, c.m->hidden, nullptr, c.m->s.logits,
+                          c.m->vocab);
     Proj p = make_proj({&c.m->head});
     return run_proj<EPI_STORE>(c, c.m->head.kind, 1, c.m->s.xh, c.m->hidden, p, c.m->s.logits,
                                c.m->vocab);
 }
 
 jl_status launch_argmax(const PassCtx& c) {
-    k_argmax<<<c.head_cap, 1024, 0, c.stream>>>(c.m->pass, c.m->s.logits, c.m->vocab);
-    JL_CUDA(cudaGetLastError());
-    return JL_OK;
+    return launch_pdl(k_argmax, dim3(c.head_cap), dim3(1024), 0, c.stream, c.m->pass,
+                      (const float*)c.m->s.logits, c.m->vocab);
 }
 
 jl_status launch_synth_bf16(uint64_t seed, uint32_t tensor_index, size_t n, uint16_t* out,

@@ -156,10 +156,91 @@ jl_status begin_model(const jl_model_options& o, jl_model** out) {
     JL_TRY(configure_kernels());
     *out = new jl_model();
     (*out)->device = o.device;
+    JL_CUDA(cudaDeviceGetAttribute(&(*out)->sms, cudaDevAttrMultiProcessorCount, o.device));
     return JL_OK;
 }
 
 }  // namespace
+
+// Tensor-core copies of the MXFP4 projections: q|k|v stacked, gate/up
+// interleaved per 64 rows (the SwiGLU epilogue needs both halves of an
+// output in one tile), o, down and an MXFP4 output table.  The row-major
+// checkpoint copy stays for the long-prompt kernel.
+jl_status build_mx(jl_model* m) {
+    auto is_mx = [](const Mat& a) { return a.kind == MAT_MXFP4; };
+    bool all = !m->lw.empty();
+    for (const auto& L : m->lw)
+        all = all && is_mx(L.q) && is_mx(L.k) && is_mx(L.v) && is_mx(L.o) && is_mx(L.gate) &&
+              is_mx(L.up) && is_mx(L.down);
+    const bool head = is_mx(m->head);
+    if (!all && !head) return JL_OK;
+    int dev = 0, sms = 148;
+    JL_CUDA(cudaGetDevice(&dev));
+    JL_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int QW = m->q_heads * HEAD, KVW = m->kv_heads * HEAD;
+    Plan plan;
+    std::vector<size_t> offs;
+    if (all)
+        for (size_t l = 0; l < m->lw.size(); ++l) {
+            offs.push_back(plan.take(mx_tile_bytes(QW + 2 * KVW, m->hidden, false)));
+            offs.push_back(plan.take(mx_tile_bytes(m->hidden, QW, false)));
+            offs.push_back(plan.take(mx_tile_bytes(m->inter, m->hidden, true)));
+            offs.push_back(plan.take(mx_tile_bytes(m->hidden, m->inter, false)));
+        }
+    const size_t head_off = head ? plan.take(mx_tile_bytes(m->vocab, m->hidden, false)) : 0;
+    if (cudaMalloc(&m->mx.arena, plan.bytes) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("cannot allocate %zu bytes for tensor-core weight tiles", plan.bytes);
+        return JL_ERR_OOM;
+    }
+    uint8_t* base = (uint8_t*)m->mx.arena;
+    int maxS = 1, maxT = 1;
+    size_t ws_floats = 1;
+    auto track = [&](const MxProj& p) {
+        maxS = std::max(maxS, p.S);
+        maxT = std::max(maxT, p.T);
+        ws_floats = std::max(ws_floats, (size_t)p.T * p.ksplit * mx_max_tokens() * 128);
+    };
+    if (all)
+        for (size_t l = 0; l < m->lw.size(); ++l) {
+            LayerW& L = m->lw[l];
+            const Mat* qkv[3] = {&L.q, &L.k, &L.v};
+            const Mat* o[1] = {&L.o};
+            const Mat* gu[2] = {&L.gate, &L.up};
+            const Mat* dn[1] = {&L.down};
+            JL_TRY(mx_build(qkv, 3, false, base + offs[4 * l], sms, &L.mx_qkv, 0));
+            JL_TRY(mx_build(o, 1, false, base + offs[4 * l + 1], sms, &L.mx_o, 0));
+            JL_TRY(mx_build(gu, 2, true, base + offs[4 * l + 2], sms, &L.mx_gateup, 0));
+            JL_TRY(mx_build(dn, 1, false, base + offs[4 * l + 3], sms, &L.mx_down, 0));
+            track(L.mx_qkv);
+            track(L.mx_o);
+            track(L.mx_gateup);
+            track(L.mx_down);
+        }
+    if (head) {
+        const Mat* h[1] = {&m->head};
+        JL_TRY(mx_build(h, 1, false, base + head_off, sms, &m->mx_head, 0));
+        track(m->mx_head);
+    }
+    Plan sp;
+    const size_t off_b = sp.take((size_t)maxS * mx_max_tokens() * 8 * 128);
+    const size_t off_sf = sp.take((size_t)maxS * 1024);
+    const size_t off_ws = sp.take(ws_floats * sizeof(float));
+    const size_t off_t = sp.take((size_t)maxT * sizeof(int));
+    if (cudaMalloc(&m->mx.scratch, sp.bytes) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("cannot allocate tensor-core scratch");
+        return JL_ERR_OOM;
+    }
+    JL_CUDA(cudaMemset(m->mx.scratch, 0, sp.bytes));
+    uint8_t* s = (uint8_t*)m->mx.scratch;
+    m->mx.bimg = s + off_b;
+    m->mx.sfb = s + off_sf;
+    m->mx.ws = (float*)(s + off_ws);
+    m->mx.tickets = (int*)(s + off_t);
+    JL_CUDA(cudaDeviceSynchronize());
+    return JL_OK;
+}
 
 jl_status model_from_weights(jl_weights* w, const HostConfig& cfg, const jl_model_options& o,
                              jl_model** out) {
@@ -298,6 +379,7 @@ jl_status model_from_weights(jl_weights* w, const HostConfig& cfg, const jl_mode
     }
     if (tied) m->head = m->embed;
     JL_TRY(finish_model(m, o));
+    JL_TRY(build_mx(m));
     *out = guard.release();
     return JL_OK;
 }
@@ -423,6 +505,7 @@ jl_status model_synthesize(const jl_synth_config& c, const jl_model_options& o, 
     if (e != cudaSuccess) return cuda_fail(e, "weight synthesis", __FILE__, __LINE__);
     if (c.tied) m->head = m->embed;
     JL_TRY(finish_model(m, o));
+    JL_TRY(build_mx(m));
     *out = guard.release();
     return JL_OK;
 }
@@ -433,11 +516,14 @@ void model_free(jl_model* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     for (auto* g : m->spec_graphs) spec_graph_free(g);
     m->spec_graphs.clear();
-    if (m->small_graph) cudaGraphExecDestroy(m->small_graph);
+    for (auto& g : m->small_graph)
+        if (g) cudaGraphExecDestroy(g);
     cudaFree(m->arena);
     cudaFree(m->rope);
     cudaFree(m->kv.base);
     cudaFree(m->scratch_arena);
+    cudaFree(m->mx.arena);
+    cudaFree(m->mx.scratch);
     cudaFreeHost(m->host_hdr);
     cudaFreeHost(m->host_row);
     cudaFreeHost(m->host_head_row);

@@ -35,7 +35,7 @@ EXPORTS = (
     "jl_model_read_tensor", "jl_cache_create", "jl_cache_free", "jl_cache_len",
     "jl_cache_truncate", "jl_predict", "jl_next_token", "jl_hidden", "jl_generate",
     "jl_schedule_fixed", "jl_schedule_adaptive", "jl_spec_options_default",
-    "jl_generate_speculative", "jl_time_pass", "jl_time_projection",
+    "jl_generate_speculative", "jl_time_pass", "jl_time_projection", "jl_project",
 )
 PROJ_QKV, PROJ_O, PROJ_GATE_UP, PROJ_DOWN, PROJ_HEAD = 0, 1, 2, 3, 4
 
@@ -140,6 +140,7 @@ def _load():
                           ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
         "jl_time_projection": ([vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                 ctypes.POINTER(ctypes.c_double), ctypes.POINTER(sz)], ctypes.c_int),
+        "jl_project": ([vp, ctypes.c_int, ctypes.c_int, f32p, sz, f32p], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -330,6 +331,18 @@ class Model:
         check(lib.jl_time_pass(self._h, _p(t, ctypes.c_uint32), len(t), rows, reps,
                                ctypes.byref(wall), ctypes.byref(gpu)))
         return wall.value, gpu.value
+
+    def project(self, layer: int, which: int, x) -> np.ndarray:
+        """One layer projection as the pass runs it (``matmul``, lib.rs:240-266,
+        in its fused forms); see jl_project in include/jalapeno.h."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        widths = {PROJ_QKV: (self.info.q_heads + 2 * self.info.kv_heads) * 128,
+                  PROJ_O: self.info.hidden, PROJ_GATE_UP: self.info.inter,
+                  PROJ_DOWN: self.info.hidden, PROJ_HEAD: self.info.vocab}
+        y = np.empty((x.shape[0], widths[which]), np.float32)
+        check(lib.jl_project(self._h, layer, which, _p(x, ctypes.c_float), x.shape[0],
+                             _p(y, ctypes.c_float)))
+        return y
 
     def time_projection(self, layer: int, which: int, rows: int, iters: int = 20) -> tuple[float, int]:
         """Mean device ms per launch of one projection kernel, and its weight bytes."""

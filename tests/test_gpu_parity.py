@@ -95,8 +95,10 @@ def test_logits_match_oracle(oracles, key, kv):
     rids, rlg = ref.predict(PROMPT, ref.cache(), all=True, logits=True)
     assert logits_close(lg, rlg)
     # against an oracle that rounds K/V like the cache under test: much tighter
+    # (a bf16 cache can round a last-bit difference of K to the next bf16
+    # value, so its bound is looser than the f32 cache's)
     bids, blg = ref.predict(PROMPT, ref.cache(round_bf16=kv == J.KV_BF16), all=True, logits=True)
-    assert rel_l2(lg, blg) < 1e-5
+    assert rel_l2(lg, blg) < (1e-5 if kv == J.KV_F32 else 1e-4)
     assert ids == bids
 
 
