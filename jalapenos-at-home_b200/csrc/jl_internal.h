@@ -202,6 +202,7 @@ struct jl_model {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     cudaGraphExec_t small_graph[5] = {};  // full pass for rows <= 1, 2, 4, 8, 16
     std::vector<jl::SpecGraph*> spec_graphs;  // owned; freed by model_free
+    std::vector<jl_cache*> caches;              // live caches; detached by model_free
     int* counters = nullptr;              // zeroed split-K / reduction counters
     std::map<std::string, std::pair<const void*, size_t>> tensor_index;  // name -> device bytes
 };

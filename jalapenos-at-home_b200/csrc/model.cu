@@ -1,5 +1,6 @@
 // Device model construction (GpuModel::new, engine/src/gpu.rs:336-428),
 // the paged KV pool and caches (GpuCache, engine/src/gpu.rs:272-300).
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -516,6 +517,10 @@ void model_free(jl_model* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     for (auto* g : m->spec_graphs) spec_graph_free(g);
     m->spec_graphs.clear();
+    // caches may outlive their model (a garbage collector frees both in any
+    // order): they keep their own page tables and forget the model
+    for (jl_cache* c : m->caches) c->m = nullptr;
+    m->caches.clear();
     for (auto& g : m->small_graph)
         if (g) cudaGraphExecDestroy(g);
     cudaFree(m->arena);
@@ -550,6 +555,7 @@ jl_status cache_create(jl_model* m, jl_cache** out) {
         set_error("cannot allocate a page table");
         return JL_ERR_OOM;
     }
+    m->caches.push_back(c);
     *out = c;
     return JL_OK;
 }
@@ -557,9 +563,11 @@ jl_status cache_create(jl_model* m, jl_cache** out) {
 void cache_free(jl_cache* c) {
     if (!c) return;
     if (c->m) {
-        cudaSetDevice(c->m->device);
-        if (c->m->stream) cudaStreamSynchronize(c->m->stream);
-        for (int32_t p : c->pages) c->m->kv.free_list.push_back(p);
+        jl_model* m = c->m;
+        cudaSetDevice(m->device);
+        if (m->stream) cudaStreamSynchronize(m->stream);
+        for (int32_t p : c->pages) m->kv.free_list.push_back(p);
+        m->caches.erase(std::remove(m->caches.begin(), m->caches.end(), c), m->caches.end());
     }
     cudaFree(c->d_pages);
     cudaFreeHost(c->h_pages);
