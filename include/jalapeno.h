@@ -234,6 +234,22 @@ typedef enum jl_projection {
 jl_status jl_project(jl_model* m, int layer, jl_projection which, const float* x, size_t rows,
                      float* y);
 
+/* jl_project for callers that cannot allocate device memory when they call
+ * it (a host running under a fixed device-memory reservation, or code that
+ * cannot take cudaMalloc's implicit synchronisation).  No counterpart in the
+ * reference: it exists for this engine's C ABI only.
+ *   x: device pointer, rows x input width f32; y: device pointer, rows x
+ *   output width f32 (widths as for jl_project); stream: a cudaStream_t of
+ *   m's device, or NULL for the model's own stream.
+ * MXFP4 projections on the tensor-core path only; rows 1..8.  All scratch
+ * comes from one fixed 4 MiB device array per device (no allocation of any
+ * kind); a projection whose scratch would exceed it is rejected with
+ * JL_ERR_INVALID_ARG.  Calls share that array, so calls that overlap on
+ * the GPU race.  The first call on a device looks up the array's address.
+ * Returns after the projection has finished (the stream is synchronised). */
+jl_status jl_project_noalloc(jl_model* m, int layer, jl_projection which, const float* x,
+                             size_t rows, float* y, void* stream);
+
 /* ------------------------------------------------------------------------
  * Profiling.
  * ---------------------------------------------------------------------- */

@@ -291,6 +291,12 @@ jl_status jl_project(jl_model* m, int layer, jl_projection which, const float* x
     JL_GUARD({ return project(m, layer, (int)which, x, rows, y); })
 }
 
+jl_status jl_project_noalloc(jl_model* m, int layer, jl_projection which, const float* x,
+                             size_t rows, float* y, void* stream) {
+    JL_NEED(m && x && y, "model, x and y must be non-null");
+    JL_GUARD({ return project_noalloc(m, layer, (int)which, x, rows, y, (cudaStream_t)stream); })
+}
+
 jl_status jl_time_projection(jl_model* m, int layer, jl_projection which, int rows, int iters,
                              double* ms_per_launch, size_t* weight_bytes) {
     JL_NEED(m && ms_per_launch && weight_bytes, "model and outputs must be non-null");

@@ -282,6 +282,20 @@ jl_status mx_build(const Mat* const* mats, int nmats, bool swiglu, uint8_t* dst,
                    MxProj* out, cudaStream_t stream);
 jl_status mx_project(const PassCtx& c, const MxProj& p, int epi, int use_head, const float* x,
                      int ldx, const uint16_t* norm, float* y, int ldy);
+// Scratch one launch of `p` over `mcap` rows needs when the caller supplies
+// it: split-K tickets (zero at launch), piece scale atoms, piece images and
+// split-K partials, in that order, each 256-byte aligned.
+struct MxScratchPlan {
+    size_t tickets = 0, sfb = 0, bimg = 0, ws = 0, total = 0;
+};
+MxScratchPlan mx_scratch_plan(const MxProj& p, int mcap);
+// mx_project over caller-owned memory: `hdr` (rows read on the device),
+// `scratch` laid out as mx_scratch_plan says, `err` the device error flag.
+jl_status mx_project_with(const MxProj& p, int epi, const PassHdr* hdr, int mcap, const float* x,
+                          int ldx, float* y, int ldy, uint8_t* scratch, int* err, int sms,
+                          cudaStream_t stream);
+jl_status project_noalloc(jl_model* m, int layer, int which, const float* x, size_t rows, float* y,
+                          cudaStream_t stream);
 // Builds the tensor-core copies of every MXFP4 projection of `m` (model.cu).
 jl_status build_mx(jl_model* m);
 jl_status launch_fill_u16(uint16_t* out, size_t n, uint16_t value, cudaStream_t stream);

@@ -583,4 +583,57 @@ jl_status mx_project(const PassCtx& c, const MxProj& p, int epi, int use_head, c
     return launch_pdl(k_mx_gemv<MX_STORE>, grid, dim3(MX_THREADS), smem, c.stream, a);
 }
 
+MxScratchPlan mx_scratch_plan(const MxProj& p, int mcap) {
+    auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    MxScratchPlan s;
+    s.tickets = up((size_t)p.T * sizeof(int));
+    s.sfb = up((size_t)p.S * SF_STAGE);
+    s.bimg = up((size_t)p.S * PIECES * mcap * 128);
+    s.ws = p.ksplit > 1 ? up((size_t)p.T * p.ksplit * mcap * 128 * sizeof(float)) : 0;
+    s.total = s.tickets + s.sfb + s.bimg + s.ws;
+    return s;
+}
+
+jl_status mx_project_with(const MxProj& p, int epi, const PassHdr* hdr, int mcap, const float* x,
+                          int ldx, float* y, int ldy, uint8_t* scratch, int* err, int sms,
+                          cudaStream_t stream) {
+    if (mcap < 1 || mcap > MX_MAXTOK) {
+        set_error("tensor-core projection takes 1..%d rows per pass, got %d", MX_MAXTOK, mcap);
+        return JL_ERR_INVALID_ARG;
+    }
+    const MxScratchPlan plan = mx_scratch_plan(p, mcap);
+    int* tickets = (int*)scratch;
+    uint8_t* sfb = scratch + plan.tickets;
+    uint8_t* bimg = sfb + plan.sfb;
+    float* ws = (float*)(bimg + plan.bimg);
+    const int N = PIECES * mcap;
+    const int items = mcap * p.S * (STAGE_K / 32);
+    JL_TRY(launch_pdl(k_mx_pieces, dim3((items + 7) / 8), dim3(256), 0, stream, hdr, 0, mcap, x, ldx,
+                      p.K, p.S, N, bimg, sfb));
+    MxArgs a;
+    a.a = p.a;
+    a.sfa = p.sfa;
+    a.b = bimg;
+    a.sfb = sfb;
+    a.T = p.T;
+    a.S = p.S;
+    a.ksplit = p.ksplit;
+    a.N = N;
+    a.mcap = mcap;
+    mx_shape(N, &a.stages, &a.nbuf);
+    a.hdr = hdr;
+    a.use_head = 0;
+    a.y = y;
+    a.ldy = ldy;
+    a.out_rows = p.out_rows;
+    a.ws = ws;
+    a.tickets = tickets;
+    a.err = err;
+    const dim3 grid(std::min(p.T * p.ksplit, sms));
+    const size_t smem = mx_smem(N);
+    if (epi == MX_ADD) return launch_pdl(k_mx_gemv<MX_ADD>, grid, dim3(MX_THREADS), smem, stream, a);
+    if (epi == MX_SWIGLU) return launch_pdl(k_mx_gemv<MX_SWIGLU>, grid, dim3(MX_THREADS), smem, stream, a);
+    return launch_pdl(k_mx_gemv<MX_STORE>, grid, dim3(MX_THREADS), smem, stream, a);
+}
+
 }  // namespace jl

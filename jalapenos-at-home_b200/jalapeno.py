@@ -36,6 +36,7 @@ EXPORTS = (
     "jl_cache_truncate", "jl_predict", "jl_next_token", "jl_hidden", "jl_generate",
     "jl_schedule_fixed", "jl_schedule_adaptive", "jl_spec_options_default",
     "jl_generate_speculative", "jl_time_pass", "jl_time_projection", "jl_project",
+    "jl_project_noalloc",
 )
 PROJ_QKV, PROJ_O, PROJ_GATE_UP, PROJ_DOWN, PROJ_HEAD = 0, 1, 2, 3, 4
 
@@ -141,6 +142,7 @@ def _load():
         "jl_time_projection": ([vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                 ctypes.POINTER(ctypes.c_double), ctypes.POINTER(sz)], ctypes.c_int),
         "jl_project": ([vp, ctypes.c_int, ctypes.c_int, f32p, sz, f32p], ctypes.c_int),
+        "jl_project_noalloc": ([vp, ctypes.c_int, ctypes.c_int, vp, sz, vp, vp], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -343,6 +345,15 @@ class Model:
         check(lib.jl_project(self._h, layer, which, _p(x, ctypes.c_float), x.shape[0],
                              _p(y, ctypes.c_float)))
         return y
+
+    def project_noalloc(self, layer: int, which: int, x_ptr: int, rows: int, y_ptr: int,
+                        stream: int = 0) -> None:
+        """jl_project on device memory the caller owns, with no allocation:
+        ``x_ptr``/``y_ptr`` are device addresses of f32 [rows, width] arrays
+        (widths as for :meth:`project`), ``stream`` a cudaStream_t handle or 0
+        for the model's stream.  See jl_project_noalloc in include/jalapeno.h."""
+        check(lib.jl_project_noalloc(self._h, layer, which, ctypes.c_void_p(x_ptr), rows,
+                                     ctypes.c_void_p(y_ptr), ctypes.c_void_p(stream or None)))
 
     def time_projection(self, layer: int, which: int, rows: int, iters: int = 20) -> tuple[float, int]:
         """Mean device ms per launch of one projection kernel, and its weight bytes."""
