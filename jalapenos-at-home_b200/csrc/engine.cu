@@ -316,8 +316,72 @@ jl_status host_pass(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int
 
 }  // namespace
 
+// The decode pass with every MXFP4 projection fused with its neighbours:
+// five kernels per layer.  Each projection's epilogue writes the next one's
+// input pieces (and, after a residual add, the sums of squares the next
+// RMSNorm needs), so no normalisation or quantisation kernel runs between
+// them; the q|k|v epilogue also does QK-norm, RoPE and the cache append.
+jl_status record_fused_pass(const PassCtx& c, int layers) {
+    const jl_model* m = c.m;
+    const MxBuffers& B = m->mx;
+    const int h = m->hidden, tiles = h / 128;
+    JL_TRY(launch_embed(c));
+    if (layers > 0) JL_TRY(mx_norm_pieces(c, m->s.x, h, m->lw[0].in_ln, h, B.bx, B.sfx, B.part));
+    for (int l = 0; l < layers; ++l) {
+        const LayerW& L = m->lw[l];
+        MxFuse qkv;  // model.rs:174-177, lib.rs:353-396
+        qkv.b = B.bx;
+        qkv.sfb = B.sfx;
+        qkv.part_in = B.part;
+        qkv.part_tiles = tiles;
+        qkv.norm_width = h;
+        qkv.layer = l;
+        qkv.qn = L.q_norm;
+        qkv.kn = L.k_norm;
+        JL_TRY(mx_project_fused(c, L.mx_qkv, MXE_QKV, qkv, m->s.qkv, qkv_ld(m)));
+        JL_TRY(launch_attention(c, l, true));  // lib.rs:401-441
+        MxFuse o;  // lib.rs:444-449 + residual, then post_attention_layernorm
+        o.b = B.battn;
+        o.sfb = B.sfattn;
+        o.bout = B.bx;
+        o.sfout = B.sfx;
+        o.part_out = B.part;
+        o.next_w = L.post_ln;
+        JL_TRY(mx_project_fused(c, L.mx_o, MXE_ADD, o, m->s.x, h));
+        MxFuse gu;  // lib.rs:459-463
+        gu.b = B.bx;
+        gu.sfb = B.sfx;
+        gu.part_in = B.part;
+        gu.part_tiles = tiles;
+        gu.norm_width = h;
+        gu.bout = B.bact;
+        gu.sfout = B.sfact;
+        JL_TRY(mx_project_fused(c, L.mx_gateup, MXE_SWIGLU, gu, nullptr, m->inter));
+        MxFuse dn;  // lib.rs:464-467 + residual, then the next input_layernorm
+        dn.b = B.bact;
+        dn.sfb = B.sfact;
+        if (l + 1 < layers) {
+            dn.bout = B.bx;
+            dn.sfout = B.sfx;
+            dn.part_out = B.part;
+            dn.next_w = m->lw[l + 1].in_ln;
+        }
+        JL_TRY(mx_project_fused(c, L.mx_down, MXE_ADD, dn, m->s.x, h));
+    }
+    return JL_OK;
+}
+
 jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head) {
     const jl_model* m = c.m;
+    if (m->mx.fused && c.rows_cap <= mx_max_tokens()) {
+        JL_TRY(record_fused_pass(c, layers));
+        if (with_head) {
+            JL_TRY(launch_rmsnorm(c, m->s.x, m->final_norm, m->s.xh, true));  // model.rs:228
+            JL_TRY(launch_head(c));                                           // model.rs:229-234
+            JL_TRY(launch_argmax(c));                                         // model.rs:235-239
+        }
+        return JL_OK;
+    }
     JL_TRY(launch_embed(c));
     for (int l = 0; l < layers; ++l) {
         const LayerW& L = m->lw[l];

@@ -115,7 +115,18 @@ struct MxBuffers {
     float* ws = nullptr;       // split-K partials
     int* tickets = nullptr;    // split-K arrival counters (kept at zero between launches)
     void* arena = nullptr;     // tiled weights
-    void* scratch = nullptr;   // bimg, sfb, ws, tickets
+    void* scratch = nullptr;   // bimg, sfb, ws, tickets and the fused-pass buffers below
+    // Fused decode pass (every layer MXFP4, widths multiples of 256): piece
+    // images of the normalised residual stream (x), the attention output and
+    // the SwiGLU activations, and per-tile sums of squares of x.
+    bool fused = false;
+    uint8_t* bx = nullptr;
+    uint8_t* sfx = nullptr;
+    uint8_t* battn = nullptr;
+    uint8_t* sfattn = nullptr;
+    uint8_t* bact = nullptr;
+    uint8_t* sfact = nullptr;
+    float* part = nullptr;     // [hidden / 128][MX_PART_STRIDE]
 };
 
 struct LayerW {
@@ -263,7 +274,7 @@ jl_status launch_rmsnorm(const PassCtx& c, const float* x, const uint16_t* w, fl
                          bool head_rows);
 jl_status launch_qkv(const PassCtx& c, const LayerW& L);
 jl_status launch_qk_rope_kv(const PassCtx& c, int layer, const LayerW& L);
-jl_status launch_attention(const PassCtx& c, int layer);
+jl_status launch_attention(const PassCtx& c, int layer, bool pieces = false);
 jl_status launch_o(const PassCtx& c, const LayerW& L);
 jl_status launch_gateup(const PassCtx& c, const LayerW& L);
 jl_status launch_down(const PassCtx& c, const LayerW& L);
@@ -274,7 +285,23 @@ jl_status launch_synth_bf16(uint64_t seed, uint32_t tensor_index, size_t n, uint
                             cudaStream_t stream);
 
 // ---- tensor-core MXFP4 projections (mx_mma.cu) ---------------------------------
-enum MxEpi : int { MXE_STORE = 0, MXE_ADD = 1, MXE_SWIGLU = 2 };
+enum MxEpi : int { MXE_STORE = 0, MXE_ADD = 1, MXE_SWIGLU = 2, MXE_QKV = 3 };
+constexpr int MX_PART_STRIDE = 16;  // rows per tile in the sum-of-squares partials
+// Fused decode-pass projection (mx_project_fused): its input pieces are
+// already in (b, sfb), written by the kernel before it.
+struct MxFuse {
+    const uint8_t* b = nullptr;        // input pieces
+    const uint8_t* sfb = nullptr;
+    const float* part_in = nullptr;    // input RMSNorm: per-tile sums of squares of x
+    int part_tiles = 0, norm_width = 0;
+    uint8_t* bout = nullptr;           // pieces of (output * next_w) for the next projection
+    uint8_t* sfout = nullptr;
+    float* part_out = nullptr;         // per-tile sums of squares of the output (residual add)
+    const uint16_t* next_w = nullptr;
+    int layer = 0;                     // q|k|v: cache layer and QK-norm weights
+    const uint16_t* qn = nullptr;
+    const uint16_t* kn = nullptr;
+};
 jl_status mx_configure();
 int mx_max_tokens();
 size_t mx_tile_bytes(int out_rows, int K, bool swiglu);
@@ -289,6 +316,12 @@ struct MxScratchPlan {
     size_t tickets = 0, sfb = 0, bimg = 0, ws = 0, total = 0;
 };
 MxScratchPlan mx_scratch_plan(const MxProj& p, int mcap);
+jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxFuse& f, float* y,
+                           int ldy);
+// Pieces of x * w and per-tile sums of squares of x for the first projection
+// of a fused pass (after the embedding).
+jl_status mx_norm_pieces(const PassCtx& c, const float* x, int ldx, const uint16_t* w, int width,
+                         uint8_t* bout, uint8_t* sfout, float* part);
 // mx_project over caller-owned memory: `hdr` (rows read on the device),
 // `scratch` laid out as mx_scratch_plan says, `err` the device error flag.
 jl_status mx_project_with(const MxProj& p, int epi, const PassHdr* hdr, int mcap, const float* x,

@@ -12,6 +12,7 @@
 #include "jl_internal.h"
 #include "kernels.cuh"
 #include "launch.cuh"
+#include "mx_pieces.cuh"
 #include "ptx.cuh"
 
 namespace jl {
@@ -381,26 +382,6 @@ __global__ void k_rmsnorm(PassBuf pb, const float* __restrict__ x, int ldx,
         o[j] = __fmul_rn(__fdiv_rn(xr[j], size), bf16f(w[j]));
 }
 
-struct KvView {
-    void* k;       // this layer's K pages
-    void* v;       // this layer's V pages
-    int kv_heads;
-    int f32;       // 1: f32 elements, 0: bf16
-    int pages;     // pool size: page ids outside [0, pages) are never dereferenced
-    int max_pos;   // RoPE table rows (context limit)
-    int* err;      // device error flag: bit 0 page id out of range, bit 1 bad position
-};
-
-__device__ __forceinline__ bool page_ok(const KvView& kv, int page) {
-    if ((unsigned)page < (unsigned)kv.pages) return true;
-    atomicOr(kv.err, 1);
-    return false;
-}
-
-__device__ __forceinline__ size_t kv_index(int page, int kvh, int t, int kv_heads) {
-    return (((size_t)page * kv_heads + kvh) * PAGE + t) * HEAD;
-}
-
 // Per-head QK-RMSNorm and RoPE of q and k, then K and V appended to the cache
 // (lib.rs:363-396): one warp per head, lane owns dims {l, l+32, l+64, l+96}
 // so both RoPE pairs (i, i+64) stay in the lane.
@@ -472,23 +453,32 @@ __device__ __forceinline__ float kv_load(const void* base, size_t idx) {
 // Causal GQA attention for one (q head, row): softmax(q.k / sqrt(128)) . v
 // over positions [0, pos] of the row's sequence (lib.rs:401-441), in chunks
 // of 128 positions with a running max.
+//
+// With `bout` set, the output row also goes out as the o projection's input
+// pieces (one 32-block per warp), and rows past the pass's row count get
+// zero pieces so every MMA column of the next projection is defined.
 template <int F32>
 __global__ void __launch_bounds__(128) k_attention(PassBuf pb, const float* __restrict__ qkv,
                                                    int ld, int q_heads, int group, KvView kv,
-                                                   float* __restrict__ out) {
-    __shared__ float qs[HEAD];
+                                                   float* __restrict__ out, uint8_t* __restrict__ bout,
+                                                   uint8_t* __restrict__ sfout, int bN) {
+    __shared__ __align__(16) float qs[HEAD];
     __shared__ float pr[128];
     __shared__ float red[32];
     ptx::grid_dependency_wait();  // PDL: the previous kernel's writes are visible past here
     ptx::launch_dependents();
     const int h = blockIdx.x, row = blockIdx.y;
-    if (row >= pb.hdr->rows) return;
-    const RowDesc rd = pb.row[row];
     const int t = threadIdx.x;
+    if (row >= pb.hdr->rows) {
+        if (bout) mx::emit_pieces_smem(qs, HEAD, 4, row, 0, 1, t, 128, h * HEAD, bN, bout, sfout);
+        return;
+    }
+    const RowDesc rd = pb.row[row];
     const int kvh = h / group;
     if (rd.pos < 0 || rd.pos >= kv.max_pos || (unsigned)rd.seq >= (unsigned)MAX_SEQS) {
         if (t == 0) atomicOr(kv.err, 2);
         out[(size_t)row * (q_heads * HEAD) + h * HEAD + t] = 0.f;
+        if (bout) mx::emit_pieces_smem(qs, HEAD, 4, row, 0, 1, t, 128, h * HEAD, bN, bout, sfout);
         return;
     }
     const int visible = rd.pos + 1;
@@ -547,7 +537,13 @@ __global__ void __launch_bounds__(128) k_attention(PassBuf pb, const float* __re
         m = nm;
         __syncthreads();
     }
-    out[(size_t)row * (q_heads * HEAD) + h * HEAD + t] = __fdiv_rn(acc, l);
+    const float o = __fdiv_rn(acc, l);
+    out[(size_t)row * (q_heads * HEAD) + h * HEAD + t] = o;
+    if (bout) {  // every thread is past its last read of qs (the loop ends on a barrier)
+        qs[t] = o;
+        __syncthreads();
+        mx::emit_pieces_smem(qs, HEAD, 4, row, 1, 1, t, 128, h * HEAD, bN, bout, sfout);
+    }
 }
 
 // First maximum of each predicted row, ties to the lower index
@@ -723,21 +719,6 @@ jl_status run_proj(const PassCtx& c, int kind, int use_head, const float* x, int
     return run_proj_kind<MAT_BF16, EPI>(c, use_head, x, ldx, p, y, ldy);
 }
 
-KvView kv_view(const jl_model* m, int layer) {
-    KvView v;
-    const size_t bytes_layer = m->kv.pages * m->kv.page_elems * m->kv.elem;
-    char* base = (char*)m->kv.base + (size_t)layer * 2 * bytes_layer;
-    v.k = base;
-    v.v = base + bytes_layer;
-    v.kv_heads = m->kv_heads;
-    v.f32 = m->kv.dtype == JL_KV_F32;
-    v.pages = (int)m->kv.pages;
-    v.max_pos = m->max_positions;
-    v.err = m->counters;
-    return v;
-}
-
-int qkv_ld(const jl_model* m) { return (m->q_heads + 2 * m->kv_heads) * HEAD; }
 
 template <int KIND, int EPI>
 jl_status configure_skinny() {
@@ -793,14 +774,17 @@ jl_status launch_qk_rope_kv(const PassCtx& c, int layer, const LayerW& L) {
                       kv_view(c.m, layer));
 }
 
-jl_status launch_attention(const PassCtx& c, int layer) {
+jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     dim3 grid(c.m->q_heads, c.rows_cap);
     const int group = c.m->q_heads / c.m->kv_heads;
+    uint8_t* bout = pieces ? c.m->mx.battn : nullptr;
+    uint8_t* sfout = pieces ? c.m->mx.sfattn : nullptr;
+    const int bN = 8 * c.rows_cap;
     if (c.m->kv.dtype == JL_KV_F32)
         return launch_pdl(k_attention<1>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
-                          qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn);
+                          qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn, bout, sfout, bN);
     return launch_pdl(k_attention<0>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
-                      qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn);
+                      qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn, bout, sfout, bN);
 }
 
 jl_status launch_o(const PassCtx& c, const LayerW& L) {

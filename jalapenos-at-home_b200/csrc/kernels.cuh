@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "jl_internal.h"
+
 namespace jl {
 
 __device__ __forceinline__ float bf16f(uint32_t bits) { return __uint_as_float(bits << 16); }
@@ -75,5 +77,43 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
                  : "l"(p));
     return v;
 }
+
+// One layer's view of the paged KV pool ([page][kv_head][PAGE][HEAD]).
+struct KvView {
+    void* k;       // this layer's K pages
+    void* v;       // this layer's V pages
+    int kv_heads;
+    int f32;       // 1: f32 elements, 0: bf16
+    int pages;     // pool size: page ids outside [0, pages) are never dereferenced
+    int max_pos;   // RoPE table rows (context limit)
+    int* err;      // device error flag: bit 0 page id out of range, bit 1 bad position
+};
+
+__device__ __forceinline__ bool page_ok(const KvView& kv, int page) {
+    if ((unsigned)page < (unsigned)kv.pages) return true;
+    atomicOr(kv.err, 1);
+    return false;
+}
+
+__device__ __forceinline__ size_t kv_index(int page, int kvh, int t, int kv_heads) {
+    return (((size_t)page * kv_heads + kvh) * PAGE + t) * HEAD;
+}
+
+// Host side: the view of `layer` and the row stride of the fused q|k|v buffer.
+inline KvView kv_view(const jl_model* m, int layer) {
+    KvView v;
+    const size_t bytes_layer = m->kv.pages * m->kv.page_elems * m->kv.elem;
+    char* base = (char*)m->kv.base + (size_t)layer * 2 * bytes_layer;
+    v.k = base;
+    v.v = base + bytes_layer;
+    v.kv_heads = m->kv_heads;
+    v.f32 = m->kv.dtype == JL_KV_F32;
+    v.pages = (int)m->kv.pages;
+    v.max_pos = m->max_positions;
+    v.err = m->counters;
+    return v;
+}
+
+inline int qkv_ld(const jl_model* m) { return (m->q_heads + 2 * m->kv_heads) * HEAD; }
 
 }  // namespace jl

@@ -228,6 +228,21 @@ jl_status build_mx(jl_model* m) {
     const size_t off_sf = sp.take((size_t)maxS * 1024);
     const size_t off_ws = sp.take(ws_floats * sizeof(float));
     const size_t off_t = sp.take((size_t)maxT * sizeof(int));
+    // fused decode pass: piece images need whole 256-element stages
+    const bool fused = all && m->hidden % 256 == 0 && QW % 256 == 0 && m->inter % 256 == 0;
+    const size_t img_x = (size_t)(m->hidden / 256) * mx_max_tokens() * 8 * 128;
+    const size_t img_a = (size_t)(QW / 256) * mx_max_tokens() * 8 * 128;
+    const size_t img_f = (size_t)(m->inter / 256) * mx_max_tokens() * 8 * 128;
+    size_t off_fx = 0, off_fsx = 0, off_fa = 0, off_fsa = 0, off_ff = 0, off_fsf = 0, off_fp = 0;
+    if (fused) {
+        off_fx = sp.take(img_x);
+        off_fsx = sp.take((size_t)(m->hidden / 256) * 1024);
+        off_fa = sp.take(img_a);
+        off_fsa = sp.take((size_t)(QW / 256) * 1024);
+        off_ff = sp.take(img_f);
+        off_fsf = sp.take((size_t)(m->inter / 256) * 1024);
+        off_fp = sp.take((size_t)(m->hidden / 128) * MX_PART_STRIDE * sizeof(float));
+    }
     if (cudaMalloc(&m->mx.scratch, sp.bytes) != cudaSuccess) {
         cudaGetLastError();
         set_error("cannot allocate tensor-core scratch");
@@ -239,6 +254,16 @@ jl_status build_mx(jl_model* m) {
     m->mx.sfb = s + off_sf;
     m->mx.ws = (float*)(s + off_ws);
     m->mx.tickets = (int*)(s + off_t);
+    if (fused) {
+        m->mx.fused = true;
+        m->mx.bx = s + off_fx;
+        m->mx.sfx = s + off_fsx;
+        m->mx.battn = s + off_fa;
+        m->mx.sfattn = s + off_fsa;
+        m->mx.bact = s + off_ff;
+        m->mx.sfact = s + off_fsf;
+        m->mx.part = (float*)(s + off_fp);
+    }
     JL_CUDA(cudaDeviceSynchronize());
     return JL_OK;
 }

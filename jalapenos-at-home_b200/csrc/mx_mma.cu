@@ -30,50 +30,27 @@
 #include "jl_internal.h"
 #include "kernels.cuh"
 #include "launch.cuh"
+#include "mx_pieces.cuh"
 #include "ptx.cuh"
 
 namespace jl {
 
 namespace {
 
-constexpr int PIECES = 8;
+using mx::PIECES;
+using mx::SF_STAGE;
+using mx::STAGE_K;
+using mx::sf_offset;
+using mx::swz128;
+
 constexpr int TILE_ROWS = 128;
-constexpr int STAGE_K = 256;             // K elements per pipeline stage
 constexpr int A_STAGE = 128 * 128;       // bytes of one weight tile stage
-constexpr int SF_STAGE = 1024;           // two scale atoms
 constexpr uint32_t WAIT_LIMIT = 1u << 22;  // polls before a wait reports failure (seconds)
 constexpr int TMEM_COLS = 256;
 constexpr int ACC_COL = 0, SFA_COL = 128, SFB_COL = 136;
 
-__device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t byte) {
-    // byte offset of (row, byte-in-row) in a 128B-swizzled K-major image
-    return (row >> 3) * 1024 + (row & 7) * 128 + ((((byte >> 4) ^ (row & 7)) & 7) << 4) + (byte & 15);
-}
-
-__device__ __forceinline__ uint32_t sf_offset(uint32_t row, uint32_t kb) {
-    // kb: scale block within the stage (0..7); row < 128
-    return (kb >> 2) * 512 + 16 * (row & 31) + 4 * (row >> 5) + (kb & 3);
-}
-
 // ---------------------------------------------------------------------------
 // activation pieces
-
-// 2^e as an exact f32 for e in [-127, 127].
-__device__ __forceinline__ float pow2i(int e) {
-    return e >= -126 ? __uint_as_float((uint32_t)(e + 127) << 23) : __uint_as_float(0x00400000u);
-}
-
-// Smallest E8M0 exponent e with amax <= 6 * 2^e (amax >= 0), clamped to the
-// E8M0 range; -127 for an all-zero block.
-__device__ __forceinline__ int piece_exponent(float amax) {
-    const uint32_t b = __float_as_uint(amax);
-    const int eb = (int)((b >> 23) & 0xFF);
-    if (eb == 0) return -127;  // zero or subnormal: 6 * 2^-127 covers it
-    // amax = 1.f * 2^(eb-127): 6 * 2^(eb-130) = 0.75 * 2^(eb-127) suffices when
-    // the significand is at most 1.5
-    const int e = (b & 0x7FFFFFu) <= 0x400000u ? eb - 129 : eb - 128;
-    return max(-127, min(127, e));
-}
 
 // One warp per (token, 32-element block): PIECES residual E2M1 pieces with
 // their E8M0 exponents, written into the stage images the MMA streams.  Piece
@@ -92,27 +69,32 @@ __global__ void __launch_bounds__(256) k_mx_pieces(const PassHdr* __restrict__ h
     const int M = min(use_head ? hdr->head_rows : hdr->rows, mcap);
     const int k = kb * 32 + lane;
     float r = (m < M && k < K) ? x[(size_t)m * ldx + k] : 0.f;
-    const int s = kb / (STAGE_K / 32), kbl = kb % (STAGE_K / 32);
-    uint8_t* img = bimg + (size_t)s * N * 128;
-    uint8_t* sf = sfb + (size_t)s * SF_STAGE;
-    const uint32_t byte = (uint32_t)(kbl * 16 + (lane >> 1));
-#pragma unroll
-    for (int p = 0; p < PIECES; ++p) {
-        const int e = piece_exponent(warp_max(fabsf(r)));
-        const float sc = __fmul_rn(fabsf(r), pow2i(-e));  // exact power-of-two scaling
-        // nearest level, ties to the even code (python/quantize_mxfp4.py:32-34)
-        uint32_t c = (sc > 0.25f) + (sc > 0.75f) + (sc > 1.25f) + (sc > 1.75f) + (sc > 2.5f) +
-                     (sc > 3.5f) + (sc > 5.0f);
-        c += (c == 1 && sc == 0.75f) || (c == 3 && sc == 1.75f) || (c == 5 && sc == 3.5f);
-        const float level = __fmul_rn(__uint_as_float(c << 22), 0x1p126f);
-        const float q = __fmul_rn(level, pow2i(e));
-        const uint32_t code = (c && r < 0.f) ? (c | 8u) : c;
-        r = r < 0.f ? __fadd_rn(r, q) : __fsub_rn(r, q);  // exact (Sterbenz)
-        const uint32_t other = __shfl_down_sync(0xffffffffu, code, 1);
-        const uint32_t n = (uint32_t)(m * PIECES + p);
-        if ((lane & 1) == 0) img[swz128(n, byte)] = (uint8_t)(code | (other << 4));
-        if (lane == 0) sf[sf_offset(n, (uint32_t)kbl)] = (uint8_t)(e + 127);
-    }
+    mx::emit_pieces(r, lane, m, kb * 32, N, bimg, sfb);
+}
+
+// Pieces of x * w for a projection that follows an RMSNorm, plus the
+// per-tile sums of squares of x the projection's epilogue turns into the
+// row's RMS: one CTA of 128 threads per (128-element tile, row).  Used where
+// no projection epilogue produced them (after the embedding).
+__global__ void __launch_bounds__(128) k_norm_pieces(const PassHdr* __restrict__ hdr, int mcap,
+                                                     const float* __restrict__ x, int ldx,
+                                                     const uint16_t* __restrict__ w, int width, int N,
+                                                     uint8_t* __restrict__ bout, uint8_t* __restrict__ sfout,
+                                                     float* __restrict__ part) {
+    __shared__ float red[4];
+    ptx::grid_dependency_wait();
+    ptx::launch_dependents();
+    const int t = blockIdx.x, m = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int M = min(hdr->rows, mcap);
+    const int k = t * 128 + threadIdx.x;
+    const float v = (m < M && k < width) ? x[(size_t)m * ldx + k] : 0.f;
+    const float wk = k < width ? bf16f(w[k]) : 0.f;
+    mx::emit_pieces(__fmul_rn(v, wk), lane, m, t * 128 + warp * 32, N, bout, sfout);
+    const float ss = warp_sum(__fmul_rn(v, v));
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) part[t * MX_PART_STRIDE + m] = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
 }
 
 // ---------------------------------------------------------------------------
@@ -133,48 +115,81 @@ struct MxArgs {
     float* ws;             // [T][ksplit][mcap][128]
     int* tickets;          // [T]
     int* err;
+    // Fused epilogue (decode pass).  Input RMSNorm: the projection reads the
+    // pieces of x*w and divides its outputs by the row's RMS, computed from
+    // per-tile sums of squares (part_in, part_tiles tiles of MX_MAXTOK).
+    const float* part_in;
+    int part_tiles, norm_width;
+    // Output pieces for the next projection (bout/sfout, bN columns) and,
+    // after a residual add, the sums of squares of the new x (part_out) and
+    // the next RMSNorm weight (next_w) the pieces are scaled by.
+    uint8_t* bout;
+    uint8_t* sfout;
+    int bN;
+    float* part_out;
+    const uint16_t* next_w;
+    // q|k|v epilogue: QK-RMSNorm, RoPE, K/V appended to the paged cache.
+    int q_heads, kv_heads;
+    const uint16_t* qn;
+    const uint16_t* kn;
+    const float2* rope;
+    const RowDesc* rows;
+    const int32_t* const* page_table;
+    KvView kv;
 };
 
-enum : int { MX_STORE = 0, MX_ADD = 1, MX_SWIGLU = 2 };
+enum : int { MX_STORE = 0, MX_ADD = 1, MX_SWIGLU = 2, MX_QKV = 3 };
 constexpr int MX_MAXSTAGES = 6;
 constexpr int MX_MAXTOK = 16;       // tokens per pass on this path: N = 8 * tokens <= 128
 constexpr int MX_THREADS = 192;     // warp 0 loads, warp 1 MMAs, warps 2-5 epilogue
+static_assert(MX_PART_STRIDE >= MX_MAXTOK, "partials hold every row of a pass");
+static_assert(MX_MAXTOK == 16, "emit_pieces_all takes 16 rows");
 
 __host__ __device__ constexpr int mx_stage_bytes(int N) { return A_STAGE + N * 128 + 2 * SF_STAGE; }
 
 // The four epilogue warps synchronise among themselves only.
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// Units of work: (tile, K slice), unit u = t * ksplit + kc, handed to the
-// persistent CTAs round robin.
-__device__ __forceinline__ void unit_range(const MxArgs& a, int u, int& t, int& s0, int& s1) {
-    t = u / a.ksplit;
-    const int kc = u - t * a.ksplit;
-    s0 = (int)((long long)kc * a.S / a.ksplit);
-    s1 = (int)((long long)(kc + 1) * a.S / a.ksplit);
-}
-
-// Persistent, warp-specialised projection.  Warp 0 lane 0 streams weight
-// stages through a ring of shared-memory slots (the first slots are issued
-// before the grid-dependency wait: weights never depend on the previous
-// kernel); warp 1 lane 0 issues the MMAs into one of two TMEM accumulators;
-// warps 2-5 drain the other accumulator, so one unit's epilogue overlaps the
-// next unit's streaming.  Warp w reads TMEM lanes 32*(w%4).., weight rows
-// 32*(w%4).. of the tile.
+// Persistent, warp-specialised projection.  Split-K runs inside a thread-
+// block cluster: the `ksplit` CTAs of a cluster take the same tiles (tile
+// cid, cid + clusters, ...), CTA rank kc streaming K slice kc of each.
+// Warp 0 lane 0 streams weight stages through a ring of shared-memory slots
+// (the first slots are issued before the grid-dependency wait: weights never
+// depend on the previous kernel); warp 1 lane 0 issues the MMAs into one of
+// two TMEM accumulators; warps 2-5 drain the other accumulator, so one tile's
+// epilogue overlaps the next tile's streaming.  Warp w reads TMEM lanes
+// 32*(w%4).., weight rows 32*(w%4).. of the tile.
+//
+// Split-K reduction through distributed shared memory: ranks 1.. write their
+// partial tile into their own shared-memory slot and arrive on the leader's
+// red_full barrier; the leader (rank 0) adds the slots in rank order (a
+// fixed order, so results do not depend on timing or on the row count), then
+// frees them (slot_free) and runs the epilogue.
 template <int EPI>
 __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     __shared__ uint64_t full[MX_MAXSTAGES], empty[MX_MAXSTAGES], tfull[2], tempty[2];
+    __shared__ uint64_t red_full, slot_free;
     __shared__ uint32_t tmem_base_s;
-    __shared__ int last_s;
-    __shared__ float up_s[MX_MAXTOK][64];
+    __shared__ float red_s[4][MX_MAXTOK];    // per-warp sums of squares
+    __shared__ float sz_s[MX_MAXTOK];        // 1 / input RMS per row
+    __shared__ float qk_s[MX_MAXTOK];        // 1 / RMS of this head, per row
+    __shared__ int kvpos_s[MX_MAXTOK];       // q|k|v: position of each row, -1 if invalid
+    __shared__ int kvpage_s[MX_MAXTOK];      //   and its cache page
 
     const int N = a.N, ST = a.stages, NB = a.nbuf;
     const int sbytes = mx_stage_bytes(N);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int units = a.T * a.ksplit;
-    const int G = gridDim.x;
+    const int ks = a.ksplit;
+    const int kc = ks > 1 ? (int)ptx::cluster_ctarank() : 0;
+    const int cid = blockIdx.x / ks, NC = gridDim.x / ks;
+    const int s0 = (int)((long long)kc * a.S / ks), s1 = (int)((long long)(kc + 1) * a.S / ks);
+    // this CTA's split-K partial [mcap][128]; the leader never publishes its
+    // own, so there the region is epilogue scratch (SwiGLU up halves, RoPE
+    // partners: xs[m][0..63])
+    float* slot = (float*)(smem + ST * sbytes);
+    float(*xs)[64] = (float(*)[64])slot;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < ST; ++i) {
@@ -185,6 +200,8 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
             ptx::mbar_init(&tfull[i], 1);
             ptx::mbar_init(&tempty[i], 4);
         }
+        ptx::mbar_init(&red_full, 4 * (ks > 1 ? ks - 1 : 1));  // four warps of every other rank
+        ptx::mbar_init(&slot_free, 4);                         // the leader's four warps
         ptx::fence_barrier_init();
     }
     if (warp == 1) {
@@ -194,6 +211,10 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
+    if (ks > 1) {  // every CTA's barriers are initialised before any remote arrive
+        ptx::cluster_arrive();
+        ptx::cluster_wait();
+    }
     const uint32_t tmem = tmem_base_s;
     bool ok = true;
 
@@ -204,9 +225,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
             int pre = 0;
             {
                 int g = 0;
-                for (int u = blockIdx.x; u < units && g < ST; u += G) {
-                    int t, s0, s1;
-                    unit_range(a, u, t, s0, s1);
+                for (int t = cid; t < a.T && g < ST; t += NC) {
                     for (int s = s0; s < s1 && g < ST; ++s, ++g) {
                         uint8_t* base = smem + g * sbytes;
                         ptx::mbar_arrive_expect_tx(&full[g], (uint32_t)sbytes);
@@ -219,9 +238,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
             }
             ptx::grid_dependency_wait();
             int g = 0;
-            for (int u = blockIdx.x; u < units && ok; u += G) {
-                int t, s0, s1;
-                unit_range(a, u, t, s0, s1);
+            for (int t = cid; t < a.T && ok; t += NC) {
                 for (int s = s0; s < s1; ++s, ++g) {
                     const int slot = g % ST;
                     uint8_t* base = smem + slot * sbytes;
@@ -247,9 +264,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
         ptx::grid_dependency_wait();
         if (lane == 0) {
             int g = 0, j = 0;
-            for (int u = blockIdx.x; u < units && ok; u += G, ++j) {
-                int t, s0, s1;
-                unit_range(a, u, t, s0, s1);
+            for (int t = cid; t < a.T && ok; t += NC, ++j) {
                 const int buf = NB == 2 ? (j & 1) : 0;
                 const int use = NB == 2 ? (j >> 1) : j;  // earlier uses of this accumulator
                 if (use > 0 && !ptx::mbar_wait(&tempty[buf], (use - 1) & 1, WAIT_LIMIT)) {
@@ -295,13 +310,55 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const int M = min(a.use_head ? a.hdr->head_rows : a.hdr->rows, a.mcap);
-        const bool lead = threadIdx.x == 64;
+        if (a.part_in) {
+            // RMS of each input row from the per-tile sums of squares, in tile order
+            if (row < a.mcap) {
+                float ss = 0.f;
+                for (int i = 0; i < a.part_tiles; ++i) ss = __fadd_rn(ss, a.part_in[i * MX_PART_STRIDE + row]);
+                sz_s[row] = __frcp_rn(sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.norm_width), 1e-6f)));
+            }
+        }
+        // q|k|v: each row's position, cache page and RoPE factors, the same
+        // for every head: fetched once, while the first tile's MMAs run
+        float2 rope_cs[MX_MAXTOK];
+        if (EPI == MX_QKV) {
+            if (row < a.mcap) {
+                int pos = -1, page = -1;
+                if (row < M) {
+                    const RowDesc rd = a.rows[row];
+                    if (rd.pos >= 0 && rd.pos < a.kv.max_pos && (unsigned)rd.seq < (unsigned)MAX_SEQS) {
+                        pos = rd.pos;
+                        page = a.page_table[rd.seq][rd.pos / PAGE];
+                    } else {
+                        atomicOr(a.kv.err, 2);
+                    }
+                }
+                kvpos_s[row] = pos;
+                kvpage_s[row] = page;
+            }
+            epi_bar();
+#pragma unroll
+            for (int m = 0; m < MX_MAXTOK; ++m) {
+                const int pos = m < a.mcap ? kvpos_s[m] : -1;
+                rope_cs[m] = pos >= 0 ? a.rope[(size_t)pos * HALF + (row & 63)] : make_float2(1.f, 0.f);
+            }
+        }
+        if (a.part_in) epi_bar();
         int j = 0;
-        for (int u = blockIdx.x; u < units; u += G, ++j) {
-            int t, s0, s1;
-            unit_range(a, u, t, s0, s1);
+        for (int t = cid; t < a.T; t += NC, ++j) {
             const int buf = NB == 2 ? (j & 1) : 0;
             const int use = NB == 2 ? (j >> 1) : j;
+            // the residual this tile adds to: only this tile's epilogue writes
+            // it, so load it while the MMAs run
+            float xold[MX_MAXTOK];
+            float wnext = 1.f;
+            if (EPI == MX_ADD) {
+                const int gr = t * TILE_ROWS + row;
+#pragma unroll
+                for (int m = 0; m < MX_MAXTOK; ++m)
+                    xold[m] = (m < M && gr < a.out_rows) ? __ldcg(a.y + (size_t)m * a.ldy + gr) : 0.f;
+                if (a.next_w) wnext = gr < a.out_rows ? bf16f(a.next_w[gr]) : 0.f;
+            }
             if (!ptx::mbar_wait(&tfull[buf], use & 1, WAIT_LIMIT)) ok = false;
             ptx::tc_fence_after();
             float val[MX_MAXTOK];
@@ -327,60 +384,175 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&tempty[buf]);
 
-            if (a.ksplit > 1) {
-                const int kc = u - t * a.ksplit;
-                float* ws = a.ws + (((size_t)t * a.ksplit + kc) * a.mcap) * 128;
+            if (ks > 1) {
+                if (kc > 0) {
+                    // publish this K slice's partial to the leader
+                    if (j > 0 && !ptx::mbar_wait_cluster(&slot_free, (j - 1) & 1, WAIT_LIMIT)) ok = false;
 #pragma unroll
-                for (int m = 0; m < MX_MAXTOK; ++m)
-                    if (m < a.mcap) __stcg(ws + (size_t)m * 128 + row, val[m]);
-                __threadfence();
-                epi_bar();
-                if (lead) {
-                    const int ticket = atomicAdd(&a.tickets[t], 1);
-                    last_s = ticket == a.ksplit - 1;
-                    if (last_s) a.tickets[t] = 0;  // every slice arrived: ready for the next launch
+                    for (int m = 0; m < MX_MAXTOK; ++m)
+                        if (m < a.mcap) slot[m * 128 + row] = val[m];
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive_remote(ptx::mapa(ptx::smem_u32(&red_full), 0));
+                    continue;
                 }
-                epi_bar();
-                if (!last_s) continue;
-                __threadfence();
-                const float* w0 = a.ws + ((size_t)t * a.ksplit * a.mcap) * 128;
-#pragma unroll
-                for (int m = 0; m < MX_MAXTOK; ++m)
-                    if (m < a.mcap) val[m] = __ldcg(w0 + (size_t)m * 128 + row);
-                for (int k = 1; k < a.ksplit; ++k) {
+                if (!ptx::mbar_wait_cluster(&red_full, j & 1, WAIT_LIMIT)) ok = false;
+                const uint32_t mine = ptx::smem_u32(slot) + (uint32_t)row * 4;
+                for (int r = 1; r < ks; ++r) {
+                    const uint32_t base = ptx::mapa(mine, (uint32_t)r);
                     float part[MX_MAXTOK];
 #pragma unroll
                     for (int m = 0; m < MX_MAXTOK; ++m)
-                        part[m] = m < a.mcap ? __ldcg(w0 + ((size_t)k * a.mcap + m) * 128 + row) : 0.f;
+                        part[m] = m < a.mcap ? ptx::ld_shared_cluster(base + (uint32_t)m * 512) : 0.f;
 #pragma unroll
                     for (int m = 0; m < MX_MAXTOK; ++m) val[m] = __fadd_rn(val[m], part[m]);
                 }
+                __syncwarp();
+                if (lane == 0)
+                    for (int r = 1; r < ks; ++r) ptx::mbar_arrive_remote(ptx::mapa(ptx::smem_u32(&slot_free), r));
+            }
+            if (a.part_in) {  // input RMSNorm: scale by 1 / the row's RMS (lib.rs:268-290)
+#pragma unroll
+                for (int m = 0; m < MX_MAXTOK; ++m)
+                    if (m < a.mcap) val[m] = __fmul_rn(val[m], sz_s[m]);
             }
             if (EPI == MX_SWIGLU) {
                 // tile rows 0..63: gate rows 64t.., rows 64..127: the matching up rows
                 if (row >= 64) {
 #pragma unroll
                     for (int m = 0; m < MX_MAXTOK; ++m)
-                        if (m < a.mcap) up_s[m][row - 64] = val[m];
+                        if (m < a.mcap) xs[m][row - 64] = val[m];
                 }
                 epi_bar();
-                if (row < 64 && t * 64 + row < a.out_rows) {
+                if (row < 64) {
+                    const int k = t * 64 + row;
+#pragma unroll
+                    for (int m = 0; m < MX_MAXTOK; ++m) {
+                        float act = 0.f;
+                        if (m < M && k < a.out_rows) {
+                            const float gt = val[m], up = xs[m][row];
+                            act = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up);
+                            if (a.y) a.y[(size_t)m * a.ldy + k] = act;
+                        }
+                        val[m] = act;
+                    }
+                }
+                if (a.bout) {  // the tile's 64 activations: two 32-blocks of the down input
+                    epi_bar();  // every up value has been read
+                    if (row < 64) {
+#pragma unroll
+                        for (int m = 0; m < MX_MAXTOK; ++m)
+                            if (m < a.mcap) xs[m][row] = val[m];
+                    }
+                    epi_bar();
+                    mx::emit_pieces_smem(&xs[0][0], 64, 2, 0, a.mcap, a.mcap, row, 128, t * 64, a.bN, a.bout,
+                                         a.sfout);
+                }
+                epi_bar();  // xs is reused by the next unit
+            } else if (EPI == MX_QKV) {
+                // tile t is head t: q heads, then k heads, then v heads (lib.rs:363-396)
+                const int Hq = a.q_heads, Hkv = a.kv_heads;
+                const bool is_q = t < Hq, is_k = !is_q && t < Hq + Hkv;
+                if (is_q || is_k) {
+                    const float w = bf16f((is_q ? a.qn : a.kn)[row]);
+#pragma unroll
+                    for (int m = 0; m < MX_MAXTOK; ++m) {
+                        const float ss = warp_sum(__fmul_rn(val[m], val[m]));
+                        if (lane == 0) red_s[quarter][m] = ss;
+                    }
+                    epi_bar();
+                    if (row < a.mcap) {
+                        const float ss = __fadd_rn(__fadd_rn(red_s[0][row], red_s[1][row]),
+                                                   __fadd_rn(red_s[2][row], red_s[3][row]));
+                        qk_s[row] = __frcp_rn(sqrtf(__fadd_rn(__fdiv_rn(ss, 128.0f), 1e-6f)));
+                    }
+                    epi_bar();
+#pragma unroll
+                    for (int m = 0; m < MX_MAXTOK; ++m)
+                        if (m < a.mcap) val[m] = __fmul_rn(__fmul_rn(val[m], qk_s[m]), w);
+                    // RoPE pairs (i, i + 64) sit in rows i and i + 64: swap halves
+                    // through shared memory, low half first
+                    float other[MX_MAXTOK];
+                    if (row < 64) {
+#pragma unroll
+                        for (int m = 0; m < MX_MAXTOK; ++m)
+                            if (m < a.mcap) xs[m][row] = val[m];
+                    }
+                    epi_bar();
+                    if (row >= 64) {
+#pragma unroll
+                        for (int m = 0; m < MX_MAXTOK; ++m) other[m] = m < a.mcap ? xs[m][row - 64] : 0.f;
+                    }
+                    epi_bar();
+                    if (row >= 64) {
+#pragma unroll
+                        for (int m = 0; m < MX_MAXTOK; ++m)
+                            if (m < a.mcap) xs[m][row - 64] = val[m];
+                    }
+                    epi_bar();
+                    if (row < 64) {
+#pragma unroll
+                        for (int m = 0; m < MX_MAXTOK; ++m) other[m] = m < a.mcap ? xs[m][row] : 0.f;
+                    }
+#pragma unroll
+                    for (int m = 0; m < MX_MAXTOK; ++m) {
+                        // lib.rs:306-313: out[i] = a cos - b sin; out[i+64] = b cos + a sin
+                        const float2 r = rope_cs[m];
+                        const float v = row < 64 ? __fsub_rn(__fmul_rn(val[m], r.x), __fmul_rn(other[m], r.y))
+                                                 : __fadd_rn(__fmul_rn(val[m], r.x), __fmul_rn(other[m], r.y));
+                        if (m < M) val[m] = v;
+                    }
+                    epi_bar();  // xs and red_s are reused by the next unit
+                }
+                if (is_q) {
+#pragma unroll
+                    for (int m = 0; m < MX_MAXTOK; ++m)
+                        if (m < M) a.y[(size_t)m * a.ldy + t * TILE_ROWS + row] = val[m];
+                } else {
+                    const int kvh = is_k ? t - Hq : t - Hq - Hkv;
+                    void* dst = is_k ? a.kv.k : a.kv.v;
 #pragma unroll
                     for (int m = 0; m < MX_MAXTOK; ++m) {
                         if (m >= M) continue;
-                        const float gt = val[m], up = up_s[m][row];
-                        a.y[(size_t)m * a.ldy + t * 64 + row] =
-                            __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up);
+                        const int pos = kvpos_s[m], page = kvpage_s[m];
+                        if (pos < 0 || !page_ok(a.kv, page)) continue;  // bad positions were flagged
+                        const size_t idx = kv_index(page, kvh, pos % PAGE, a.kv.kv_heads) + row;
+                        if (a.kv.f32) ((float*)dst)[idx] = val[m];
+                        else ((uint16_t*)dst)[idx] = f2bf16(val[m]);
                     }
                 }
-                epi_bar();  // up_s is reused by the next unit
-            } else if (t * TILE_ROWS + row < a.out_rows) {
+            } else {
+                const int gr = t * TILE_ROWS + row;
+                const bool valid = gr < a.out_rows;
 #pragma unroll
                 for (int m = 0; m < MX_MAXTOK; ++m) {
-                    if (m >= M) continue;
-                    float* out = a.y + (size_t)m * a.ldy + t * TILE_ROWS + row;
-                    if (EPI == MX_ADD) *out = __fadd_rn(*out, val[m]);
-                    else *out = val[m];
+                    if (m < M && valid) {
+                        const float v = EPI == MX_ADD ? __fadd_rn(xold[m], val[m]) : val[m];
+                        a.y[(size_t)m * a.ldy + gr] = v;
+                        val[m] = v;
+                    } else {
+                        val[m] = 0.f;
+                    }
+                }
+                if (a.bout) {  // the next projection's input: pieces of x * w
+#pragma unroll
+                    for (int m = 0; m < MX_MAXTOK; ++m)
+                        if (m < a.mcap) slot[m * 128 + row] = __fmul_rn(val[m], wnext);
+                    epi_bar();
+                    mx::emit_pieces_smem(slot, 128, 4, 0, a.mcap, a.mcap, row, 128, t * TILE_ROWS, a.bN, a.bout,
+                                         a.sfout);
+                    epi_bar();  // the staging area is reused by the next tile
+                }
+                if (a.part_out) {  // sum of squares of this tile's 128 outputs, per row
+#pragma unroll
+                    for (int m = 0; m < MX_MAXTOK; ++m) {
+                        const float ss = warp_sum(__fmul_rn(val[m], val[m]));
+                        if (lane == 0) red_s[quarter][m] = ss;
+                    }
+                    epi_bar();
+                    if (row < a.mcap)
+                        a.part_out[t * MX_PART_STRIDE + row] = __fadd_rn(__fadd_rn(red_s[0][row], red_s[1][row]),
+                                                                    __fadd_rn(red_s[2][row], red_s[3][row]));
+                    epi_bar();
                 }
             }
         }
@@ -388,6 +560,10 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
     ptx::launch_dependents();
     ptx::tc_fence_before();
     __syncthreads();
+    if (ks > 1) {  // no CTA leaves while a peer may still read its slot
+        ptx::cluster_arrive();
+        ptx::cluster_wait();
+    }
     if (warp == 1) ptx::tmem_dealloc(tmem, TMEM_COLS);
     if (!ok && lane == 0) atomicOr(a.err, 4);  // a bounded wait gave up
 }
@@ -450,17 +626,32 @@ __global__ void k_mx_tile(TileSrc src, int swiglu, int K, int T, int S, uint8_t*
     }
 }
 
-// K slices per tile for one persistent CTA per SM: the busiest CTA streams
-// ceil(T*ks / sms) units of ceil(S/ks) stages; a unit also costs about one
-// stage of epilogue and a split costs a partial-sum round trip.  The choice
-// depends only on the matrix shape, never on the token count.
-int mx_ksplit(int T, int S, int sms) {
+constexpr int MX_MAXCLUSTER = 8;  // portable cluster size: split-K at most 8 ways
+constexpr int MX_MAXDEV = 64;
+// Clusters of each size that fit at one CTA per SM, per device (the GPU's
+// processing clusters decide how many SMs a cluster size can use).
+int g_clusters[MX_MAXDEV][MX_MAXCLUSTER + 1];
+
+int mx_clusters(int ks) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int n = (dev >= 0 && dev < MX_MAXDEV) ? g_clusters[dev][ks] : 0;
+    return n > 0 ? n : 1;
+}
+
+// K slices per tile: a cluster of ks CTAs streams ceil(T / clusters) tiles
+// of ceil(S / ks) stages each; a tile also costs about one stage of
+// epilogue, and a split about half a stage for the reduction through
+// distributed shared memory.  The choice depends only on the matrix shape,
+// never on the token count.
+int mx_ksplit(int T, int S) {
     int best = 1;
     double best_cost = 1e30;
-    for (int ks = 1; ks <= S; ++ks) {
-        const int per_cta = (T * ks + sms - 1) / sms;
+    for (int ks = 1; ks <= std::min(S, MX_MAXCLUSTER); ++ks) {
+        const int nc = mx_clusters(ks);
+        const int per_cluster = (T + nc - 1) / nc;
         const int per_unit = (S + ks - 1) / ks;
-        const double cost = (double)per_cta * (per_unit + 1.0) + (ks > 1 ? 1.0 : 0.0);
+        const double cost = (double)per_cluster * (per_unit + 1.0) + (ks > 1 ? 0.5 : 0.0);
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
             best = ks;
@@ -477,18 +668,59 @@ void mx_shape(int N, int* stages, int* nbuf) {
     *stages = N <= 64 ? 4 : 3;
 }
 
+// Stages, then the split-K slot (N / 8 rows x 128 f32), then alignment slack.
 size_t mx_smem(int N) {
     int st, nb;
     mx_shape(N, &st, &nb);
-    return (size_t)st * mx_stage_bytes(N) + 1024;  // + alignment slack
+    return (size_t)st * mx_stage_bytes(N) + (size_t)N * 64 + 1024;
 }
+
+constexpr int MX_PROBE_SMEM = 120 * 1024;  // more than half an SM: one CTA per SM
 
 template <int EPI>
 jl_status configure_mx() {
     JL_CUDA(cudaFuncSetAttribute(k_mx_gemv<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)std::max(mx_smem(64), mx_smem(8 * MX_MAXTOK))));
+                                 (int)std::max<size_t>(MX_PROBE_SMEM, std::max(mx_smem(64), mx_smem(8 * MX_MAXTOK)))));
     JL_CUDA(cudaFuncSetAttribute(k_mx_gemv<EPI>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     return JL_OK;
+}
+
+template <int EPI>
+jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream) {
+    const int nc = std::min(a.T, a.ksplit > 1 ? mx_clusters(a.ksplit) : sms);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nc * a.ksplit);
+    cfg.blockDim = dim3(MX_THREADS);
+    cfg.dynamicSmemBytes = mx_smem(a.N);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int n = 1;
+    if (a.ksplit > 1) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = (unsigned)a.ksplit;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        n = 2;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    JL_CUDA(cudaLaunchKernelEx(&cfg, k_mx_gemv<EPI>, a));
+    return JL_OK;
+}
+
+jl_status launch_gemv(int epi, const MxArgs& a, int sms, cudaStream_t stream) {
+    if (a.ksplit < 1 || a.ksplit > MX_MAXCLUSTER) {
+        set_error("tensor-core projection: split-K %d outside 1..%d", a.ksplit, MX_MAXCLUSTER);
+        return JL_ERR_INVALID_ARG;
+    }
+    switch (epi) {
+        case MX_ADD: return launch_gemv_t<MX_ADD>(a, sms, stream);
+        case MX_SWIGLU: return launch_gemv_t<MX_SWIGLU>(a, sms, stream);
+        case MX_QKV: return launch_gemv_t<MX_QKV>(a, sms, stream);
+        default: return launch_gemv_t<MX_STORE>(a, sms, stream);
+    }
 }
 
 }  // namespace
@@ -497,6 +729,29 @@ jl_status mx_configure() {
     JL_TRY(configure_mx<MX_STORE>());
     JL_TRY(configure_mx<MX_ADD>());
     JL_TRY(configure_mx<MX_SWIGLU>());
+    JL_TRY(configure_mx<MX_QKV>());
+    int dev = 0, sms = 0;
+    JL_CUDA(cudaGetDevice(&dev));
+    JL_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    if (dev >= 0 && dev < MX_MAXDEV) {
+        g_clusters[dev][1] = sms;
+        for (int ks = 2; ks <= MX_MAXCLUSTER; ++ks) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(ks * sms);
+            cfg.blockDim = dim3(MX_THREADS);
+            cfg.dynamicSmemBytes = MX_PROBE_SMEM;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = (unsigned)ks;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            JL_CUDA(cudaOccupancyMaxActiveClusters(&n, k_mx_gemv<MX_STORE>, &cfg));
+            g_clusters[dev][ks] = n;
+        }
+    }
     return JL_OK;
 }
 
@@ -533,7 +788,8 @@ jl_status mx_build(const Mat* const* mats, int nmats, bool swiglu, uint8_t* dst,
     p.out_rows = out_rows;
     p.a = dst;
     p.sfa = dst + (size_t)p.T * p.S * A_STAGE;
-    p.ksplit = mx_ksplit(p.T, p.S, sms);
+    p.ksplit = mx_ksplit(p.T, p.S);
+    (void)sms;
     const size_t chunks = (size_t)p.T * p.S * TILE_ROWS * 8;
     const int grid = (int)std::min<size_t>((chunks + 255) / 256, (size_t)sms * 8);
     k_mx_tile<<<grid, 256, 0, stream>>>(src, swiglu ? 1 : 0, K, p.T, p.S, (uint8_t*)p.a,
@@ -557,7 +813,7 @@ jl_status mx_project(const PassCtx& c, const MxProj& p, int epi, int use_head, c
     JL_TRY(launch_pdl(k_mx_pieces, dim3((items + 7) / 8), dim3(256), 0, c.stream,
                       (const PassHdr*)m->pass.hdr, use_head, mcap, x, ldx, p.K, p.S, N, m->mx.bimg,
                       m->mx.sfb));
-    MxArgs a;
+    MxArgs a = {};
     a.a = p.a;
     a.sfa = p.sfa;
     a.b = m->mx.bimg;
@@ -576,11 +832,67 @@ jl_status mx_project(const PassCtx& c, const MxProj& p, int epi, int use_head, c
     a.ws = m->mx.ws;
     a.tickets = m->mx.tickets;
     a.err = m->counters;
-    const dim3 grid(std::min(p.T * p.ksplit, m->sms));
-    const size_t smem = mx_smem(N);
-    if (epi == MX_ADD) return launch_pdl(k_mx_gemv<MX_ADD>, grid, dim3(MX_THREADS), smem, c.stream, a);
-    if (epi == MX_SWIGLU) return launch_pdl(k_mx_gemv<MX_SWIGLU>, grid, dim3(MX_THREADS), smem, c.stream, a);
-    return launch_pdl(k_mx_gemv<MX_STORE>, grid, dim3(MX_THREADS), smem, c.stream, a);
+    return launch_gemv(epi, a, m->sms, c.stream);
+}
+
+jl_status mx_norm_pieces(const PassCtx& c, const float* x, int ldx, const uint16_t* w, int width,
+                         uint8_t* bout, uint8_t* sfout, float* part) {
+    const int mcap = c.rows_cap;
+    if (mcap < 1 || mcap > MX_MAXTOK || width % STAGE_K) {
+        set_error("norm pieces take 1..%d rows and a width that is a multiple of %d", MX_MAXTOK, STAGE_K);
+        return JL_ERR_INVALID_ARG;
+    }
+    return launch_pdl(k_norm_pieces, dim3(width / 128, mcap), dim3(128), 0, c.stream,
+                      (const PassHdr*)c.m->pass.hdr, mcap, x, ldx, w, width, PIECES * mcap, bout, sfout, part);
+}
+
+jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxFuse& f, float* y,
+                           int ldy) {
+    const jl_model* m = c.m;
+    const int mcap = c.rows_cap;
+    if (mcap < 1 || mcap > MX_MAXTOK) {
+        set_error("tensor-core projection takes 1..%d rows per pass, got %d", MX_MAXTOK, mcap);
+        return JL_ERR_INVALID_ARG;
+    }
+    const int N = PIECES * mcap;
+    MxArgs a = {};
+    a.a = p.a;
+    a.sfa = p.sfa;
+    a.b = f.b;
+    a.sfb = f.sfb;
+    a.T = p.T;
+    a.S = p.S;
+    a.ksplit = p.ksplit;
+    a.N = N;
+    a.mcap = mcap;
+    mx_shape(N, &a.stages, &a.nbuf);
+    a.hdr = m->pass.hdr;
+    a.use_head = 0;
+    a.y = y;
+    a.ldy = ldy;
+    a.out_rows = p.out_rows;
+    a.ws = m->mx.ws;
+    a.tickets = m->mx.tickets;
+    a.err = m->counters;
+    a.part_in = f.part_in;
+    a.part_tiles = f.part_tiles;
+    a.norm_width = f.norm_width;
+    a.bout = f.bout;
+    a.sfout = f.sfout;
+    a.bN = N;
+    a.part_out = f.part_out;
+    a.next_w = f.next_w;
+    if (epi == MX_QKV) {
+        a.q_heads = m->q_heads;
+        a.kv_heads = m->kv_heads;
+        a.qn = f.qn;
+        a.kn = f.kn;
+        a.rope = (const float2*)m->rope;
+        a.rows = m->pass.row;
+        a.page_table = m->pass.page_table;
+        a.kv = kv_view(m, f.layer);
+    }
+    return launch_gemv(epi, a, m->sms, c.stream);
 }
 
 MxScratchPlan mx_scratch_plan(const MxProj& p, int mcap) {
@@ -610,7 +922,7 @@ jl_status mx_project_with(const MxProj& p, int epi, const PassHdr* hdr, int mcap
     const int items = mcap * p.S * (STAGE_K / 32);
     JL_TRY(launch_pdl(k_mx_pieces, dim3((items + 7) / 8), dim3(256), 0, stream, hdr, 0, mcap, x, ldx,
                       p.K, p.S, N, bimg, sfb));
-    MxArgs a;
+    MxArgs a = {};
     a.a = p.a;
     a.sfa = p.sfa;
     a.b = bimg;
@@ -629,11 +941,7 @@ jl_status mx_project_with(const MxProj& p, int epi, const PassHdr* hdr, int mcap
     a.ws = ws;
     a.tickets = tickets;
     a.err = err;
-    const dim3 grid(std::min(p.T * p.ksplit, sms));
-    const size_t smem = mx_smem(N);
-    if (epi == MX_ADD) return launch_pdl(k_mx_gemv<MX_ADD>, grid, dim3(MX_THREADS), smem, stream, a);
-    if (epi == MX_SWIGLU) return launch_pdl(k_mx_gemv<MX_SWIGLU>, grid, dim3(MX_THREADS), smem, stream, a);
-    return launch_pdl(k_mx_gemv<MX_STORE>, grid, dim3(MX_THREADS), smem, stream, a);
+    return launch_gemv(epi, a, sms, stream);
 }
 
 }  // namespace jl
