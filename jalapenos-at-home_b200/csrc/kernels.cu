@@ -546,6 +546,179 @@ __global__ void __launch_bounds__(128) k_attention(PassBuf pb, const float* __re
     }
 }
 
+// Decode attention (lib.rs:401-441) for passes of at most a few rows: one CTA
+// per (KV head, row), one warp per query head of the GQA group, sharing the
+// head's K and V.  The cache keeps a (page, KV head) as one contiguous
+// PAGE x 128 block, so one thread copies a window of ATT_WIN pages of K and V
+// into shared memory with bulk copies and a single (bounded) mbarrier wait.
+// Positions then go 32 at a time: lane j scores position c0 + j, reading its
+// K row with the 16-byte chunks rotated by j (no bank conflicts); the warp
+// updates the running max and sum, and lanes switch to owning 4 of the 128
+// dimensions to accumulate the 32 V rows.  The output row also goes out as
+// the o projection's input pieces; rows past the pass's row count get zero
+// pieces.
+constexpr int ATT_WIN = 2;              // pages per shared-memory window
+constexpr uint32_t ATT_WAIT = 1u << 22;  // polls before the page copy reports failure
+
+__host__ __device__ constexpr int att_page_bytes(int f32) { return PAGE * HEAD * (f32 ? 4 : 2); }
+__host__ __device__ constexpr int att_smem(int f32) { return 2 * ATT_WIN * att_page_bytes(f32); }
+
+template <int F32>
+__global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __restrict__ qkv, int ld,
+                                                     int group, KvView kv, float* __restrict__ out,
+                                                     int out_ld, uint8_t* __restrict__ bout,
+                                                     uint8_t* __restrict__ sfout, int bN) {
+    static_assert(PAGE % 32 == 0, "chunks of 32 positions stay inside a page");
+    constexpr int PB = att_page_bytes(F32);
+    extern __shared__ __align__(128) uint8_t kvs[];  // [ATT_WIN][K|V][PAGE][HEAD]
+    __shared__ __align__(16) float qsh[8][HEAD];
+    __shared__ uint64_t bar;
+    __shared__ int page_s[ATT_WIN];
+    ptx::grid_dependency_wait();
+    ptx::launch_dependents();
+    const int g = blockIdx.x, row = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = g * group + warp;
+    float* qw = qsh[warp];
+    const int rows = pb.hdr->rows;
+    bool valid = row < rows;
+    RowDesc rd = {};
+    if (valid) {
+        rd = pb.row[row];
+        if (rd.pos < 0 || rd.pos >= kv.max_pos || (unsigned)rd.seq >= (unsigned)MAX_SEQS) {
+            if (threadIdx.x == 0) atomicOr(kv.err, 2);
+            *(float4*)(out + (size_t)row * out_ld + h * HEAD + 4 * lane) = make_float4(0.f, 0.f, 0.f, 0.f);
+            valid = false;
+        }
+    }
+    if (!valid) {  // uniform over the CTA
+        if (bout) mx::emit_pieces_smem(qw, HEAD, 4, row, 0, 1, lane, 32, h * HEAD, bN, bout, sfout);
+        return;
+    }
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&bar, 1);
+        ptx::fence_barrier_init();
+    }
+    *(float4*)(qw + 4 * lane) = *(const float4*)(qkv + (size_t)row * ld + h * HEAD + 4 * lane);
+    __syncthreads();
+    const int visible = rd.pos + 1;
+    const int npages = (visible + PAGE - 1) / PAGE;
+    const int32_t* pt = pb.page_table[rd.seq];
+    const int kvh = g;
+    const float scale = sqrtf(128.0f);
+    float m = -INFINITY, l = 0.f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
+    for (int w0 = 0, it = 0; w0 < npages; w0 += ATT_WIN, ++it) {
+        const int wn = min(ATT_WIN, npages - w0);
+        if (threadIdx.x == 0) {
+            uint32_t bytes = 0;
+            int pg[ATT_WIN];
+            for (int i = 0; i < wn; ++i) {
+                pg[i] = pt[w0 + i];
+                if (!page_ok(kv, pg[i])) pg[i] = -1;
+                else bytes += 2 * PB;
+                page_s[i] = pg[i];
+            }
+            ptx::mbar_arrive_expect_tx(&bar, bytes);
+            for (int i = 0; i < wn; ++i) {
+                if (pg[i] < 0) continue;
+                const size_t off = kv_index(pg[i], kvh, 0, kv.kv_heads) * (F32 ? 4 : 2);
+                ptx::bulk_g2s(kvs + (2 * i) * PB, (const uint8_t*)kv.k + off, PB, &bar);
+                ptx::bulk_g2s(kvs + (2 * i + 1) * PB, (const uint8_t*)kv.v + off, PB, &bar);
+            }
+        }
+        if (!ptx::mbar_wait(&bar, it & 1, ATT_WAIT)) ok = false;
+        __syncthreads();  // page_s is visible
+        if (ok) {
+            for (int i = 0; i < wn; ++i) {
+                if (page_s[i] < 0) continue;  // flagged: its positions are left out
+                const uint8_t* Ks = kvs + (2 * i) * PB;
+                const uint8_t* Vs = kvs + (2 * i + 1) * PB;
+                for (int half = 0; half < PAGE / 32; ++half) {
+                    const int c0 = (w0 + i) * PAGE + half * 32;
+                    if (c0 >= visible) break;
+                    const int r = half * 32 + lane;  // row of this lane's position in the page
+                    float sc = -INFINITY;
+                    if (c0 + lane < visible) {
+                        float dot = 0.f;
+                        if (F32) {
+                            const float4* kr = (const float4*)(Ks + (size_t)r * HEAD * 4);
+#pragma unroll 8
+                            for (int c = 0; c < 32; ++c) {
+                                const int cc = (c + lane) & 31;
+                                const float4 k4 = kr[cc];
+                                const float4 q4 = *(const float4*)(qw + 4 * cc);
+                                dot = fmaf(q4.x, k4.x, dot);
+                                dot = fmaf(q4.y, k4.y, dot);
+                                dot = fmaf(q4.z, k4.z, dot);
+                                dot = fmaf(q4.w, k4.w, dot);
+                            }
+                        } else {
+                            const uint4* kr = (const uint4*)(Ks + (size_t)r * HEAD * 2);
+#pragma unroll 4
+                            for (int c = 0; c < 16; ++c) {
+                                const int cc = (c + lane) & 15;
+                                const uint4 k8 = kr[cc];
+                                const float4 qa = *(const float4*)(qw + 8 * cc);
+                                const float4 qb = *(const float4*)(qw + 8 * cc + 4);
+                                dot = fmaf(qa.x, __uint_as_float(k8.x << 16), dot);
+                                dot = fmaf(qa.y, __uint_as_float(k8.x & 0xffff0000u), dot);
+                                dot = fmaf(qa.z, __uint_as_float(k8.y << 16), dot);
+                                dot = fmaf(qa.w, __uint_as_float(k8.y & 0xffff0000u), dot);
+                                dot = fmaf(qb.x, __uint_as_float(k8.z << 16), dot);
+                                dot = fmaf(qb.y, __uint_as_float(k8.z & 0xffff0000u), dot);
+                                dot = fmaf(qb.z, __uint_as_float(k8.w << 16), dot);
+                                dot = fmaf(qb.w, __uint_as_float(k8.w & 0xffff0000u), dot);
+                            }
+                        }
+                        sc = __fdiv_rn(dot, scale);
+                    }
+                    const float cmax = warp_max(sc);
+                    const float nm = fmaxf(m, cmax);
+                    const float corr = nm == -INFINITY ? 1.f : expf(m - nm);
+                    const float p = sc == -INFINITY ? 0.f : expf(sc - nm);
+                    l = fmaf(l, corr, warp_sum(p));
+#pragma unroll
+                    for (int d = 0; d < 4; ++d) acc[d] *= corr;
+                    m = nm;
+                    const int n = min(32, visible - c0);
+#pragma unroll 8
+                    for (int jj = 0; jj < n; ++jj) {
+                        const float pj = __shfl_sync(0xffffffffu, p, jj);
+                        const int vr = half * 32 + jj;
+                        float v[4];
+                        if (F32) {
+                            const float4 v4 = *(const float4*)(Vs + ((size_t)vr * HEAD + 4 * lane) * 4);
+                            v[0] = v4.x; v[1] = v4.y; v[2] = v4.z; v[3] = v4.w;
+                        } else {
+                            const uint2 v2 = *(const uint2*)(Vs + ((size_t)vr * HEAD + 4 * lane) * 2);
+                            v[0] = __uint_as_float(v2.x << 16);
+                            v[1] = __uint_as_float(v2.x & 0xffff0000u);
+                            v[2] = __uint_as_float(v2.y << 16);
+                            v[3] = __uint_as_float(v2.y & 0xffff0000u);
+                        }
+#pragma unroll
+                        for (int d = 0; d < 4; ++d) acc[d] = fmaf(pj, v[d], acc[d]);
+                    }
+                }
+            }
+        }
+        __syncthreads();  // the window is free for the next copy
+    }
+    if (!ok && threadIdx.x == 0) atomicOr(kv.err, 4);  // a page copy did not arrive in time
+    float o[4];
+#pragma unroll
+    for (int d = 0; d < 4; ++d) o[d] = __fdiv_rn(acc[d], l);
+    *(float4*)(out + (size_t)row * out_ld + h * HEAD + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
+    if (bout) {
+        __syncwarp();  // every lane has finished reading q
+        *(float4*)(qw + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
+        __syncwarp();
+        mx::emit_pieces_smem(qw, HEAD, 4, row, 1, 1, lane, 32, h * HEAD, bN, bout, sfout);
+    }
+}
+
 // First maximum of each predicted row, ties to the lower index
 // (model.rs:288-296, gpu.metal:176-212).
 __global__ void __launch_bounds__(1024) k_argmax(PassBuf pb, const float* __restrict__ logits,
@@ -743,6 +916,8 @@ jl_status configure_kernels() {
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_STORE>()));
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_ADD>()));
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_SWIGLU>()));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_decode<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(0)));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_decode<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(1)));
     JL_TRY(mx_configure());
     if (dev < 64) done[dev] = true;
     return JL_OK;
@@ -780,6 +955,15 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     uint8_t* bout = pieces ? c.m->mx.battn : nullptr;
     uint8_t* sfout = pieces ? c.m->mx.sfattn : nullptr;
     const int bN = 8 * c.rows_cap;
+    if (pieces && group <= 8) {  // the fused decode pass: a warp per query head
+        const dim3 g2(c.m->kv_heads, c.rows_cap), blk(32 * group);
+        const int qw = c.m->q_heads * HEAD;
+        if (c.m->kv.dtype == JL_KV_F32)
+            return launch_pdl(k_attn_decode<1>, g2, blk, att_smem(1), c.stream, c.m->pass, (const float*)c.m->s.qkv,
+                              qkv_ld(c.m), group, kv_view(c.m, layer), c.m->s.attn, qw, bout, sfout, bN);
+        return launch_pdl(k_attn_decode<0>, g2, blk, att_smem(0), c.stream, c.m->pass, (const float*)c.m->s.qkv,
+                          qkv_ld(c.m), group, kv_view(c.m, layer), c.m->s.attn, qw, bout, sfout, bN);
+    }
     if (c.m->kv.dtype == JL_KV_F32)
         return launch_pdl(k_attention<1>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
                           qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn, bout, sfout, bN);
