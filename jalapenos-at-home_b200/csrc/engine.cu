@@ -375,6 +375,8 @@ jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head) {
     const jl_model* m = c.m;
     if (m->mx.fused && c.rows_cap <= mx_max_tokens()) {
         JL_TRY(record_fused_pass(c, layers));
+        if (with_head && m->bf_head.a && c.head_cap <= mx_max_tokens())  // model.rs:220-239
+            return mx_head_fused(c, m->bf_head, m->final_norm, m->s.logits, m->vocab);
         if (with_head) {
             JL_TRY(launch_rmsnorm(c, m->s.x, m->final_norm, m->s.xh, true));  // model.rs:228
             JL_TRY(launch_head(c));                                           // model.rs:229-234

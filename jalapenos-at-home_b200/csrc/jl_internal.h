@@ -127,6 +127,11 @@ struct MxBuffers {
     uint8_t* bact = nullptr;
     uint8_t* sfact = nullptr;
     float* part = nullptr;     // [hidden / 128][MX_PART_STRIDE]
+    // bf16 output table on the tensor cores: its input pieces and each
+    // tile's first maximum per row
+    uint8_t* bhead = nullptr;  // [hidden / 64][64 * 128]
+    float* amax_v = nullptr;   // [T][MX_PART_STRIDE]
+    int* amax_i = nullptr;
 };
 
 struct LayerW {
@@ -192,6 +197,7 @@ struct jl_model {
     bool tied = false;
     jl::Mat embed, head;
     jl::MxProj mx_head;                   // tensor-core copy of an MXFP4 output table
+    jl::MxProj bf_head;                   // tensor-core copy of a bf16 output table (fused pass)
     jl::MxBuffers mx;
     const uint16_t* final_norm = nullptr;
     std::vector<jl::LayerW> lw;
@@ -322,6 +328,11 @@ jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxF
 // of a fused pass (after the embedding).
 jl_status mx_norm_pieces(const PassCtx& c, const float* x, int ldx, const uint16_t* w, int width,
                          uint8_t* bout, uint8_t* sfout, float* part);
+// bf16 output table on the tensor cores (kind::f16): load-time tiles, and the
+// fused final norm + logits + argmax of a decode pass.
+size_t bf16_tile_bytes(int rows, int K);
+jl_status mx_build_bf16(const Mat& w, uint8_t* dst, MxProj* out, cudaStream_t stream);
+jl_status mx_head_fused(const PassCtx& c, const MxProj& p, const uint16_t* norm, float* logits, int ldy);
 // mx_project over caller-owned memory: `hdr` (rows read on the device),
 // `scratch` laid out as mx_scratch_plan says, `err` the device error flag.
 jl_status mx_project_with(const MxProj& p, int epi, const PassHdr* hdr, int mcap, const float* x,

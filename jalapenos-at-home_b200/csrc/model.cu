@@ -179,6 +179,10 @@ jl_status build_mx(jl_model* m) {
     JL_CUDA(cudaGetDevice(&dev));
     JL_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int QW = m->q_heads * HEAD, KVW = m->kv_heads * HEAD;
+    // fused decode pass: piece images need whole 256-element stages; a bf16
+    // output table then also runs on the tensor cores
+    const bool fused = all && m->hidden % 256 == 0 && QW % 256 == 0 && m->inter % 256 == 0;
+    const bool head_bf = fused && m->head.kind == MAT_BF16;
     Plan plan;
     std::vector<size_t> offs;
     if (all)
@@ -189,6 +193,7 @@ jl_status build_mx(jl_model* m) {
             offs.push_back(plan.take(mx_tile_bytes(m->hidden, m->inter, false)));
         }
     const size_t head_off = head ? plan.take(mx_tile_bytes(m->vocab, m->hidden, false)) : 0;
+    const size_t bfh_off = head_bf ? plan.take(bf16_tile_bytes(m->vocab, m->hidden)) : 0;
     if (cudaMalloc(&m->mx.arena, plan.bytes) != cudaSuccess) {
         cudaGetLastError();
         set_error("cannot allocate %zu bytes for tensor-core weight tiles", plan.bytes);
@@ -223,13 +228,12 @@ jl_status build_mx(jl_model* m) {
         JL_TRY(mx_build(h, 1, false, base + head_off, sms, &m->mx_head, 0));
         track(m->mx_head);
     }
+    if (head_bf) JL_TRY(mx_build_bf16(m->head, base + bfh_off, &m->bf_head, 0));
     Plan sp;
     const size_t off_b = sp.take((size_t)maxS * mx_max_tokens() * 8 * 128);
     const size_t off_sf = sp.take((size_t)maxS * 1024);
     const size_t off_ws = sp.take(ws_floats * sizeof(float));
     const size_t off_t = sp.take((size_t)maxT * sizeof(int));
-    // fused decode pass: piece images need whole 256-element stages
-    const bool fused = all && m->hidden % 256 == 0 && QW % 256 == 0 && m->inter % 256 == 0;
     const size_t img_x = (size_t)(m->hidden / 256) * mx_max_tokens() * 8 * 128;
     const size_t img_a = (size_t)(QW / 256) * mx_max_tokens() * 8 * 128;
     const size_t img_f = (size_t)(m->inter / 256) * mx_max_tokens() * 8 * 128;
@@ -242,6 +246,12 @@ jl_status build_mx(jl_model* m) {
         off_ff = sp.take(img_f);
         off_fsf = sp.take((size_t)(m->inter / 256) * 1024);
         off_fp = sp.take((size_t)(m->hidden / 128) * MX_PART_STRIDE * sizeof(float));
+    }
+    size_t off_bh = 0, off_av = 0, off_ai = 0;
+    if (head_bf) {
+        off_bh = sp.take((size_t)(m->hidden / 64) * (4 * mx_max_tokens()) * 128);
+        off_av = sp.take((size_t)m->bf_head.T * MX_PART_STRIDE * sizeof(float));
+        off_ai = sp.take((size_t)m->bf_head.T * MX_PART_STRIDE * sizeof(int));
     }
     if (cudaMalloc(&m->mx.scratch, sp.bytes) != cudaSuccess) {
         cudaGetLastError();
@@ -263,6 +273,11 @@ jl_status build_mx(jl_model* m) {
         m->mx.bact = s + off_ff;
         m->mx.sfact = s + off_fsf;
         m->mx.part = (float*)(s + off_fp);
+    }
+    if (head_bf) {
+        m->mx.bhead = s + off_bh;
+        m->mx.amax_v = (float*)(s + off_av);
+        m->mx.amax_i = (int*)(s + off_ai);
     }
     JL_CUDA(cudaDeviceSynchronize());
     return JL_OK;

@@ -97,6 +97,112 @@ __global__ void __launch_bounds__(128) k_norm_pieces(const PassHdr* __restrict__
     if (threadIdx.x == 0) part[t * MX_PART_STRIDE + m] = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
 }
 
+// The final RMSNorm of the rows whose next token is predicted
+// (model.rs:228, lib.rs:268-290, the same arithmetic as k_rmsnorm), written
+// as the bf16 output table's input: four bf16 pieces per value (each the
+// rounding of what the previous ones left; together about 32 significant
+// bits, more than the f32 value holds), row n = 4 * r + piece of an image
+// with N MMA columns and 64 K-elements (128 bytes) per stage.  CTA r < N/4;
+// rows past the predicted ones are zero.
+__global__ void __launch_bounds__(256) k_head_pieces(PassBuf pb, int head_cap, const float* __restrict__ x,
+                                                     int hidden, const uint16_t* __restrict__ w, int N,
+                                                     uint8_t* __restrict__ bimg) {
+    __shared__ float red[32];
+    ptx::grid_dependency_wait();
+    ptx::launch_dependents();
+    const int r = blockIdx.x;
+    const bool live = r < min(pb.hdr->head_rows, head_cap);
+    const float* xr = live ? x + (size_t)pb.head_row[r] * hidden : x;
+    float size = 1.f;
+    if (live) {  // uniform over the CTA
+        float ss = 0.f;
+        for (int j = threadIdx.x; j < hidden; j += blockDim.x) ss = fmaf(xr[j], xr[j], ss);
+        ss = block_sum(ss, red);
+        size = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)hidden), 1e-6f));
+    }
+    for (int j2 = threadIdx.x; j2 < hidden / 2; j2 += blockDim.x) {
+        const int j = 2 * j2;
+        float v0 = 0.f, v1 = 0.f;
+        if (live) {
+            v0 = __fmul_rn(__fdiv_rn(xr[j], size), bf16f(w[j]));
+            v1 = __fmul_rn(__fdiv_rn(xr[j + 1], size), bf16f(w[j + 1]));
+        }
+        uint8_t* img = bimg + (size_t)(j / 64) * N * 128;
+        const uint32_t byte = (uint32_t)(j % 64) * 2;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const uint32_t b0 = f2bf16(v0), b1 = f2bf16(v1);
+            v0 = __fsub_rn(v0, bf16f(b0));  // exact: a value minus its rounding
+            v1 = __fsub_rn(v1, bf16f(b1));
+            *(uint32_t*)(img + swz128((uint32_t)(4 * r + p), byte)) = b0 | (b1 << 16);
+        }
+    }
+}
+
+// First maximum of each predicted row over the head tiles' partial maxima,
+// in tile order (ties to the lower index, model.rs:288-296).
+__global__ void __launch_bounds__(256) k_argmax_tiles(PassBuf pb, int T, const float* __restrict__ amax_v,
+                                                      const int* __restrict__ amax_i) {
+    __shared__ float bv_s[8];
+    __shared__ int bi_s[8];
+    ptx::grid_dependency_wait();
+    ptx::launch_dependents();
+    const int r = blockIdx.x;
+    if (r >= pb.hdr->head_rows) return;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const float v = amax_v[t * MX_PART_STRIDE + r];
+        const int i = amax_i[t * MX_PART_STRIDE + r];
+        if (v > bv || (v == bv && i < bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_down_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_down_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        bv_s[warp] = bv;
+        bi_s[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int q = 1; q < (int)(blockDim.x >> 5); ++q)
+            if (bv_s[q] > bv || (bv_s[q] == bv && bi_s[q] < bi)) {
+                bv = bv_s[q];
+                bi = bi_s[q];
+            }
+        pb.out_ids[r] = bi == 0x7fffffff ? 0u : (uint32_t)bi;
+    }
+}
+
+// Load-time re-layout of a bf16 matrix [rows][K] into the tiled, swizzled
+// stages of the bf16 projection: tile t, stage s = rows 128t.., elements
+// 64s..64s+63 (128 bytes per row).  One thread per 16-byte chunk.
+__global__ void k_bf16_tile(const uint16_t* __restrict__ src, int rows, int K, int T, int S,
+                            uint8_t* __restrict__ dst) {
+    const size_t chunks = (size_t)T * S * TILE_ROWS * 8;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < chunks;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int c16 = (int)(i % 8);
+        const int r = (int)((i / 8) % TILE_ROWS);
+        const int s = (int)((i / (8 * TILE_ROWS)) % S);
+        const int t = (int)(i / ((size_t)8 * TILE_ROWS * S));
+        const int gr = t * TILE_ROWS + r, k0 = s * 64 + c16 * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (gr < rows && k0 < K) v = *reinterpret_cast<const uint4*>(src + (size_t)gr * K + k0);
+        *reinterpret_cast<uint4*>(dst + ((size_t)t * S + s) * A_STAGE + swz128((uint32_t)r, (uint32_t)c16 * 16)) = v;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // the projection
 
@@ -136,16 +242,26 @@ struct MxArgs {
     const RowDesc* rows;
     const int32_t* const* page_table;
     KvView kv;
+    // head: each tile's first maximum per row ([T][MX_PART_STRIDE])
+    float* amax_v;
+    int* amax_i;
 };
 
-enum : int { MX_STORE = 0, MX_ADD = 1, MX_SWIGLU = 2, MX_QKV = 3 };
+enum : int { MX_STORE = 0, MX_ADD = 1, MX_SWIGLU = 2, MX_QKV = 3, MX_HEAD = 4 };
+// Weight formats: MXFP4 (kind::mxf4 block-scaled MMA, 8 E2M1 activation
+// pieces per row) or bf16 (kind::f16 MMA, 4 bf16 activation pieces per row).
+enum : int { KIND_MX = 0, KIND_BF = 1 };
 constexpr int MX_MAXSTAGES = 6;
 constexpr int MX_MAXTOK = 16;       // tokens per pass on this path: N = 8 * tokens <= 128
 constexpr int MX_THREADS = 192;     // warp 0 loads, warp 1 MMAs, warps 2-5 epilogue
 static_assert(MX_PART_STRIDE >= MX_MAXTOK, "partials hold every row of a pass");
 static_assert(MX_MAXTOK == 16, "emit_pieces_all takes 16 rows");
 
-__host__ __device__ constexpr int mx_stage_bytes(int N) { return A_STAGE + N * 128 + 2 * SF_STAGE; }
+__host__ __device__ constexpr int mx_stage_bytes(int N, int kind = KIND_MX) {
+    return A_STAGE + N * 128 + (kind == KIND_MX ? 2 * SF_STAGE : 0);
+}
+// MMA columns one row occupies (its pieces, then padding).
+__host__ __device__ constexpr int cols_per_row(int kind) { return kind == KIND_MX ? 8 : 4; }
 
 // The four epilogue warps synchronise among themselves only.
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -165,21 +281,22 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 // red_full barrier; the leader (rank 0) adds the slots in rank order (a
 // fixed order, so results do not depend on timing or on the row count), then
 // frees them (slot_free) and runs the epilogue.
-template <int EPI>
+template <int EPI, int KIND>
 __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     __shared__ uint64_t full[MX_MAXSTAGES], empty[MX_MAXSTAGES], tfull[2], tempty[2];
     __shared__ uint64_t red_full, slot_free;
     __shared__ uint32_t tmem_base_s;
-    __shared__ float red_s[4][MX_MAXTOK];    // per-warp sums of squares
+    __shared__ float red_s[4][MX_MAXTOK];    // per-warp sums of squares / row maxima
+    __shared__ int redi_s[4][MX_MAXTOK];     // per-warp arg maxima
     __shared__ float sz_s[MX_MAXTOK];        // 1 / input RMS per row
     __shared__ float qk_s[MX_MAXTOK];        // 1 / RMS of this head, per row
     __shared__ int kvpos_s[MX_MAXTOK];       // q|k|v: position of each row, -1 if invalid
     __shared__ int kvpage_s[MX_MAXTOK];      //   and its cache page
 
     const int N = a.N, ST = a.stages, NB = a.nbuf;
-    const int sbytes = mx_stage_bytes(N);
+    const int sbytes = mx_stage_bytes(N, KIND);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ks = a.ksplit;
     const int kc = ks > 1 ? (int)ptx::cluster_ctarank() : 0;
@@ -230,8 +347,9 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                         uint8_t* base = smem + g * sbytes;
                         ptx::mbar_arrive_expect_tx(&full[g], (uint32_t)sbytes);
                         ptx::bulk_g2s(base, a.a + ((size_t)t * a.S + s) * A_STAGE, A_STAGE, &full[g]);
-                        ptx::bulk_g2s(base + A_STAGE + N * 128, a.sfa + ((size_t)t * a.S + s) * SF_STAGE,
-                                      SF_STAGE, &full[g]);
+                        if (KIND == KIND_MX)
+                            ptx::bulk_g2s(base + A_STAGE + N * 128, a.sfa + ((size_t)t * a.S + s) * SF_STAGE,
+                                          SF_STAGE, &full[g]);
                     }
                 }
                 pre = g;
@@ -249,12 +367,14 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                         }
                         ptx::mbar_arrive_expect_tx(&full[slot], (uint32_t)sbytes);
                         ptx::bulk_g2s(base, a.a + ((size_t)t * a.S + s) * A_STAGE, A_STAGE, &full[slot]);
-                        ptx::bulk_g2s(base + A_STAGE + N * 128, a.sfa + ((size_t)t * a.S + s) * SF_STAGE,
-                                      SF_STAGE, &full[slot]);
+                        if (KIND == KIND_MX)
+                            ptx::bulk_g2s(base + A_STAGE + N * 128, a.sfa + ((size_t)t * a.S + s) * SF_STAGE,
+                                          SF_STAGE, &full[slot]);
                     }
                     ptx::bulk_g2s(base + A_STAGE, a.b + (size_t)s * N * 128, (uint32_t)(N * 128), &full[slot]);
-                    ptx::bulk_g2s(base + A_STAGE + N * 128 + SF_STAGE, a.sfb + (size_t)s * SF_STAGE,
-                                  SF_STAGE, &full[slot]);
+                    if (KIND == KIND_MX)
+                        ptx::bulk_g2s(base + A_STAGE + N * 128 + SF_STAGE, a.sfb + (size_t)s * SF_STAGE,
+                                      SF_STAGE, &full[slot]);
                 }
             }
             // every load is issued: the next kernel may start prefetching
@@ -283,21 +403,29 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                     uint8_t* base = smem + slot * sbytes;
                     const uint32_t a_addr = ptx::smem_u32(base);
                     const uint32_t b_addr = ptx::smem_u32(base + A_STAGE);
-                    const uint32_t sfa_addr = ptx::smem_u32(base + A_STAGE + N * 128);
-                    const uint32_t sfb_addr = sfa_addr + SF_STAGE;
-                    ptx::tmem_cp_32x128b_warpx4(tmem + SFA_COL, ptx::smem_desc(sfa_addr, 16, 128, 0));
-                    ptx::tmem_cp_32x128b_warpx4(tmem + SFA_COL + 4, ptx::smem_desc(sfa_addr + 512, 16, 128, 0));
-                    ptx::tmem_cp_32x128b_warpx4(tmem + SFB_COL, ptx::smem_desc(sfb_addr, 16, 128, 0));
-                    ptx::tmem_cp_32x128b_warpx4(tmem + SFB_COL + 4, ptx::smem_desc(sfb_addr + 512, 16, 128, 0));
+                    if (KIND == KIND_MX) {
+                        const uint32_t sfa_addr = ptx::smem_u32(base + A_STAGE + N * 128);
+                        const uint32_t sfb_addr = sfa_addr + SF_STAGE;
+                        ptx::tmem_cp_32x128b_warpx4(tmem + SFA_COL, ptx::smem_desc(sfa_addr, 16, 128, 0));
+                        ptx::tmem_cp_32x128b_warpx4(tmem + SFA_COL + 4, ptx::smem_desc(sfa_addr + 512, 16, 128, 0));
+                        ptx::tmem_cp_32x128b_warpx4(tmem + SFB_COL, ptx::smem_desc(sfb_addr, 16, 128, 0));
+                        ptx::tmem_cp_32x128b_warpx4(tmem + SFB_COL + 4, ptx::smem_desc(sfb_addr + 512, 16, 128, 0));
+                    }
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
+                        // 32 bytes of K per instruction: 64 E2M1 codes or 16 bf16 values
                         const uint64_t ad = ptx::smem_desc(a_addr + 32 * q, 16, 1024, 2);
                         const uint64_t bd = ptx::smem_desc(b_addr + 32 * q, 16, 1024, 2);
-                        const uint32_t sf_id = (uint32_t)(q & 1) * 2;
-                        const uint32_t sfa_t = (tmem + SFA_COL + (q >> 1) * 4) | (sf_id << 30);
-                        const uint32_t sfb_t = (tmem + SFB_COL + (q >> 1) * 4) | (sf_id << 30);
-                        ptx::mma_mxf4(d_tmem, ad, bd, ptx::mxf4_idesc(128, (uint32_t)N, sf_id, sf_id), sfa_t,
-                                      sfb_t, (s > s0 || q > 0) ? 1u : 0u);
+                        if (KIND == KIND_MX) {
+                            const uint32_t sf_id = (uint32_t)(q & 1) * 2;
+                            const uint32_t sfa_t = (tmem + SFA_COL + (q >> 1) * 4) | (sf_id << 30);
+                            const uint32_t sfb_t = (tmem + SFB_COL + (q >> 1) * 4) | (sf_id << 30);
+                            ptx::mma_mxf4(d_tmem, ad, bd, ptx::mxf4_idesc(128, (uint32_t)N, sf_id, sf_id), sfa_t,
+                                          sfb_t, (s > s0 || q > 0) ? 1u : 0u);
+                        } else {
+                            ptx::mma_bf16(d_tmem, ad, bd, ptx::bf16_idesc(128, (uint32_t)N),
+                                          (s > s0 || q > 0) ? 1u : 0u);
+                        }
                     }
                     ptx::tc_commit(&empty[slot]);
                 }
@@ -363,21 +491,22 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
             ptx::tc_fence_after();
             float val[MX_MAXTOK];
             const uint32_t lanebase = tmem + ((uint32_t)(quarter * 32) << 16) + ACC_COL + buf * 64;
+            constexpr int CPR = cols_per_row(KIND), RPL = 32 / CPR;  // rows per 32-column load
 #pragma unroll
-            for (int m0 = 0; m0 < MX_MAXTOK; m0 += 4) {
+            for (int m0 = 0; m0 < MX_MAXTOK; m0 += RPL) {
                 if (m0 < a.mcap) {  // uniform: the whole warp loads together
                     float v[32];
-                    ptx::tmem_ld32(lanebase + m0 * 8, v);
+                    ptx::tmem_ld32(lanebase + m0 * CPR, v);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        float acc = v[8 * i + 7];  // smallest correction first
+                    for (int i = 0; i < RPL; ++i) {
+                        float acc = v[CPR * i + CPR - 1];  // smallest correction first
 #pragma unroll
-                        for (int p = 6; p >= 0; --p) acc = __fadd_rn(acc, v[8 * i + p]);
+                        for (int p = CPR - 2; p >= 0; --p) acc = __fadd_rn(acc, v[CPR * i + p]);
                         val[m0 + i] = acc;
                     }
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) val[m0 + i] = 0.f;
+                    for (int i = 0; i < RPL; ++i) val[m0 + i] = 0.f;
                 }
             }
             ptx::tc_fence_before();
@@ -520,6 +649,45 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                         else ((uint16_t*)dst)[idx] = f2bf16(val[m]);
                     }
                 }
+            } else if (EPI == MX_HEAD) {
+                // logits, and this tile's first maximum per row (model.rs:288-296):
+                // ties go to the lower vocabulary index
+                const int gr = t * TILE_ROWS + row;
+                const bool valid = gr < a.out_rows;
+#pragma unroll
+                for (int m = 0; m < MX_MAXTOK; ++m)
+                    if (m < M && valid) a.y[(size_t)m * a.ldy + gr] = val[m];
+#pragma unroll
+                for (int m = 0; m < MX_MAXTOK; ++m) {
+                    float bv = valid ? val[m] : -INFINITY;
+                    int bi = gr;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const float ov = __shfl_down_sync(0xffffffffu, bv, o);
+                        const int oi = __shfl_down_sync(0xffffffffu, bi, o);
+                        if (ov > bv || (ov == bv && oi < bi)) {
+                            bv = ov;
+                            bi = oi;
+                        }
+                    }
+                    if (lane == 0) {
+                        red_s[quarter][m] = bv;
+                        redi_s[quarter][m] = bi;
+                    }
+                }
+                epi_bar();
+                if (row < M) {  // quarters hold increasing indices: keep the first on ties
+                    float bv = red_s[0][row];
+                    int bi = redi_s[0][row];
+                    for (int q = 1; q < 4; ++q)
+                        if (red_s[q][row] > bv) {
+                            bv = red_s[q][row];
+                            bi = redi_s[q][row];
+                        }
+                    a.amax_v[t * MX_PART_STRIDE + row] = bv;
+                    a.amax_i[t * MX_PART_STRIDE + row] = bi;
+                }
+                epi_bar();  // red_s is reused by the next tile
             } else {
                 const int gr = t * TILE_ROWS + row;
                 const bool valid = gr < a.out_rows;
@@ -669,29 +837,31 @@ void mx_shape(int N, int* stages, int* nbuf) {
 }
 
 // Stages, then the split-K slot (N / 8 rows x 128 f32), then alignment slack.
-size_t mx_smem(int N) {
+// Stages, then the split-K slot (mcap rows x 128 f32), then alignment slack.
+size_t mx_smem(int N, int kind, int mcap) {
     int st, nb;
     mx_shape(N, &st, &nb);
-    return (size_t)st * mx_stage_bytes(N) + (size_t)N * 64 + 1024;
+    return (size_t)st * mx_stage_bytes(N, kind) + (size_t)mcap * 512 + 1024;
 }
 
 constexpr int MX_PROBE_SMEM = 120 * 1024;  // more than half an SM: one CTA per SM
 
-template <int EPI>
+template <int EPI, int KIND>
 jl_status configure_mx() {
-    JL_CUDA(cudaFuncSetAttribute(k_mx_gemv<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)std::max<size_t>(MX_PROBE_SMEM, std::max(mx_smem(64), mx_smem(8 * MX_MAXTOK)))));
-    JL_CUDA(cudaFuncSetAttribute(k_mx_gemv<EPI>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    const size_t most = std::max(mx_smem(64, KIND, MX_MAXTOK), mx_smem(8 * MX_MAXTOK, KIND, MX_MAXTOK));
+    JL_CUDA(cudaFuncSetAttribute(k_mx_gemv<EPI, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)std::max<size_t>(MX_PROBE_SMEM, most)));
+    JL_CUDA(cudaFuncSetAttribute(k_mx_gemv<EPI, KIND>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     return JL_OK;
 }
 
-template <int EPI>
+template <int EPI, int KIND>
 jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream) {
     const int nc = std::min(a.T, a.ksplit > 1 ? mx_clusters(a.ksplit) : sms);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(nc * a.ksplit);
     cfg.blockDim = dim3(MX_THREADS);
-    cfg.dynamicSmemBytes = mx_smem(a.N);
+    cfg.dynamicSmemBytes = mx_smem(a.N, KIND, a.mcap);
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -706,7 +876,7 @@ jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream) {
     }
     cfg.attrs = attr;
     cfg.numAttrs = n;
-    JL_CUDA(cudaLaunchKernelEx(&cfg, k_mx_gemv<EPI>, a));
+    JL_CUDA(cudaLaunchKernelEx(&cfg, k_mx_gemv<EPI, KIND>, a));
     return JL_OK;
 }
 
@@ -716,20 +886,22 @@ jl_status launch_gemv(int epi, const MxArgs& a, int sms, cudaStream_t stream) {
         return JL_ERR_INVALID_ARG;
     }
     switch (epi) {
-        case MX_ADD: return launch_gemv_t<MX_ADD>(a, sms, stream);
-        case MX_SWIGLU: return launch_gemv_t<MX_SWIGLU>(a, sms, stream);
-        case MX_QKV: return launch_gemv_t<MX_QKV>(a, sms, stream);
-        default: return launch_gemv_t<MX_STORE>(a, sms, stream);
+        case MX_ADD: return launch_gemv_t<MX_ADD, KIND_MX>(a, sms, stream);
+        case MX_SWIGLU: return launch_gemv_t<MX_SWIGLU, KIND_MX>(a, sms, stream);
+        case MX_QKV: return launch_gemv_t<MX_QKV, KIND_MX>(a, sms, stream);
+        case MX_HEAD: return launch_gemv_t<MX_HEAD, KIND_BF>(a, sms, stream);
+        default: return launch_gemv_t<MX_STORE, KIND_MX>(a, sms, stream);
     }
 }
 
 }  // namespace
 
 jl_status mx_configure() {
-    JL_TRY(configure_mx<MX_STORE>());
-    JL_TRY(configure_mx<MX_ADD>());
-    JL_TRY(configure_mx<MX_SWIGLU>());
-    JL_TRY(configure_mx<MX_QKV>());
+    JL_TRY((configure_mx<MX_STORE, KIND_MX>()));
+    JL_TRY((configure_mx<MX_ADD, KIND_MX>()));
+    JL_TRY((configure_mx<MX_SWIGLU, KIND_MX>()));
+    JL_TRY((configure_mx<MX_QKV, KIND_MX>()));
+    JL_TRY((configure_mx<MX_HEAD, KIND_BF>()));
     int dev = 0, sms = 0;
     JL_CUDA(cudaGetDevice(&dev));
     JL_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -748,7 +920,7 @@ jl_status mx_configure() {
             cfg.attrs = attr;
             cfg.numAttrs = 1;
             int n = 0;
-            JL_CUDA(cudaOccupancyMaxActiveClusters(&n, k_mx_gemv<MX_STORE>, &cfg));
+            JL_CUDA(cudaOccupancyMaxActiveClusters(&n, k_mx_gemv<MX_STORE, KIND_MX>, &cfg));
             g_clusters[dev][ks] = n;
         }
     }
@@ -942,6 +1114,65 @@ jl_status mx_project_with(const MxProj& p, int epi, const PassHdr* hdr, int mcap
     a.tickets = tickets;
     a.err = err;
     return launch_gemv(epi, a, sms, stream);
+}
+
+size_t bf16_tile_bytes(int rows, int K) {
+    const int T = (rows + TILE_ROWS - 1) / TILE_ROWS, S = (K + 63) / 64;
+    return (size_t)T * S * A_STAGE;
+}
+
+jl_status mx_build_bf16(const Mat& w, uint8_t* dst, MxProj* out, cudaStream_t stream) {
+    if (w.kind != MAT_BF16 || w.cols % 64) {
+        set_error("the bf16 tensor-core table needs bf16 rows of a multiple of 64 elements");
+        return JL_ERR_INVALID_ARG;
+    }
+    MxProj p;
+    p.T = (w.rows + TILE_ROWS - 1) / TILE_ROWS;
+    p.S = w.cols / 64;
+    p.K = w.cols;
+    p.out_rows = w.rows;
+    p.a = dst;
+    p.sfa = nullptr;
+    p.ksplit = mx_ksplit(p.T, p.S);
+    const size_t chunks = (size_t)p.T * p.S * TILE_ROWS * 8;
+    const int grid = (int)std::min<size_t>((chunks + 255) / 256, 148 * 8);
+    k_bf16_tile<<<grid, 256, 0, stream>>>((const uint16_t*)w.data, w.rows, w.cols, p.T, p.S, dst);
+    JL_CUDA(cudaGetLastError());
+    *out = p;
+    return JL_OK;
+}
+
+jl_status mx_head_fused(const PassCtx& c, const MxProj& p, const uint16_t* norm, float* logits,
+                        int ldy) {
+    const jl_model* m = c.m;
+    const int mcap = c.head_cap;
+    if (mcap < 1 || mcap > MX_MAXTOK || !m->mx.bhead) {
+        set_error("tensor-core output table takes 1..%d rows per pass", MX_MAXTOK);
+        return JL_ERR_INVALID_ARG;
+    }
+    const int N = ((4 * mcap + 7) / 8) * 8;  // four pieces per row, a multiple of 8 columns
+    JL_TRY(launch_pdl(k_head_pieces, dim3(N / 4), dim3(256), 0, c.stream, m->pass, mcap,
+                      (const float*)m->s.x, m->hidden, norm, N, m->mx.bhead));
+    MxArgs a = {};
+    a.a = p.a;
+    a.b = m->mx.bhead;
+    a.T = p.T;
+    a.S = p.S;
+    a.ksplit = p.ksplit;
+    a.N = N;
+    a.mcap = mcap;
+    mx_shape(N, &a.stages, &a.nbuf);
+    a.hdr = m->pass.hdr;
+    a.use_head = 1;
+    a.y = logits;
+    a.ldy = ldy;
+    a.out_rows = p.out_rows;
+    a.err = m->counters;
+    a.amax_v = m->mx.amax_v;
+    a.amax_i = m->mx.amax_i;
+    JL_TRY(launch_gemv(MX_HEAD, a, m->sms, c.stream));
+    return launch_pdl(k_argmax_tiles, dim3(mcap), dim3(256), 0, c.stream, m->pass, p.T,
+                      (const float*)m->mx.amax_v, (const int*)m->mx.amax_i);
 }
 
 }  // namespace jl

@@ -195,6 +195,29 @@ __device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t a_desc, uint6
         : "memory");
 }
 
+// Instruction descriptor of tcgen05.mma kind::f16 with A and B both bf16 (one
+// type for both operands), f32 accumulation, both operands K-major.
+__device__ __forceinline__ uint32_t bf16_idesc(uint32_t M, uint32_t N) {
+    uint32_t d = 0;
+    d |= 1u << 4;   // D format F32
+    d |= 1u << 7;   // A format BF16
+    d |= 1u << 10;  // B format BF16
+    d |= ((N >> 3) & 0x3Fu) << 17;
+    d |= ((M >> 4) & 0x1Fu) << 24;
+    return d;       // K = 16 per instruction
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n"
+        "}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Copies a 32-row x 16-byte block (one scale-factor atom) from shared memory
 // to TMEM, broadcast to the four 32-lane quarters.
 __device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t src_desc) {
