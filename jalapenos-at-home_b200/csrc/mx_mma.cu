@@ -252,6 +252,7 @@ enum : int { MX_STORE = 0, MX_ADD = 1, MX_SWIGLU = 2, MX_QKV = 3, MX_HEAD = 4 };
 // pieces per row) or bf16 (kind::f16 MMA, 4 bf16 activation pieces per row).
 enum : int { KIND_MX = 0, KIND_BF = 1 };
 constexpr int MX_MAXSTAGES = 6;
+constexpr int MX_MAXCLUSTER = 8;  // portable cluster size: split-K at most 8 ways
 constexpr int MX_MAXTOK = 16;       // tokens per pass on this path: N = 8 * tokens <= 128
 constexpr int MX_THREADS = 192;     // warp 0 loads, warp 1 MMAs, warps 2-5 epilogue
 static_assert(MX_PART_STRIDE >= MX_MAXTOK, "partials hold every row of a pass");
@@ -262,6 +263,32 @@ __host__ __device__ constexpr int mx_stage_bytes(int N, int kind = KIND_MX) {
 }
 // MMA columns one row occupies (its pieces, then padding).
 __host__ __device__ constexpr int cols_per_row(int kind) { return kind == KIND_MX ? 8 : 4; }
+
+// Per-warp sums of v[m]^2 over the warp's 32 rows for rows m < mcap (MT a
+// bucket >= mcap: the rows advance together), written to red[quarter][m].
+// Each row's reduction tree is the same whatever the bucket.
+template <int MT>
+__device__ __forceinline__ void warp_sq_sums_t(const float (&v)[16], float (*red)[16], int quarter, int lane) {
+    float s[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) s[m] = __fmul_rn(v[m], v[m]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) s[m] += __shfl_xor_sync(0xffffffffu, s[m], o);
+    if (lane == 0)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) red[quarter][m] = s[m];
+}
+
+__device__ __forceinline__ void warp_sq_sums(const float (&v)[16], int mcap, float (*red)[16], int quarter,
+                                             int lane) {
+    if (mcap <= 1) warp_sq_sums_t<1>(v, red, quarter, lane);
+    else if (mcap <= 2) warp_sq_sums_t<2>(v, red, quarter, lane);
+    else if (mcap <= 4) warp_sq_sums_t<4>(v, red, quarter, lane);
+    else if (mcap <= 8) warp_sq_sums_t<8>(v, red, quarter, lane);
+    else warp_sq_sums_t<16>(v, red, quarter, lane);
+}
 
 // The four epilogue warps synchronise among themselves only.
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -302,9 +329,9 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
     const int kc = ks > 1 ? (int)ptx::cluster_ctarank() : 0;
     const int cid = blockIdx.x / ks, NC = gridDim.x / ks;
     const int s0 = (int)((long long)kc * a.S / ks), s1 = (int)((long long)(kc + 1) * a.S / ks);
-    // this CTA's split-K partial [mcap][128]; the leader never publishes its
-    // own, so there the region is epilogue scratch (SwiGLU up halves, RoPE
-    // partners: xs[m][0..63])
+    // this CTA's split-K partial [128][mcap rounded up to 4]; the leader
+    // never publishes its own, so there the region is epilogue scratch
+    // (staged outputs [m][128], SwiGLU up halves and RoPE partners xs[m][64])
     float* slot = (float*)(smem + ST * sbytes);
     float(*xs)[64] = (float(*)[64])slot;
 
@@ -514,26 +541,38 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
             if (lane == 0) ptx::mbar_arrive(&tempty[buf]);
 
             if (ks > 1) {
+                // slot layout [row][sst]: a row's partials for 4 tokens are one 16-byte word
+                const int sst = (a.mcap + 3) & ~3;
                 if (kc > 0) {
                     // publish this K slice's partial to the leader
                     if (j > 0 && !ptx::mbar_wait_cluster(&slot_free, (j - 1) & 1, WAIT_LIMIT)) ok = false;
 #pragma unroll
-                    for (int m = 0; m < MX_MAXTOK; ++m)
-                        if (m < a.mcap) slot[m * 128 + row] = val[m];
+                    for (int m4 = 0; m4 < MX_MAXTOK; m4 += 4)
+                        if (m4 < a.mcap)
+                            *(float4*)(slot + row * sst + m4) =
+                                make_float4(val[m4], val[m4 + 1], val[m4 + 2], val[m4 + 3]);
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive_remote(ptx::mapa(ptx::smem_u32(&red_full), 0));
                     continue;
                 }
                 if (!ptx::mbar_wait_cluster(&red_full, j & 1, WAIT_LIMIT)) ok = false;
-                const uint32_t mine = ptx::smem_u32(slot) + (uint32_t)row * 4;
-                for (int r = 1; r < ks; ++r) {
-                    const uint32_t base = ptx::mapa(mine, (uint32_t)r);
-                    float part[MX_MAXTOK];
+                const uint32_t mine = ptx::smem_u32(slot) + (uint32_t)(row * sst) * 4;
 #pragma unroll
-                    for (int m = 0; m < MX_MAXTOK; ++m)
-                        part[m] = m < a.mcap ? ptx::ld_shared_cluster(base + (uint32_t)m * 512) : 0.f;
+                for (int m4 = 0; m4 < MX_MAXTOK; m4 += 4) {
+                    if (m4 >= a.mcap) continue;
+                    // every rank's word first (one round trip), then the sums in rank order
+                    float4 part[MX_MAXCLUSTER - 1];
 #pragma unroll
-                    for (int m = 0; m < MX_MAXTOK; ++m) val[m] = __fadd_rn(val[m], part[m]);
+                    for (int r = 1; r < MX_MAXCLUSTER; ++r)
+                        if (r < ks) part[r - 1] = ptx::ld_shared_cluster_v4(ptx::mapa(mine + (uint32_t)m4 * 4, (uint32_t)r));
+#pragma unroll
+                    for (int r = 1; r < MX_MAXCLUSTER; ++r) {
+                        if (r >= ks) continue;
+                        val[m4] = __fadd_rn(val[m4], part[r - 1].x);
+                        val[m4 + 1] = __fadd_rn(val[m4 + 1], part[r - 1].y);
+                        val[m4 + 2] = __fadd_rn(val[m4 + 2], part[r - 1].z);
+                        val[m4 + 3] = __fadd_rn(val[m4 + 3], part[r - 1].w);
+                    }
                 }
                 __syncwarp();
                 if (lane == 0)
@@ -583,11 +622,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                 const bool is_q = t < Hq, is_k = !is_q && t < Hq + Hkv;
                 if (is_q || is_k) {
                     const float w = bf16f((is_q ? a.qn : a.kn)[row]);
-#pragma unroll
-                    for (int m = 0; m < MX_MAXTOK; ++m) {
-                        const float ss = warp_sum(__fmul_rn(val[m], val[m]));
-                        if (lane == 0) red_s[quarter][m] = ss;
-                    }
+                    warp_sq_sums(val, a.mcap, red_s, quarter, lane);
                     epi_bar();
                     if (row < a.mcap) {
                         const float ss = __fadd_rn(__fadd_rn(red_s[0][row], red_s[1][row]),
@@ -711,11 +746,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                     epi_bar();  // the staging area is reused by the next tile
                 }
                 if (a.part_out) {  // sum of squares of this tile's 128 outputs, per row
-#pragma unroll
-                    for (int m = 0; m < MX_MAXTOK; ++m) {
-                        const float ss = warp_sum(__fmul_rn(val[m], val[m]));
-                        if (lane == 0) red_s[quarter][m] = ss;
-                    }
+                    warp_sq_sums(val, a.mcap, red_s, quarter, lane);
                     epi_bar();
                     if (row < a.mcap)
                         a.part_out[t * MX_PART_STRIDE + row] = __fadd_rn(__fadd_rn(red_s[0][row], red_s[1][row]),
@@ -794,7 +825,6 @@ __global__ void k_mx_tile(TileSrc src, int swiglu, int K, int T, int S, uint8_t*
     }
 }
 
-constexpr int MX_MAXCLUSTER = 8;  // portable cluster size: split-K at most 8 ways
 constexpr int MX_MAXDEV = 64;
 // Clusters of each size that fit at one CTA per SM, per device (the GPU's
 // processing clusters decide how many SMs a cluster size can use).
@@ -841,7 +871,7 @@ void mx_shape(int N, int* stages, int* nbuf) {
 size_t mx_smem(int N, int kind, int mcap) {
     int st, nb;
     mx_shape(N, &st, &nb);
-    return (size_t)st * mx_stage_bytes(N, kind) + (size_t)mcap * 512 + 1024;
+    return (size_t)st * mx_stage_bytes(N, kind) + (size_t)((mcap + 3) & ~3) * 512 + 1024;
 }
 
 constexpr int MX_PROBE_SMEM = 120 * 1024;  // more than half an SM: one CTA per SM
