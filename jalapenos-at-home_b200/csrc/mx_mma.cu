@@ -574,8 +574,10 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                         val[m4 + 3] = __fadd_rn(val[m4 + 3], part[r - 1].w);
                     }
                 }
+                // the other ranks only wait for their slot when this cluster has
+                // another tile; at exit the cluster barrier keeps every slot alive
                 __syncwarp();
-                if (lane == 0)
+                if (lane == 0 && t + NC < a.T)
                     for (int r = 1; r < ks; ++r) ptx::mbar_arrive_remote(ptx::mapa(ptx::smem_u32(&slot_free), r));
             }
             if (a.part_in) {  // input RMSNorm: scale by 1 / the row's RMS (lib.rs:268-290)
@@ -837,19 +839,29 @@ int mx_clusters(int ks) {
     return n > 0 ? n : 1;
 }
 
-// K slices per tile: a cluster of ks CTAs streams ceil(T / clusters) tiles
-// of ceil(S / ks) stages each; a tile also costs about one stage of
-// epilogue, and a split about half a stage for the reduction through
-// distributed shared memory.  The choice depends only on the matrix shape,
-// never on the token count.
+// K slices per tile, from an estimate in microseconds of the time after the
+// dependency wait: a CTA's first MX_PREFETCH stages are loaded before the
+// wait, the rest stream at its share of HBM bandwidth (at most what one SM
+// pulls); a tile costs about a microsecond of epilogue, and a split the
+// reduction through distributed shared memory.  The choice depends only on
+// the matrix shape, never on the token count.
+constexpr int MX_PREFETCH = 4;           // ring stages issued before the dependency wait
+constexpr double MX_STAGE_KB = 17.0;     // weight bytes of a stage (codes + scales)
+constexpr double MX_HBM_GBS = 6000.0;
+constexpr double MX_SM_GBS = 120.0;
+constexpr double MX_EPI_US = 1.0;
+constexpr double MX_REDUCE_US = 1.5;
+
 int mx_ksplit(int T, int S) {
     int best = 1;
     double best_cost = 1e30;
     for (int ks = 1; ks <= std::min(S, MX_MAXCLUSTER); ++ks) {
-        const int nc = mx_clusters(ks);
-        const int per_cluster = (T + nc - 1) / nc;
-        const int per_unit = (S + ks - 1) / ks;
-        const double cost = (double)per_cluster * (per_unit + 1.0) + (ks > 1 ? 0.5 : 0.0);
+        const int nc = std::min(mx_clusters(ks), T);
+        const int tiles = (T + nc - 1) / nc;            // per cluster
+        const int stages = tiles * ((S + ks - 1) / ks);  // per CTA
+        const double after_kb = std::max(0, stages - MX_PREFETCH) * MX_STAGE_KB;
+        const double gbs = std::min(MX_SM_GBS, MX_HBM_GBS / (nc * ks));
+        const double cost = after_kb / gbs + tiles * MX_EPI_US + (ks > 1 ? MX_REDUCE_US : 0.0);
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
             best = ks;
