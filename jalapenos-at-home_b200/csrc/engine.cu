@@ -373,8 +373,10 @@ jl_status record_fused_pass(const PassCtx& c, int layers) {
 
 jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head) {
     const jl_model* m = c.m;
-    if (m->mx.fused && c.rows_cap <= mx_max_tokens()) {
-        JL_TRY(record_fused_pass(c, layers));
+    const bool dec = c.draft && m->dec_ok && c.rows_cap <= 2;
+    if (dec || (m->mx.fused && c.rows_cap <= mx_max_tokens())) {
+        if (dec) JL_TRY(record_dec_pass(c, layers));
+        else JL_TRY(record_fused_pass(c, layers));
         if (with_head && m->bf_head.a && c.head_cap <= mx_max_tokens())  // model.rs:220-239
             return mx_head_fused(c, m->bf_head, m->final_norm, m->s.logits, m->vocab);
         if (with_head) {
@@ -688,7 +690,7 @@ jl_status build_spec_graph(SpecGraph* g) {
         JL_TRY(add_conditional(body, &prev, 1, h_step[i], cudaGraphCondTypeIf, &ifn, &ifb));
         const cudaGraphConditionalHandle nxt = i + 1 < G ? h_step[i + 1] : 0;
         JL_TRY(capture_into(ifb, st, nullptr, [&]() -> jl_status {
-            PassCtx c{D, st, 1, 1};
+            PassCtx c{D, st, 1, 1, true};
             JL_TRY(record_pass_ctx(c, D->layers, true));
             k_draft_step<<<1, 1, 0, st>>>(g->st, D->pass, g->oracle_args, i, nxt);
             JL_CUDA(cudaGetLastError());
@@ -713,7 +715,7 @@ jl_status build_spec_graph(SpecGraph* g) {
         cudaGraph_t ifb;
         JL_TRY(add_conditional(body, &prev, 1, h_catch, cudaGraphCondTypeIf, &ifn, &ifb));
         JL_TRY(capture_into(ifb, st, nullptr, [&]() -> jl_status {
-            PassCtx c{D, st, 2, 1};
+            PassCtx c{D, st, 2, 1, true};
             JL_TRY(record_pass_ctx(c, D->layers, true));
             k_catchup_done<<<1, 1, 0, st>>>(g->st, D->pass, g->oracle_args);
             JL_CUDA(cudaGetLastError());

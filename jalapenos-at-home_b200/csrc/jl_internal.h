@@ -198,6 +198,7 @@ struct jl_model {
     jl::Mat embed, head;
     jl::MxProj mx_head;                   // tensor-core copy of an MXFP4 output table
     jl::MxProj bf_head;                   // tensor-core copy of a bf16 output table (fused pass)
+    bool dec_ok = false;                  // draft steps may run on the CUDA-core kernels
     jl::MxBuffers mx;
     const uint16_t* final_norm = nullptr;
     std::vector<jl::LayerW> lw;
@@ -274,6 +275,7 @@ struct PassCtx {
     cudaStream_t stream;
     int rows_cap;   // rows the pass may hold
     int head_cap;   // predicted rows the pass may hold
+    bool draft = false;  // a speculative loop's draft step (may take the CUDA-core path)
 };
 jl_status launch_embed(const PassCtx& c);
 jl_status launch_rmsnorm(const PassCtx& c, const float* x, const uint16_t* w, float* out,
@@ -333,6 +335,10 @@ jl_status mx_norm_pieces(const PassCtx& c, const float* x, int ldx, const uint16
 size_t bf16_tile_bytes(int rows, int K);
 jl_status mx_build_bf16(const Mat& w, uint8_t* dst, MxProj* out, cudaStream_t stream);
 jl_status mx_head_fused(const PassCtx& c, const MxProj& p, const uint16_t* norm, float* logits, int ldy);
+// Draft-step passes of 1..2 rows on CUDA cores (dec.cu).
+bool dec_supported(const jl_model* m);
+jl_status dec_configure();
+jl_status record_dec_pass(const PassCtx& c, int layers);
 // mx_project over caller-owned memory: `hdr` (rows read on the device),
 // `scratch` laid out as mx_scratch_plan says, `err` the device error flag.
 jl_status mx_project_with(const MxProj& p, int epi, const PassHdr* hdr, int mcap, const float* x,

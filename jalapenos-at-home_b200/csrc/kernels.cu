@@ -919,6 +919,7 @@ jl_status configure_kernels() {
     JL_CUDA(cudaFuncSetAttribute(k_attn_decode<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(0)));
     JL_CUDA(cudaFuncSetAttribute(k_attn_decode<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(1)));
     JL_TRY(mx_configure());
+    JL_TRY(dec_configure());
     if (dev < 64) done[dev] = true;
     return JL_OK;
 }
@@ -955,7 +956,7 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     uint8_t* bout = pieces ? c.m->mx.battn : nullptr;
     uint8_t* sfout = pieces ? c.m->mx.sfattn : nullptr;
     const int bN = 8 * c.rows_cap;
-    if (pieces && group <= 8) {  // the fused decode pass: a warp per query head
+    if (c.rows_cap <= SMALL_M && group <= 8) {  // decode passes: a warp per query head
         const dim3 g2(c.m->kv_heads, c.rows_cap), blk(32 * group);
         const int qw = c.m->q_heads * HEAD;
         if (c.m->kv.dtype == JL_KV_F32)

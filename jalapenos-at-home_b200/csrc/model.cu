@@ -229,6 +229,7 @@ jl_status build_mx(jl_model* m) {
         track(m->mx_head);
     }
     if (head_bf) JL_TRY(mx_build_bf16(m->head, base + bfh_off, &m->bf_head, 0));
+    m->dec_ok = dec_supported(m);
     Plan sp;
     const size_t off_b = sp.take((size_t)maxS * mx_max_tokens() * 8 * 128);
     const size_t off_sf = sp.take((size_t)maxS * 1024);
