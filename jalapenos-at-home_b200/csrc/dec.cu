@@ -170,6 +170,21 @@ __global__ void __launch_bounds__(512) k_dec_qkv(DecQkvArgs a) {
     ptx::grid_dependency_wait();
     ptx::launch_dependents();
     const int rows = min(a.pb.hdr->rows, a.mcap);
+    // warp m finishes row m: its position, RoPE factors and cache page are
+    // fetched now, while the input loads and the dot products run
+    RowDesc rd = {};
+    float2 c0 = make_float2(1.f, 0.f), c1 = make_float2(1.f, 0.f);
+    int page = -1;
+    bool row_ok = false;
+    if (warp < M && warp < rows) {
+        rd = a.pb.row[warp];
+        row_ok = rd.pos >= 0 && rd.pos < a.kv.max_pos && (unsigned)rd.seq < (unsigned)MAX_SEQS;
+        if (row_ok) {
+            c0 = a.rope[(size_t)rd.pos * HALF + lane];
+            c1 = a.rope[(size_t)rd.pos * HALF + lane + 32];
+            if (!is_q) page = a.pb.page_table[rd.seq][rd.pos / PAGE];
+        }
+    }
     dec_load_x(a.x, K, M, K, a.norm, xs4, red);
     const bool ok = ptx::mbar_wait(&bar, 0, DEC_WAIT);
     __syncthreads();
@@ -190,8 +205,7 @@ __global__ void __launch_bounds__(512) k_dec_qkv(DecQkvArgs a) {
     if (warp >= M || warp >= rows) return;
     const int m = warp;
     float a0 = res[m][lane], a1 = res[m][lane + 32], a2 = res[m][lane + 64], a3 = res[m][lane + 96];
-    const RowDesc rd = a.pb.row[m];
-    if (rd.pos < 0 || rd.pos >= a.kv.max_pos || (unsigned)rd.seq >= (unsigned)MAX_SEQS) {
+    if (!row_ok) {
         if (lane == 0) atomicOr(a.kv.err, 2);
         return;
     }
@@ -205,8 +219,6 @@ __global__ void __launch_bounds__(512) k_dec_qkv(DecQkvArgs a) {
         a2 = __fmul_rn(__fdiv_rn(a2, size), bf16f(gw[lane + 64]));
         a3 = __fmul_rn(__fdiv_rn(a3, size), bf16f(gw[lane + 96]));
         // lib.rs:306-313: out[i] = a cos - b sin; out[i+64] = b cos + a sin
-        const float2 c0 = a.rope[(size_t)rd.pos * HALF + lane];
-        const float2 c1 = a.rope[(size_t)rd.pos * HALF + lane + 32];
         const float b0 = __fsub_rn(__fmul_rn(a0, c0.x), __fmul_rn(a2, c0.y));
         const float b2 = __fadd_rn(__fmul_rn(a2, c0.x), __fmul_rn(a0, c0.y));
         const float b1 = __fsub_rn(__fmul_rn(a1, c1.x), __fmul_rn(a3, c1.y));
@@ -218,7 +230,6 @@ __global__ void __launch_bounds__(512) k_dec_qkv(DecQkvArgs a) {
         d[lane] = a0; d[lane + 32] = a1; d[lane + 64] = a2; d[lane + 96] = a3;
         return;
     }
-    const int page = a.pb.page_table[rd.seq][rd.pos / PAGE];
     if (!page_ok(a.kv, page)) return;
     const size_t idx = kv_index(page, kvh, rd.pos % PAGE, a.kv.kv_heads);
     if (a.kv.f32) {

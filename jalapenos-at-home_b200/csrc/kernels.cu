@@ -574,62 +574,87 @@ __global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __
     __shared__ __align__(16) float qsh[8][HEAD];
     __shared__ uint64_t bar;
     __shared__ int page_s[ATT_WIN];
-    ptx::grid_dependency_wait();
-    ptx::launch_dependents();
     const int g = blockIdx.x, row = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = g * group + warp;
+    const int kvh = g;
     float* qw = qsh[warp];
+    // The pass's rows and page tables were written before this pass began,
+    // and the cache rows before this row's position by earlier passes: the
+    // first window of pages is copied before waiting for the q|k|v kernel,
+    // which writes only this row's own K/V (fetched again after the wait).
     const int rows = pb.hdr->rows;
     bool valid = row < rows;
     RowDesc rd = {};
     if (valid) {
         rd = pb.row[row];
-        if (rd.pos < 0 || rd.pos >= kv.max_pos || (unsigned)rd.seq >= (unsigned)MAX_SEQS) {
-            if (threadIdx.x == 0) atomicOr(kv.err, 2);
-            *(float4*)(out + (size_t)row * out_ld + h * HEAD + 4 * lane) = make_float4(0.f, 0.f, 0.f, 0.f);
-            valid = false;
-        }
+        valid = rd.pos >= 0 && rd.pos < kv.max_pos && (unsigned)rd.seq < (unsigned)MAX_SEQS;
     }
-    if (!valid) {  // uniform over the CTA
-        if (bout) mx::emit_pieces_smem(qw, HEAD, 4, row, 0, 1, lane, 32, h * HEAD, bN, bout, sfout);
-        return;
-    }
-    if (threadIdx.x == 0) {
+    const int visible = valid ? rd.pos + 1 : 0;
+    const int npages = (visible + PAGE - 1) / PAGE;
+    const int32_t* pt = valid ? pb.page_table[rd.seq] : nullptr;
+    if (valid && threadIdx.x == 0) {
         ptx::mbar_init(&bar, 1);
         ptx::fence_barrier_init();
     }
+    auto issue_window = [&](int w0) {  // thread 0: copy pages w0 .. w0+ATT_WIN-1
+        const int wn = min(ATT_WIN, npages - w0);
+        uint32_t bytes = 0;
+        int pg[ATT_WIN];
+        for (int i = 0; i < wn; ++i) {
+            pg[i] = pt[w0 + i];
+            if (!page_ok(kv, pg[i])) pg[i] = -1;
+            else bytes += 2 * PB;
+            page_s[i] = pg[i];
+        }
+        ptx::mbar_arrive_expect_tx(&bar, bytes);
+        for (int i = 0; i < wn; ++i) {
+            if (pg[i] < 0) continue;
+            const size_t off = kv_index(pg[i], kvh, 0, kv.kv_heads) * (F32 ? 4 : 2);
+            ptx::bulk_g2s(kvs + (2 * i) * PB, (const uint8_t*)kv.k + off, PB, &bar);
+            ptx::bulk_g2s(kvs + (2 * i + 1) * PB, (const uint8_t*)kv.v + off, PB, &bar);
+        }
+    };
+    if (valid && threadIdx.x == 0) issue_window(0);
+    __syncthreads();  // the barrier is initialised before anyone waits on it
+    ptx::grid_dependency_wait();
+    ptx::launch_dependents();
+    if (row < rows && !valid) {  // uniform over the CTA
+        if (threadIdx.x == 0) atomicOr(kv.err, 2);
+        *(float4*)(out + (size_t)row * out_ld + h * HEAD + 4 * lane) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (!valid) {
+        if (bout) mx::emit_pieces_smem(qw, HEAD, 4, row, 0, 1, lane, 32, h * HEAD, bN, bout, sfout);
+        return;
+    }
     *(float4*)(qw + 4 * lane) = *(const float4*)(qkv + (size_t)row * ld + h * HEAD + 4 * lane);
-    __syncthreads();
-    const int visible = rd.pos + 1;
-    const int npages = (visible + PAGE - 1) / PAGE;
-    const int32_t* pt = pb.page_table[rd.seq];
-    const int kvh = g;
     const float scale = sqrtf(128.0f);
     float m = -INFINITY, l = 0.f;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     bool ok = true;
     for (int w0 = 0, it = 0; w0 < npages; w0 += ATT_WIN, ++it) {
         const int wn = min(ATT_WIN, npages - w0);
-        if (threadIdx.x == 0) {
-            uint32_t bytes = 0;
-            int pg[ATT_WIN];
-            for (int i = 0; i < wn; ++i) {
-                pg[i] = pt[w0 + i];
-                if (!page_ok(kv, pg[i])) pg[i] = -1;
-                else bytes += 2 * PB;
-                page_s[i] = pg[i];
-            }
-            ptx::mbar_arrive_expect_tx(&bar, bytes);
-            for (int i = 0; i < wn; ++i) {
-                if (pg[i] < 0) continue;
-                const size_t off = kv_index(pg[i], kvh, 0, kv.kv_heads) * (F32 ? 4 : 2);
-                ptx::bulk_g2s(kvs + (2 * i) * PB, (const uint8_t*)kv.k + off, PB, &bar);
-                ptx::bulk_g2s(kvs + (2 * i + 1) * PB, (const uint8_t*)kv.v + off, PB, &bar);
+        if (threadIdx.x == 0 && w0 > 0) issue_window(w0);
+        if (!ptx::mbar_wait(&bar, it & 1, ATT_WAIT)) ok = false;
+        // The q|k|v kernel of this pass wrote this row's K/V and those of the
+        // pass's earlier rows of the sequence (at most `row` positions back):
+        // fetch them again over the early copy.
+        {
+            constexpr int RB = HEAD * (F32 ? 4 : 2);  // bytes of one row: 256 or 512
+            const int lo = max(rd.pos - row, w0 * PAGE), hi = min(rd.pos, (w0 + wn) * PAGE - 1);
+            for (int p = lo + warp; p <= hi; p += group) {
+                const int pg = pt[p / PAGE];
+                if ((unsigned)pg >= (unsigned)kv.pages) continue;  // flagged when the window was copied
+                const int i = p / PAGE - w0;
+                const size_t src = kv_index(pg, kvh, p % PAGE, kv.kv_heads) * (F32 ? 4 : 2);
+                const size_t dst = (size_t)(p % PAGE) * RB;
+                for (int o = lane * 16; o < RB; o += 32 * 16) {
+                    *(uint4*)(kvs + (2 * i) * PB + dst + o) = *(const uint4*)((const uint8_t*)kv.k + src + o);
+                    *(uint4*)(kvs + (2 * i + 1) * PB + dst + o) = *(const uint4*)((const uint8_t*)kv.v + src + o);
+                }
             }
         }
-        if (!ptx::mbar_wait(&bar, it & 1, ATT_WAIT)) ok = false;
-        __syncthreads();  // page_s is visible
+        __syncthreads();  // page_s and the fresh rows are visible
         if (ok) {
             for (int i = 0; i < wn; ++i) {
                 if (page_s[i] < 0) continue;  // flagged: its positions are left out
