@@ -73,7 +73,7 @@ def run_profile(args, dist):
     target, draft = make_models(J, dist.local)
     prompt = O.prompt_ids(args.prompt, 151936, 2)
     tw, tg = target.time_pass(prompt, args.gamma + 1, reps=1)
-    dw, dg = draft.time_pass(prompt, 1, reps=1)
+    dw, dg = draft.time_pass_draft(prompt, reps=1)
     print(json.dumps({"profile": True, "target_pass_ms": tg, "draft_pass_ms": dg,
                       "target_rows": args.gamma + 1}), flush=True)
 
@@ -340,8 +340,13 @@ def main():
     bytes_per_round = ti.pass_bytes + args.gamma * di.pass_bytes
     roof_tps = peak * 1e9 * tokens_per_round / bytes_per_round
 
-    # dominant kernel: the target's gate/up projection inside a k+1-row verify pass
-    kern = {"gate_up": J.PROJ_GATE_UP, "qkv": J.PROJ_QKV, "down": J.PROJ_DOWN, "o": J.PROJ_O}
+    # dominant kernel family: the target's MXFP4 projections (k_mx_gemv); the
+    # largest, gate/up, timed as the fused kernel of a k+1-row verify pass
+    # (launched back to back on the model's stream, CUDA events, inputs left
+    # by the timed decode steps).  Algorithmic bytes per launch: the gate and
+    # up weights (codes + scales).
+    kern = {"gate_up": J.PROJ_GATE_UP, "down": J.PROJ_DOWN, "o": J.PROJ_O, "qkv": J.PROJ_QKV,
+            "head": J.PROJ_HEAD}
     kt = {}
     for name, which in kern.items():
         ms, nb = target.time_projection(0, which, args.gamma + 1, iters=20)
@@ -365,7 +370,7 @@ def main():
         "path_roofline": {"bytes_per_round_k": bytes_per_round, "roofline_tok_s": roof_tps,
                           "frac": value / dist.world / roof_tps, "achieved_gbs": path_gbs,
                           "peak_gbs": peak, "peak_kind": peak_kind},
-        "roofline": {"bound": "hbm", "kernel": "skinny MXFP4 gate/up projection, 5-row verify",
+        "roofline": {"bound": "hbm", "kernel": "k_mx_gemv<SWIGLU>: fused MXFP4 gate/up projection, k+1-row verify",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "bytes_per_launch": nb, "ms_per_launch": ms,
                      "peak_kind": peak_kind},
@@ -376,13 +381,17 @@ def main():
         "clocks": clocks.summary(),
         "wall_s": wall_total,
     }
-    # kernels in the timed steps: a pass is embed + 8 per layer + 3 for the
-    # head; the loop adds verify-setup and accept per verify pass, one
-    # bookkeeping kernel per draft pass and one round-begin kernel per round.
-    per_pass_t = 8 * ti.layers + 4
-    per_pass_d = 8 * di.layers + 4
-    line["gpu_launches"] = (args.steps * (per_pass_t + per_pass_d) + verify * (per_pass_t + 2)
-                            + drafts * (per_pass_d + 1) + rounds)
+    # kernels launched in the timed steps: per step the prefills (target and
+    # draft, 16-row chunks), every verify pass (k+1 rows), every draft step
+    # (one row; catch-ups take the same kernels) plus its bookkeeping kernel,
+    # and three loop kernels per round (round begin, verify setup, accept)
+    kt16, kd16 = target.pass_kernels(16), draft.pass_kernels(16)
+    kt_v, kd_1 = target.pass_kernels(args.gamma + 1), draft.pass_kernels(1, draft_step=True)
+    launches = 0
+    for r, _ in results:
+        launches += (r.prefill.passes // 2) * (kt16 + kd16) + r.verify.passes * kt_v
+        launches += r.draft.passes * (kd_1 + 1) + 3 * r.rounds
+    line["gpu_launches"] = launches
     if not args.no_sweep:
         sweep = {}
         for p, stream in ((0.0, True), (0.5, True), (0.0, False)):

@@ -263,10 +263,26 @@ jl_status jl_time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t row
 
 /* Launches one projection kernel of `layer` for `rows` input rows `iters`
  * times back to back on the model's stream and returns the mean device time
- * per launch (CUDA events) and the weight bytes each launch reads.  No
- * reference counterpart: it feeds the per-kernel roofline report. */
+ * per launch (CUDA events) and the weight bytes each launch reads.  On a
+ * model whose decode pass is fused (every projection MXFP4), O, GATE_UP and
+ * DOWN time the fused kernel that pass runs, on the input pieces a previous
+ * pass left behind, and HEAD with a bf16 table the final norm + tensor-core
+ * table + argmax kernels; otherwise the standalone projection.  No reference
+ * counterpart: it feeds the per-kernel roofline report. */
 jl_status jl_time_projection(jl_model* m, int layer, jl_projection which, int rows, int iters,
                              double* ms_per_launch, size_t* weight_bytes);
+
+/* jl_time_pass for one row taking the path a speculative loop's draft step
+ * takes (on a model whose draft steps have a path of their own; otherwise
+ * the same as jl_time_pass with rows = 1).  No reference counterpart: it
+ * feeds the profile of a speculative round. */
+jl_status jl_time_pass_draft(jl_model* m, const uint32_t* prompt, size_t n, size_t reps,
+                             double* wall_ms, double* gpu_ms);
+
+/* Kernels one forward pass of `rows` rows (with its next-token prediction)
+ * launches: `draft_step` nonzero for a speculative loop's draft step.  No
+ * reference counterpart: it feeds the launch count of the benchmark. */
+jl_status jl_pass_kernels(const jl_model* m, size_t rows, int draft_step, size_t* kernels);
 
 /* generate_scheduled: both models share token ids; the target has the
  * final say, so the output equals jl_generate(target, ...) whenever the

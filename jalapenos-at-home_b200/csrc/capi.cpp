@@ -291,6 +291,19 @@ jl_status jl_project(jl_model* m, int layer, jl_projection which, const float* x
     JL_GUARD({ return project(m, layer, (int)which, x, rows, y); })
 }
 
+jl_status jl_time_pass_draft(jl_model* m, const uint32_t* prompt, size_t n, size_t reps,
+                             double* wall_ms, double* gpu_ms) {
+    JL_NEED(m && prompt && wall_ms && gpu_ms, "model, prompt and outputs must be non-null");
+    JL_GUARD({ return time_pass(m, prompt, n, 1, reps, wall_ms, gpu_ms, true); })
+}
+
+jl_status jl_pass_kernels(const jl_model* m, size_t rows, int draft_step, size_t* kernels) {
+    JL_NEED(m && kernels, "model and output must be non-null");
+    JL_NEED(rows >= 1, "a pass has at least one row");
+    *kernels = pass_kernels(m, rows, draft_step != 0);
+    return JL_OK;
+}
+
 jl_status jl_project_noalloc(jl_model* m, int layer, jl_projection which, const float* x,
                              size_t rows, float* y, void* stream) {
     JL_NEED(m && x && y, "model, x and y must be non-null");

@@ -270,7 +270,7 @@ jl_status check_ids(const jl_model* m, const uint32_t* ids, size_t n) {
 
 // Stages one pass's rows from the host and runs it on m->stream.
 jl_status host_pass(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int head_rows,
-                    bool all, int layers) {
+                    bool all, int layers, bool draft_step = false) {
     PassHdr* h = m->host_hdr;
     h->rows = (int32_t)n;
     h->head_rows = head_rows;
@@ -292,6 +292,23 @@ jl_status host_pass(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int
     JL_CUDA(cudaMemcpyAsync(m->pass.page_table, m->host_page_table, sizeof(int32_t*),
                             cudaMemcpyHostToDevice, st));
     const bool full = layers == m->layers && head_rows > 0;
+    if (full && draft_step && m->dec_ok && n <= 2) {
+        // a speculative loop's draft step, captured on its own
+        cudaGraphExec_t& exec = m->draft_graph[n - 1];
+        if (!exec) {
+            cudaGraph_t g;
+            JL_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            PassCtx ctx{m, st, (int)n, (int)n, true};
+            jl_status rs = record_pass_ctx(ctx, m->layers, true);
+            cudaError_t ce = cudaStreamEndCapture(st, &g);
+            if (rs != JL_OK) return rs;
+            JL_CUDA(ce);
+            JL_CUDA(cudaGraphInstantiate(&exec, g, 0));
+            cudaGraphDestroy(g);
+        }
+        JL_CUDA(cudaGraphLaunch(exec, st));
+        return JL_OK;
+    }
     if (full && n <= (size_t)SMALL_M) {
         // one captured pass per row bucket 1, 2, 4, 8, 16
         int b = 0;
@@ -412,7 +429,7 @@ jl_status record_pass(jl_model* m, cudaStream_t stream, int rows_cap, int layers
 }
 
 jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool all,
-                  uint32_t* out_ids, float* out_logits) {
+                  uint32_t* out_ids, float* out_logits, bool draft_step) {
     if (n == 0 || c->len + n > (size_t)m->max_positions) {  // model.rs:212
         set_error("predict needs 1..%zu tokens, got %zu", (size_t)m->max_positions - c->len, n);
         return JL_ERR_INVALID_ARG;
@@ -430,7 +447,7 @@ jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool 
         const size_t take = std::min(chunk, n - done);
         const bool last = done + take == n;
         const int head_rows = all ? (int)take : (last ? 1 : 0);
-        JL_TRY(host_pass(m, c, ids + done, take, head_rows, all, m->layers));
+        JL_TRY(host_pass(m, c, ids + done, take, head_rows, all, m->layers, draft_step));
         if (head_rows) {
             const size_t first = all ? done : 0;
             JL_CUDA(cudaMemcpyAsync(m->host_out, m->pass.out_ids, head_rows * sizeof(uint32_t),
@@ -450,7 +467,7 @@ jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool 
 }
 
 jl_status time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t rows, size_t reps,
-                    double* wall_ms, double* gpu_ms) {
+                    double* wall_ms, double* gpu_ms, bool draft_step) {
     // model.rs:245-266
     if (rows == 0 || reps == 0 || n + rows > (size_t)m->max_positions) {
         set_error("time_pass needs rows > 0, reps > 0 and prompt + rows within the context");
@@ -467,7 +484,7 @@ jl_status time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t rows, 
     for (size_t r = 0; r < reps + 2; ++r) {
         const auto t0 = std::chrono::steady_clock::now();
         JL_CUDA(cudaEventRecord(m->ev0, m->stream));
-        JL_TRY(predict(m, c, tokens.data(), rows, rows > 1, out.data(), nullptr));
+        JL_TRY(predict(m, c, tokens.data(), rows, rows > 1, out.data(), nullptr, draft_step));
         JL_CUDA(cudaEventRecord(m->ev1, m->stream));
         JL_CUDA(cudaEventSynchronize(m->ev1));
         wall.push_back(std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
@@ -537,7 +554,42 @@ jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters
     *m->host_hdr = h;
     JL_CUDA(cudaMemcpyAsync(m->pass.hdr, m->host_hdr, sizeof(PassHdr), cudaMemcpyHostToDevice, m->stream));
     PassCtx c{m, m->stream, rows, rows};
+    const bool fused = m->mx.fused && rows <= mx_max_tokens();
+    const int hid = m->hidden, tiles = hid / 128;
     auto launch = [&]() -> jl_status {
+        if (fused && which == 1) {  // o: residual add, pieces and sums of squares out
+            MxFuse f;
+            f.b = m->mx.battn;
+            f.sfb = m->mx.sfattn;
+            f.bout = m->mx.bx;
+            f.sfout = m->mx.sfx;
+            f.part_out = m->mx.part;
+            f.next_w = L.post_ln;
+            return mx_project_fused(c, L.mx_o, MXE_ADD, f, m->s.x, hid);
+        }
+        if (fused && which == 2) {  // gate/up: input RMSNorm, SwiGLU, pieces out
+            MxFuse f;
+            f.b = m->mx.bx;
+            f.sfb = m->mx.sfx;
+            f.part_in = m->mx.part;
+            f.part_tiles = tiles;
+            f.norm_width = hid;
+            f.bout = m->mx.bact;
+            f.sfout = m->mx.sfact;
+            return mx_project_fused(c, L.mx_gateup, MXE_SWIGLU, f, nullptr, m->inter);
+        }
+        if (which == 4 && m->bf_head.a && rows <= mx_max_tokens())  // final norm + bf16 table + argmax
+            return mx_head_fused(c, m->bf_head, m->final_norm, m->s.logits, m->vocab);
+        if (fused && which == 3) {  // down: residual add, pieces and sums of squares out
+            MxFuse f;
+            f.b = m->mx.bact;
+            f.sfb = m->mx.sfact;
+            f.bout = m->mx.bx;
+            f.sfout = m->mx.sfx;
+            f.part_out = m->mx.part;
+            f.next_w = L.in_ln;
+            return mx_project_fused(c, L.mx_down, MXE_ADD, f, m->s.x, hid);
+        }
         switch (which) {
             case 0: return launch_qkv(c, L);
             case 1: return launch_o(c, L);
@@ -560,6 +612,18 @@ jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters
         default: *bytes = m->head.bytes();
     }
     return JL_OK;
+}
+
+size_t pass_kernels(const jl_model* m, size_t rows, bool draft_step) {
+    const size_t L = (size_t)m->layers;
+    if (draft_step && m->dec_ok && rows <= 2)  // embed, 5 per layer, head pieces + table + argmax
+        return 1 + 5 * L + (m->bf_head.a ? 3 : (m->mx_head.a ? 4 : 3));
+    if (m->mx.fused && rows <= (size_t)mx_max_tokens())  // embed + norm pieces, 5 per layer, head
+        return 2 + 5 * L + (m->bf_head.a ? 3 : (m->mx_head.a ? 4 : 3));
+    // embed, 8 per layer (norm, q|k|v, rope, attention, o, norm, gate/up, down) with
+    // an extra pieces kernel before each tensor-core projection, head
+    const bool mx = !m->lw.empty() && m->lw[0].mx_qkv.a && rows <= (size_t)mx_max_tokens();
+    return 1 + (mx ? 12 : 8) * L + (m->mx_head.a && rows <= (size_t)mx_max_tokens() ? 4 : 3);
 }
 
 jl_status hidden(jl_model* m, const uint32_t* ids, size_t n, size_t layers, float* out) {

@@ -219,6 +219,7 @@ struct jl_model {
     cudaStream_t stream = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     cudaGraphExec_t small_graph[5] = {};  // full pass for rows <= 1, 2, 4, 8, 16
+    cudaGraphExec_t draft_graph[2] = {};  // draft-step pass of 1 or 2 rows (profiling)
     std::vector<jl::SpecGraph*> spec_graphs;  // owned; freed by model_free
     std::vector<jl_cache*> caches;              // live caches; detached by model_free
     int* counters = nullptr;              // zeroed split-K / reduction counters
@@ -255,13 +256,14 @@ jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head);
 // Sets kernel attributes once per device, before any stream capture.
 jl_status configure_kernels();
 jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool all,
-                  uint32_t* out_ids, float* out_logits);
+                  uint32_t* out_ids, float* out_logits, bool draft_step = false);
 jl_status hidden(jl_model* m, const uint32_t* ids, size_t n, size_t layers, float* out);
 jl_status time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t rows, size_t reps,
-                    double* wall_ms, double* gpu_ms);
+                    double* wall_ms, double* gpu_ms, bool draft_step = false);
 jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters, double* ms,
                           size_t* bytes);
 jl_status project(jl_model* m, int layer, int which, const float* x, size_t rows, float* y);
+size_t pass_kernels(const jl_model* m, size_t rows, bool draft_step);
 jl_status generate(jl_model* m, const uint32_t* prompt, size_t n, size_t count, uint32_t* out,
                    size_t cap, size_t* out_len);
 jl_status generate_speculative(jl_model* target, jl_model* draft, const uint32_t* prompt,

@@ -564,6 +564,8 @@ void model_free(jl_model* m) {
     m->caches.clear();
     for (auto& g : m->small_graph)
         if (g) cudaGraphExecDestroy(g);
+    for (auto& g : m->draft_graph)
+        if (g) cudaGraphExecDestroy(g);
     cudaFree(m->arena);
     cudaFree(m->rope);
     cudaFree(m->kv.base);

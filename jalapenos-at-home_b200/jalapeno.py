@@ -36,7 +36,7 @@ EXPORTS = (
     "jl_cache_truncate", "jl_predict", "jl_next_token", "jl_hidden", "jl_generate",
     "jl_schedule_fixed", "jl_schedule_adaptive", "jl_spec_options_default",
     "jl_generate_speculative", "jl_time_pass", "jl_time_projection", "jl_project",
-    "jl_project_noalloc",
+    "jl_project_noalloc", "jl_pass_kernels", "jl_time_pass_draft",
 )
 PROJ_QKV, PROJ_O, PROJ_GATE_UP, PROJ_DOWN, PROJ_HEAD = 0, 1, 2, 3, 4
 
@@ -143,6 +143,9 @@ def _load():
                                 ctypes.POINTER(ctypes.c_double), ctypes.POINTER(sz)], ctypes.c_int),
         "jl_project": ([vp, ctypes.c_int, ctypes.c_int, f32p, sz, f32p], ctypes.c_int),
         "jl_project_noalloc": ([vp, ctypes.c_int, ctypes.c_int, vp, sz, vp, vp], ctypes.c_int),
+        "jl_pass_kernels": ([vp, sz, ctypes.c_int, ctypes.POINTER(sz)], ctypes.c_int),
+        "jl_time_pass_draft": ([vp, u32p, sz, sz, ctypes.POINTER(ctypes.c_double),
+                                ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -354,6 +357,20 @@ class Model:
         for the model's stream.  See jl_project_noalloc in include/jalapeno.h."""
         check(lib.jl_project_noalloc(self._h, layer, which, ctypes.c_void_p(x_ptr), rows,
                                      ctypes.c_void_p(y_ptr), ctypes.c_void_p(stream or None)))
+
+    def time_pass_draft(self, prompt, reps: int = 15) -> tuple[float, float]:
+        """time_pass of one row on the draft-step path: median (wall_ms, gpu_ms)."""
+        t = u32(prompt)
+        wall, gpu = ctypes.c_double(), ctypes.c_double()
+        check(lib.jl_time_pass_draft(self._h, _p(t, ctypes.c_uint32), len(t), reps,
+                                     ctypes.byref(wall), ctypes.byref(gpu)))
+        return wall.value, gpu.value
+
+    def pass_kernels(self, rows: int, draft_step: bool = False) -> int:
+        """Kernels one forward pass of `rows` rows launches (see jl_pass_kernels)."""
+        n = ctypes.c_size_t()
+        check(lib.jl_pass_kernels(self._h, rows, int(draft_step), ctypes.byref(n)))
+        return n.value
 
     def time_projection(self, layer: int, which: int, rows: int, iters: int = 20) -> tuple[float, int]:
         """Mean device ms per launch of one projection kernel, and its weight bytes."""
