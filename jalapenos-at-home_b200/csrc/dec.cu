@@ -8,7 +8,7 @@
 // them (MXFP4 codes and scales, exactly as the checkpoint stores them) into
 // shared memory with bulk copies BEFORE it waits for the previous kernel
 // (weights never depend on it).  After the wait it loads the f32 input rows,
-// normalises them (the same arithmetic as k_rmsnorm), and each warp computes
+// normalises them (RMSNorm, lib.rs:268-290), and each warp computes
 // its rows' dot products: lanes take 32-element blocks, decode E2M1 pairs in
 // hardware (cvt.rn.f16x2.e2m1x2), apply the block's E8M0 scale, and the warp
 // sums.  Epilogues: q|k|v (QK-RMSNorm, RoPE, K/V appended to the cache),
@@ -54,29 +54,49 @@ __device__ __forceinline__ void dec_copy_rows(const DecTile& t, int r0, int n, i
 
 // Loads M input rows (f32, width K) into shared memory in the swizzled chunk
 // layout; with `w` set, as the RMSNorm x / sqrt(mean(x^2) + 1e-6) * w
-// (lib.rs:268-290, the arithmetic of k_rmsnorm).  Whole CTA.
+// (lib.rs:268-290).  Whole CTA.
+// Each thread holds at most DEC_XCHUNKS float4 chunks of a row in registers,
+// so x is read from global memory once.
+constexpr int DEC_XCHUNKS = 4;
+
 __device__ __forceinline__ void dec_load_x(const float* __restrict__ x, int ldx, int M, int K,
                                            const uint16_t* __restrict__ w, float4* xs4, float* red) {
     const int K4 = K / 4;
     for (int m = 0; m < M; ++m) {
         const float* xr = x + (size_t)m * ldx;
+        float4 v[DEC_XCHUNKS];
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < DEC_XCHUNKS; ++i) {
+            const int c = threadIdx.x + i * blockDim.x;
+            v[i] = c < K4 ? reinterpret_cast<const float4*>(xr)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         float size = 1.f;
         if (w) {
-            float ss = 0.f;
-            for (int j = threadIdx.x; j < K; j += blockDim.x) ss = fmaf(xr[j], xr[j], ss);
+            // each thread sums the squares of its chunks, then the CTA adds
+            // the threads' sums (block_sum)
+#pragma unroll
+            for (int i = 0; i < DEC_XCHUNKS; ++i) {
+                ss = fmaf(v[i].x, v[i].x, ss);
+                ss = fmaf(v[i].y, v[i].y, ss);
+                ss = fmaf(v[i].z, v[i].z, ss);
+                ss = fmaf(v[i].w, v[i].w, ss);
+            }
             ss = block_sum(ss, red);
             size = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-6f));
         }
-        for (int c = threadIdx.x; c < K4; c += blockDim.x) {
-            float4 v = reinterpret_cast<const float4*>(xr)[c];
+#pragma unroll
+        for (int i = 0; i < DEC_XCHUNKS; ++i) {
+            const int c = threadIdx.x + i * blockDim.x;
+            if (c >= K4) continue;
             if (w) {
                 const uint2 wv = *reinterpret_cast<const uint2*>(w + 4 * c);
-                v.x = __fmul_rn(__fdiv_rn(v.x, size), bf16f(wv.x & 0xffffu));
-                v.y = __fmul_rn(__fdiv_rn(v.y, size), bf16f(wv.x >> 16));
-                v.z = __fmul_rn(__fdiv_rn(v.z, size), bf16f(wv.y & 0xffffu));
-                v.w = __fmul_rn(__fdiv_rn(v.w, size), bf16f(wv.y >> 16));
+                v[i].x = __fmul_rn(__fdiv_rn(v[i].x, size), bf16f(wv.x & 0xffffu));
+                v[i].y = __fmul_rn(__fdiv_rn(v[i].y, size), bf16f(wv.x >> 16));
+                v[i].z = __fmul_rn(__fdiv_rn(v[i].z, size), bf16f(wv.y & 0xffffu));
+                v[i].w = __fmul_rn(__fdiv_rn(v[i].w, size), bf16f(wv.y >> 16));
             }
-            xs4[m * K4 + dec_swz(c)] = v;
+            xs4[m * K4 + dec_swz(c)] = v[i];
         }
     }
 }
@@ -127,129 +147,16 @@ __device__ __forceinline__ void dec_dot(const uint8_t* wr, const uint8_t* sr, in
 }
 
 // ---------------------------------------------------------------------------
-// q|k|v: CTA = one head (128 rows of q, k or v), 16 warps x 8 rows.
+// CTA = DEC_TR output rows, 8 warps.  Output rows are numbered across up to
+// three stacked matrices (q | k | v; a tile never straddles two); SwiGLU
+// tiles take DEC_TR gate rows and the matching up rows.
 
-struct DecQkvArgs {
-    DecTile q, k, v;
-    int K, q_heads, kv_heads;
-    const float* x;          // residual stream [rows][K]
-    const uint16_t* norm;    // input_layernorm
-    const uint16_t* qn;      // q_norm / k_norm
-    const uint16_t* kn;
-    const float2* rope;
-    PassBuf pb;
-    KvView kv;
-    float* q_out;            // [rows][ld]
-    int ld;
-    int mcap;
-};
-
-template <int M>
-__global__ void __launch_bounds__(512) k_dec_qkv(DecQkvArgs a) {
-    extern __shared__ __align__(128) uint8_t dsm[];
-    __shared__ uint64_t bar;
-    __shared__ float red[32];
-    __shared__ float res[DEC_MAXROWS][HEAD];
-    const int h = blockIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int K = a.K;
-    const bool is_q = h < a.q_heads, is_k = !is_q && h < a.q_heads + a.kv_heads;
-    const int kvh = is_k ? h - a.q_heads : h - a.q_heads - a.kv_heads;
-    const DecTile& t = is_q ? a.q : (is_k ? a.k : a.v);
-    const int r0 = is_q ? h * HEAD : kvh * HEAD;
-    uint8_t* wsm = dsm;
-    uint8_t* ssm = dsm + HEAD * (K / 2);
-    float4* xs4 = reinterpret_cast<float4*>(ssm + HEAD * (K / 32));
-    if (threadIdx.x == 0) {
-        ptx::mbar_init(&bar, 1);
-        ptx::fence_barrier_init();
-        ptx::mbar_arrive_expect_tx(&bar, (uint32_t)(HEAD * (K / 2) + HEAD * (K / 32)));
-        dec_copy_rows(t, r0, HEAD, K, wsm, ssm, &bar);
-    }
-    __syncthreads();  // the barrier is initialised before anyone waits on it
-    ptx::grid_dependency_wait();
-    ptx::launch_dependents();
-    const int rows = min(a.pb.hdr->rows, a.mcap);
-    // warp m finishes row m: its position, RoPE factors and cache page are
-    // fetched now, while the input loads and the dot products run
-    RowDesc rd = {};
-    float2 c0 = make_float2(1.f, 0.f), c1 = make_float2(1.f, 0.f);
-    int page = -1;
-    bool row_ok = false;
-    if (warp < M && warp < rows) {
-        rd = a.pb.row[warp];
-        row_ok = rd.pos >= 0 && rd.pos < a.kv.max_pos && (unsigned)rd.seq < (unsigned)MAX_SEQS;
-        if (row_ok) {
-            c0 = a.rope[(size_t)rd.pos * HALF + lane];
-            c1 = a.rope[(size_t)rd.pos * HALF + lane + 32];
-            if (!is_q) page = a.pb.page_table[rd.seq][rd.pos / PAGE];
-        }
-    }
-    dec_load_x(a.x, K, M, K, a.norm, xs4, red);
-    const bool ok = ptx::mbar_wait(&bar, 0, DEC_WAIT);
-    __syncthreads();
-    if (!ok) {
-        if (threadIdx.x == 0) atomicOr(a.kv.err, 4);
-        return;
-    }
-    for (int i = 0; i < HEAD / 16; ++i) {
-        const int r = warp * (HEAD / 16) + i;
-        float o[M];
-        dec_dot<M>(wsm + (size_t)r * (K / 2), ssm + (size_t)r * (K / 32), K, xs4, lane, o);
-        if (lane == 0)
-#pragma unroll
-            for (int m = 0; m < M; ++m) res[m][r] = o[m];
-    }
-    __syncthreads();
-    // warp m finishes row m, as k_qk_rope_kv does: lane owns dims l, l+32, l+64, l+96
-    if (warp >= M || warp >= rows) return;
-    const int m = warp;
-    float a0 = res[m][lane], a1 = res[m][lane + 32], a2 = res[m][lane + 64], a3 = res[m][lane + 96];
-    if (!row_ok) {
-        if (lane == 0) atomicOr(a.kv.err, 2);
-        return;
-    }
-    if (is_q || is_k) {
-        const uint16_t* gw = is_q ? a.qn : a.kn;
-        float ss = fmaf(a0, a0, fmaf(a1, a1, fmaf(a2, a2, a3 * a3)));
-        ss = warp_sum(ss);
-        const float size = sqrtf(__fadd_rn(__fdiv_rn(ss, 128.0f), 1e-6f));
-        a0 = __fmul_rn(__fdiv_rn(a0, size), bf16f(gw[lane]));
-        a1 = __fmul_rn(__fdiv_rn(a1, size), bf16f(gw[lane + 32]));
-        a2 = __fmul_rn(__fdiv_rn(a2, size), bf16f(gw[lane + 64]));
-        a3 = __fmul_rn(__fdiv_rn(a3, size), bf16f(gw[lane + 96]));
-        // lib.rs:306-313: out[i] = a cos - b sin; out[i+64] = b cos + a sin
-        const float b0 = __fsub_rn(__fmul_rn(a0, c0.x), __fmul_rn(a2, c0.y));
-        const float b2 = __fadd_rn(__fmul_rn(a2, c0.x), __fmul_rn(a0, c0.y));
-        const float b1 = __fsub_rn(__fmul_rn(a1, c1.x), __fmul_rn(a3, c1.y));
-        const float b3 = __fadd_rn(__fmul_rn(a3, c1.x), __fmul_rn(a1, c1.y));
-        a0 = b0; a1 = b1; a2 = b2; a3 = b3;
-    }
-    if (is_q) {
-        float* d = a.q_out + (size_t)m * a.ld + h * HEAD;
-        d[lane] = a0; d[lane + 32] = a1; d[lane + 64] = a2; d[lane + 96] = a3;
-        return;
-    }
-    if (!page_ok(a.kv, page)) return;
-    const size_t idx = kv_index(page, kvh, rd.pos % PAGE, a.kv.kv_heads);
-    if (a.kv.f32) {
-        float* d = (float*)(is_k ? a.kv.k : a.kv.v) + idx;
-        d[lane] = a0; d[lane + 32] = a1; d[lane + 64] = a2; d[lane + 96] = a3;
-    } else {
-        uint16_t* d = (uint16_t*)(is_k ? a.kv.k : a.kv.v) + idx;
-        d[lane] = f2bf16(a0); d[lane + 32] = f2bf16(a1);
-        d[lane + 64] = f2bf16(a2); d[lane + 96] = f2bf16(a3);
-    }
-}
-
-// ---------------------------------------------------------------------------
-// residual add (o, down) and SwiGLU (gate/up): CTA = DEC_TR output rows
-// (SwiGLU: DEC_TR gate rows and the matching up rows), 8 warps.
-
-constexpr int DEC_TR = 32;
+constexpr int DEC_TR = 16;
+enum : int { DEC_STORE = 0, DEC_ADD = 1, DEC_SWIGLU = 2 };
 
 struct DecArgs {
-    DecTile w0, w1;          // the matrix (SwiGLU: gate, up)
+    DecTile w[3];            // stacked matrices (SwiGLU: gate, up)
+    int rows[3];             // their row counts (unused entries 0)
     int K, out_rows;
     const float* x;          // input rows [rows][K]
     const uint16_t* norm;    // RMSNorm weight applied to x first, or null
@@ -260,7 +167,7 @@ struct DecArgs {
     int* err;
 };
 
-template <int M, bool SWIGLU>
+template <int M, int EPI>
 __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
     extern __shared__ __align__(128) uint8_t dsm[];
     __shared__ uint64_t bar;
@@ -269,17 +176,21 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
     const int K = a.K;
     const int r0 = blockIdx.x * DEC_TR;
     const int n = min(DEC_TR, a.out_rows - r0);
-    const int nm = SWIGLU ? 2 : 1;
-    uint8_t* wsm = dsm;                                   // [nm][DEC_TR][K/2]
-    uint8_t* ssm = dsm + nm * DEC_TR * (K / 2);           // [nm][DEC_TR][K/32]
-    float4* xs4 = reinterpret_cast<float4*>(ssm + nm * DEC_TR * (K / 32));
+    constexpr int NM = EPI == DEC_SWIGLU ? 2 : 1;
+    // the matrix this tile's rows come from, and the first local row
+    int mat = 0, lr0 = r0;
+    if (EPI != DEC_SWIGLU)
+        while (mat < 2 && lr0 >= a.rows[mat]) lr0 -= a.rows[mat++];
+    uint8_t* wsm = dsm;                                   // [NM][DEC_TR][K/2]
+    uint8_t* ssm = dsm + NM * DEC_TR * (K / 2);           // [NM][DEC_TR][K/32]
+    float4* xs4 = reinterpret_cast<float4*>(ssm + NM * DEC_TR * (K / 32));
     if (threadIdx.x == 0) {
         ptx::mbar_init(&bar, 1);
         ptx::fence_barrier_init();
-        ptx::mbar_arrive_expect_tx(&bar, (uint32_t)(nm * n * (K / 2 + K / 32)));
-        dec_copy_rows(a.w0, r0, n, K, wsm, ssm, &bar);
-        if (SWIGLU)
-            dec_copy_rows(a.w1, r0, n, K, wsm + DEC_TR * (K / 2), ssm + DEC_TR * (K / 32), &bar);
+        ptx::mbar_arrive_expect_tx(&bar, (uint32_t)(NM * n * (K / 2 + K / 32)));
+        dec_copy_rows(a.w[mat], lr0, n, K, wsm, ssm, &bar);
+        if (EPI == DEC_SWIGLU)
+            dec_copy_rows(a.w[1], r0, n, K, wsm + DEC_TR * (K / 2), ssm + DEC_TR * (K / 32), &bar);
     }
     __syncthreads();  // the barrier is initialised before anyone waits on it
     ptx::grid_dependency_wait();
@@ -295,7 +206,7 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
     for (int r = warp; r < n; r += 8) {
         float o[M];
         dec_dot<M>(wsm + (size_t)r * (K / 2), ssm + (size_t)r * (K / 32), K, xs4, lane, o);
-        if (SWIGLU) {
+        if (EPI == DEC_SWIGLU) {
             float u[M];
             dec_dot<M>(wsm + (size_t)(DEC_TR + r) * (K / 2), ssm + (size_t)(DEC_TR + r) * (K / 32), K, xs4,
                        lane, u);
@@ -310,15 +221,15 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
             for (int m = 0; m < M; ++m)
                 if (m < rows) {
                     float* d = a.y + (size_t)m * a.ldy + r0 + r;
-                    *d = __fadd_rn(*d, o[m]);  // residual (model.rs:178-186)
+                    *d = EPI == DEC_ADD ? __fadd_rn(*d, o[m]) : o[m];  // residual (model.rs:178-186)
                 }
         }
     }
 }
 
-template <int M, bool SWIGLU>
+template <int M, int EPI>
 jl_status configure_dec_proj(int smem) {
-    JL_CUDA(cudaFuncSetAttribute(k_dec_proj<M, SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    JL_CUDA(cudaFuncSetAttribute(k_dec_proj<M, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     return JL_OK;
 }
 
@@ -327,41 +238,39 @@ size_t dec_proj_smem(int K, bool swiglu) {
     return (size_t)nm * DEC_TR * (K / 2 + K / 32) + (size_t)DEC_MAXROWS * K * 4;
 }
 
-size_t dec_qkv_smem(int K) { return (size_t)HEAD * (K / 2 + K / 32) + (size_t)DEC_MAXROWS * K * 4; }
-
 DecTile tile_of(const Mat& w) { return DecTile{(const uint8_t*)w.data, w.scales}; }
 
 }  // namespace
 
 bool dec_supported(const jl_model* m) {
     if (m->lw.empty()) return false;
-    const int QW = m->q_heads * HEAD;
+    const int QW = m->q_heads * HEAD, KVW = m->kv_heads * HEAD;
     auto ok = [](int K) { return K % 512 == 0; };  // scale rows of whole 16-byte words
     for (const auto& L : m->lw)
         if (L.q.kind != MAT_MXFP4 || L.k.kind != MAT_MXFP4 || L.v.kind != MAT_MXFP4 || L.o.kind != MAT_MXFP4 ||
             L.gate.kind != MAT_MXFP4 || L.up.kind != MAT_MXFP4 || L.down.kind != MAT_MXFP4)
             return false;
-    return ok(m->hidden) && ok(QW) && ok(m->inter) && dec_qkv_smem(m->hidden) <= 200 * 1024 &&
-           dec_proj_smem(std::max(m->hidden, std::max(QW, m->inter)), true) <= 200 * 1024 &&
-           m->q_heads / m->kv_heads <= 8;
+    const int widest = std::max(m->hidden, std::max(QW, m->inter));
+    if (widest / 4 > DEC_XCHUNKS * 256) return false;  // input row in registers (256-thread CTAs)
+    return ok(m->hidden) && ok(QW) && ok(m->inter) && QW % DEC_TR == 0 && KVW % DEC_TR == 0 &&
+           dec_proj_smem(widest, true) <= 200 * 1024 && m->q_heads / m->kv_heads <= 8;
 }
 
 constexpr int DEC_SMEM_MAX = 200 * 1024;  // dec_supported keeps every launch under this
 
 jl_status dec_configure() {
-    const int proj = DEC_SMEM_MAX;
-    JL_TRY((configure_dec_proj<1, false>(proj)));
-    JL_TRY((configure_dec_proj<2, false>(proj)));
-    JL_TRY((configure_dec_proj<1, true>(proj)));
-    JL_TRY((configure_dec_proj<2, true>(proj)));
-    const int qkv = DEC_SMEM_MAX;
-    JL_CUDA(cudaFuncSetAttribute(k_dec_qkv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, qkv));
-    JL_CUDA(cudaFuncSetAttribute(k_dec_qkv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, qkv));
+    JL_TRY((configure_dec_proj<1, DEC_STORE>(DEC_SMEM_MAX)));
+    JL_TRY((configure_dec_proj<2, DEC_STORE>(DEC_SMEM_MAX)));
+    JL_TRY((configure_dec_proj<1, DEC_ADD>(DEC_SMEM_MAX)));
+    JL_TRY((configure_dec_proj<2, DEC_ADD>(DEC_SMEM_MAX)));
+    JL_TRY((configure_dec_proj<1, DEC_SWIGLU>(DEC_SMEM_MAX)));
+    JL_TRY((configure_dec_proj<2, DEC_SWIGLU>(DEC_SMEM_MAX)));
     return JL_OK;
 }
 
-// The draft-step pass: embedding, then per layer q|k|v, attention, o, gate/up
-// and down on CUDA cores (attention as in the decode pass).
+// The draft-step pass: embedding, then per layer the raw q|k|v projection,
+// attention (which applies QK-RMSNorm and RoPE and appends K/V), o, gate/up
+// and down, all projections on CUDA cores.
 jl_status record_dec_pass(const PassCtx& c, int layers) {
     const jl_model* m = c.m;
     const int M = c.rows_cap;
@@ -369,37 +278,19 @@ jl_status record_dec_pass(const PassCtx& c, int layers) {
         set_error("draft-step pass takes 1..%d rows", DEC_MAXROWS);
         return JL_ERR_INVALID_ARG;
     }
-    const int h = m->hidden, QW = m->q_heads * HEAD;
+    const int h = m->hidden, QW = m->q_heads * HEAD, KVW = m->kv_heads * HEAD;
     JL_TRY(launch_embed(c));
     for (int l = 0; l < layers; ++l) {
         const LayerW& L = m->lw[l];
-        DecQkvArgs q{};
-        q.q = tile_of(L.q);
-        q.k = tile_of(L.k);
-        q.v = tile_of(L.v);
-        q.K = h;
-        q.q_heads = m->q_heads;
-        q.kv_heads = m->kv_heads;
-        q.x = m->s.x;
-        q.norm = L.in_ln;
-        q.qn = L.q_norm;
-        q.kn = L.k_norm;
-        q.rope = (const float2*)m->rope;
-        q.pb = m->pass;
-        q.kv = kv_view(m, l);
-        q.q_out = m->s.qkv;
-        q.ld = qkv_ld(m);
-        q.mcap = M;
-        const dim3 qg(m->q_heads + 2 * m->kv_heads);
-        const size_t qs = dec_qkv_smem(h);
-        if (M == 1) JL_TRY(launch_pdl(k_dec_qkv<1>, qg, dim3(512), qs, c.stream, q));
-        else JL_TRY(launch_pdl(k_dec_qkv<2>, qg, dim3(512), qs, c.stream, q));
-        JL_TRY(launch_attention(c, l, false));  // lib.rs:401-441
-        auto proj = [&](const Mat& w0, const Mat* w1, int K, const float* x, const uint16_t* norm, float* y,
-                        int ldy, int out_rows) -> jl_status {
+        auto proj = [&](int epi, const Mat* w0, const Mat* w1, const Mat* w2, int K, const float* x,
+                        const uint16_t* norm, float* y, int ldy, int out_rows) -> jl_status {
             DecArgs d{};
-            d.w0 = tile_of(w0);
-            if (w1) d.w1 = tile_of(*w1);
+            const Mat* ws[3] = {w0, w1, w2};
+            for (int i = 0; i < 3; ++i)
+                if (ws[i]) {
+                    d.w[i] = tile_of(*ws[i]);
+                    d.rows[i] = ws[i]->rows;
+                }
             d.K = K;
             d.out_rows = out_rows;
             d.x = x;
@@ -410,17 +301,24 @@ jl_status record_dec_pass(const PassCtx& c, int layers) {
             d.mcap = M;
             d.err = m->counters;
             const dim3 g((out_rows + DEC_TR - 1) / DEC_TR);
-            const size_t sm = dec_proj_smem(K, w1 != nullptr);
-            if (w1) {
-                if (M == 1) return launch_pdl(k_dec_proj<1, true>, g, dim3(256), sm, c.stream, d);
-                return launch_pdl(k_dec_proj<2, true>, g, dim3(256), sm, c.stream, d);
+            const size_t sm = dec_proj_smem(K, epi == DEC_SWIGLU);
+            const dim3 b(256);
+            switch (epi * 2 + (M - 1)) {
+                case DEC_STORE * 2: return launch_pdl(k_dec_proj<1, DEC_STORE>, g, b, sm, c.stream, d);
+                case DEC_STORE * 2 + 1: return launch_pdl(k_dec_proj<2, DEC_STORE>, g, b, sm, c.stream, d);
+                case DEC_ADD * 2: return launch_pdl(k_dec_proj<1, DEC_ADD>, g, b, sm, c.stream, d);
+                case DEC_ADD * 2 + 1: return launch_pdl(k_dec_proj<2, DEC_ADD>, g, b, sm, c.stream, d);
+                case DEC_SWIGLU * 2: return launch_pdl(k_dec_proj<1, DEC_SWIGLU>, g, b, sm, c.stream, d);
+                default: return launch_pdl(k_dec_proj<2, DEC_SWIGLU>, g, b, sm, c.stream, d);
             }
-            if (M == 1) return launch_pdl(k_dec_proj<1, false>, g, dim3(256), sm, c.stream, d);
-            return launch_pdl(k_dec_proj<2, false>, g, dim3(256), sm, c.stream, d);
         };
-        JL_TRY(proj(L.o, nullptr, QW, m->s.attn, nullptr, m->s.x, h, h));                // lib.rs:444-449
-        JL_TRY(proj(L.gate, &L.up, h, m->s.x, L.post_ln, m->s.act, m->inter, m->inter));  // lib.rs:459-463
-        JL_TRY(proj(L.down, nullptr, m->inter, m->s.act, nullptr, m->s.x, h, h));         // lib.rs:464-467
+        // lib.rs:353-355: raw q | k | v, normalised and rotated by the attention kernel
+        JL_TRY(proj(DEC_STORE, &L.q, &L.k, &L.v, h, m->s.x, L.in_ln, m->s.qkv, qkv_ld(m), QW + 2 * KVW));
+        JL_TRY(launch_attention_raw(c, l, L.q_norm, L.k_norm));                                  // lib.rs:363-441
+        JL_TRY(proj(DEC_ADD, &L.o, nullptr, nullptr, QW, m->s.attn, nullptr, m->s.x, h, h));         // lib.rs:444-449
+        JL_TRY(proj(DEC_SWIGLU, &L.gate, &L.up, nullptr, h, m->s.x, L.post_ln, m->s.act, m->inter,
+                    m->inter));                                                                     // lib.rs:459-463
+        JL_TRY(proj(DEC_ADD, &L.down, nullptr, nullptr, m->inter, m->s.act, nullptr, m->s.x, h, h));  // lib.rs:464-467
     }
     return JL_OK;
 }

@@ -285,6 +285,9 @@ jl_status launch_rmsnorm(const PassCtx& c, const float* x, const uint16_t* w, fl
 jl_status launch_qkv(const PassCtx& c, const LayerW& L);
 jl_status launch_qk_rope_kv(const PassCtx& c, int layer, const LayerW& L);
 jl_status launch_attention(const PassCtx& c, int layer, bool pieces = false);
+// Decode attention on raw q|k|v rows: it applies QK-RMSNorm and RoPE itself
+// and appends this pass's K/V to the cache (the draft-step pass).
+jl_status launch_attention_raw(const PassCtx& c, int layer, const uint16_t* qn, const uint16_t* kn);
 jl_status launch_o(const PassCtx& c, const LayerW& L);
 jl_status launch_gateup(const PassCtx& c, const LayerW& L);
 jl_status launch_down(const PassCtx& c, const LayerW& L);

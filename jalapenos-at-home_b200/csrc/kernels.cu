@@ -563,12 +563,44 @@ constexpr uint32_t ATT_WAIT = 1u << 22;  // polls before the page copy reports f
 __host__ __device__ constexpr int att_page_bytes(int f32) { return PAGE * HEAD * (f32 ? 4 : 2); }
 __host__ __device__ constexpr int att_smem(int f32) { return 2 * ATT_WIN * att_page_bytes(f32); }
 
-template <int F32>
+// RAW (passes of at most two rows, the draft-step pass): q|k|v are the raw
+// projections.  Each warp normalises (QK-RMSNorm) and rotates (RoPE) its
+// query head; warp j computes row j's K (normalised, rotated) and V for this
+// KV head, which stand in for the cache rows of this pass, and the row's own
+// K/V are appended to the cache (lib.rs:363-396).
+struct AttnRaw {
+    const uint16_t* qn;   // q_norm / k_norm weights
+    const uint16_t* kn;
+    const float2* rope;
+    int k_off, v_off;     // columns of k and v in a q|k|v row
+};
+
+// QK-RMSNorm and RoPE of one head held as dims (l, l+32, l+64, l+96) by lane
+// l (lib.rs:306-313, 372-388; the arithmetic of k_qk_rope_kv).
+__device__ __forceinline__ void norm_rope4(float& a0, float& a1, float& a2, float& a3, const uint16_t* gw,
+                                           float2 c0, float2 c1, int lane) {
+    float ss = fmaf(a0, a0, fmaf(a1, a1, fmaf(a2, a2, a3 * a3)));
+    ss = warp_sum(ss);
+    const float size = sqrtf(__fadd_rn(__fdiv_rn(ss, 128.0f), 1e-6f));
+    a0 = __fmul_rn(__fdiv_rn(a0, size), bf16f(gw[lane]));
+    a1 = __fmul_rn(__fdiv_rn(a1, size), bf16f(gw[lane + 32]));
+    a2 = __fmul_rn(__fdiv_rn(a2, size), bf16f(gw[lane + 64]));
+    a3 = __fmul_rn(__fdiv_rn(a3, size), bf16f(gw[lane + 96]));
+    const float b0 = __fsub_rn(__fmul_rn(a0, c0.x), __fmul_rn(a2, c0.y));
+    const float b2 = __fadd_rn(__fmul_rn(a2, c0.x), __fmul_rn(a0, c0.y));
+    const float b1 = __fsub_rn(__fmul_rn(a1, c1.x), __fmul_rn(a3, c1.y));
+    const float b3 = __fadd_rn(__fmul_rn(a3, c1.x), __fmul_rn(a1, c1.y));
+    a0 = b0; a1 = b1; a2 = b2; a3 = b3;
+}
+
+template <int F32, int RAW>
 __global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __restrict__ qkv, int ld,
                                                      int group, KvView kv, float* __restrict__ out,
                                                      int out_ld, uint8_t* __restrict__ bout,
-                                                     uint8_t* __restrict__ sfout, int bN) {
+                                                     uint8_t* __restrict__ sfout, int bN, AttnRaw raw) {
     static_assert(PAGE % 32 == 0, "chunks of 32 positions stay inside a page");
+    __shared__ float nk[2][HEAD], nv[2][HEAD];  // RAW: this pass's rows of this KV head
+    __shared__ int npos[2];
     constexpr int PB = att_page_bytes(F32);
     extern __shared__ __align__(128) uint8_t kvs[];  // [ATT_WIN][K|V][PAGE][HEAD]
     __shared__ __align__(16) float qsh[8][HEAD];
@@ -627,7 +659,50 @@ __global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __
         if (bout) mx::emit_pieces_smem(qw, HEAD, 4, row, 0, 1, lane, 32, h * HEAD, bN, bout, sfout);
         return;
     }
-    *(float4*)(qw + 4 * lane) = *(const float4*)(qkv + (size_t)row * ld + h * HEAD + 4 * lane);
+    if (RAW) {
+        const float* qr = qkv + (size_t)row * ld + h * HEAD;
+        float a0 = qr[lane], a1 = qr[lane + 32], a2 = qr[lane + 64], a3 = qr[lane + 96];
+        norm_rope4(a0, a1, a2, a3, raw.qn, raw.rope[(size_t)rd.pos * HALF + lane],
+                   raw.rope[(size_t)rd.pos * HALF + lane + 32], lane);
+        qw[lane] = a0; qw[lane + 32] = a1; qw[lane + 64] = a2; qw[lane + 96] = a3;
+        if (warp <= row && warp < 2) {  // row j = warp of this pass (same sequence)
+            const int j = warp;
+            const RowDesc rj = pb.row[j];
+            const bool good = rj.pos >= 0 && rj.pos < kv.max_pos && rj.seq == rd.seq;
+            const float* kr = qkv + (size_t)j * ld + raw.k_off + kvh * HEAD;
+            const float* vr = qkv + (size_t)j * ld + raw.v_off + kvh * HEAD;
+            float k0 = kr[lane], k1 = kr[lane + 32], k2 = kr[lane + 64], k3 = kr[lane + 96];
+            const int pj = good ? rj.pos : 0;
+            norm_rope4(k0, k1, k2, k3, raw.kn, raw.rope[(size_t)pj * HALF + lane],
+                       raw.rope[(size_t)pj * HALF + lane + 32], lane);
+            const float v0 = vr[lane], v1 = vr[lane + 32], v2 = vr[lane + 64], v3 = vr[lane + 96];
+            nk[j][lane] = k0; nk[j][lane + 32] = k1; nk[j][lane + 64] = k2; nk[j][lane + 96] = k3;
+            nv[j][lane] = v0; nv[j][lane + 32] = v1; nv[j][lane + 64] = v2; nv[j][lane + 96] = v3;
+            if (lane == 0) npos[j] = good ? rj.pos : -1;
+            if (j == row && good) {  // the row's own K/V go to the cache
+                const int pg = pt[rj.pos / PAGE];
+                if (page_ok(kv, pg)) {
+                    const size_t idx = kv_index(pg, kvh, rj.pos % PAGE, kv.kv_heads);
+                    if (F32) {
+                        float* dk = (float*)kv.k + idx;
+                        float* dv = (float*)kv.v + idx;
+                        dk[lane] = k0; dk[lane + 32] = k1; dk[lane + 64] = k2; dk[lane + 96] = k3;
+                        dv[lane] = v0; dv[lane + 32] = v1; dv[lane + 64] = v2; dv[lane + 96] = v3;
+                    } else {
+                        uint16_t* dk = (uint16_t*)kv.k + idx;
+                        uint16_t* dv = (uint16_t*)kv.v + idx;
+                        dk[lane] = f2bf16(k0); dk[lane + 32] = f2bf16(k1);
+                        dk[lane + 64] = f2bf16(k2); dk[lane + 96] = f2bf16(k3);
+                        dv[lane] = f2bf16(v0); dv[lane + 32] = f2bf16(v1);
+                        dv[lane + 64] = f2bf16(v2); dv[lane + 96] = f2bf16(v3);
+                    }
+                }
+            }
+        }
+        __syncthreads();  // nk, nv, npos
+    } else {
+        *(float4*)(qw + 4 * lane) = *(const float4*)(qkv + (size_t)row * ld + h * HEAD + 4 * lane);
+    }
     const float scale = sqrtf(128.0f);
     float m = -INFINITY, l = 0.f;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -636,10 +711,28 @@ __global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __
         const int wn = min(ATT_WIN, npages - w0);
         if (threadIdx.x == 0 && w0 > 0) issue_window(w0);
         if (!ptx::mbar_wait(&bar, it & 1, ATT_WAIT)) ok = false;
+        if (RAW) {
+            // this pass's rows (computed above, in the cache's element type)
+            // over the early copy
+            for (int j = warp; j <= row && j < 2; j += group) {
+                const int p = npos[j];
+                const int i = p / PAGE - w0;
+                if (p < 0 || i < 0 || i >= wn) continue;
+                const size_t at = (size_t)(p % PAGE) * HEAD;
+                for (int d = lane; d < HEAD; d += 32) {
+                    if (F32) {
+                        ((float*)(kvs + (2 * i) * PB))[at + d] = nk[j][d];
+                        ((float*)(kvs + (2 * i + 1) * PB))[at + d] = nv[j][d];
+                    } else {
+                        ((uint16_t*)(kvs + (2 * i) * PB))[at + d] = f2bf16(nk[j][d]);
+                        ((uint16_t*)(kvs + (2 * i + 1) * PB))[at + d] = f2bf16(nv[j][d]);
+                    }
+                }
+            }
+        } else {
         // The q|k|v kernel of this pass wrote this row's K/V and those of the
         // pass's earlier rows of the sequence (at most `row` positions back):
         // fetch them again over the early copy.
-        {
             constexpr int RB = HEAD * (F32 ? 4 : 2);  // bytes of one row: 256 or 512
             const int lo = max(rd.pos - row, w0 * PAGE), hi = min(rd.pos, (w0 + wn) * PAGE - 1);
             for (int p = lo + warp; p <= hi; p += group) {
@@ -941,8 +1034,10 @@ jl_status configure_kernels() {
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_STORE>()));
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_ADD>()));
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_SWIGLU>()));
-    JL_CUDA(cudaFuncSetAttribute(k_attn_decode<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(0)));
-    JL_CUDA(cudaFuncSetAttribute(k_attn_decode<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(1)));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_decode<0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(0)));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_decode<1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(1)));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_decode<0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(0)));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_decode<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(1)));
     JL_TRY(mx_configure());
     JL_TRY(dec_configure());
     if (dev < 64) done[dev] = true;
@@ -984,11 +1079,14 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     if (c.rows_cap <= SMALL_M && group <= 8) {  // decode passes: a warp per query head
         const dim3 g2(c.m->kv_heads, c.rows_cap), blk(32 * group);
         const int qw = c.m->q_heads * HEAD;
+        const AttnRaw none{};
         if (c.m->kv.dtype == JL_KV_F32)
-            return launch_pdl(k_attn_decode<1>, g2, blk, att_smem(1), c.stream, c.m->pass, (const float*)c.m->s.qkv,
-                              qkv_ld(c.m), group, kv_view(c.m, layer), c.m->s.attn, qw, bout, sfout, bN);
-        return launch_pdl(k_attn_decode<0>, g2, blk, att_smem(0), c.stream, c.m->pass, (const float*)c.m->s.qkv,
-                          qkv_ld(c.m), group, kv_view(c.m, layer), c.m->s.attn, qw, bout, sfout, bN);
+            return launch_pdl(k_attn_decode<1, 0>, g2, blk, att_smem(1), c.stream, c.m->pass,
+                              (const float*)c.m->s.qkv, qkv_ld(c.m), group, kv_view(c.m, layer), c.m->s.attn, qw,
+                              bout, sfout, bN, none);
+        return launch_pdl(k_attn_decode<0, 0>, g2, blk, att_smem(0), c.stream, c.m->pass,
+                          (const float*)c.m->s.qkv, qkv_ld(c.m), group, kv_view(c.m, layer), c.m->s.attn, qw,
+                          bout, sfout, bN, none);
     }
     if (c.m->kv.dtype == JL_KV_F32)
         return launch_pdl(k_attention<1>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
@@ -1029,6 +1127,30 @@ jl_status launch_head(const PassCtx& c) {
     Proj p = make_proj({&c.m->head});
     return run_proj<EPI_STORE>(c, c.m->head.kind, 1, c.m->s.xh, c.m->hidden, p, c.m->s.logits,
                                c.m->vocab);
+}
+
+jl_status launch_attention_raw(const PassCtx& c, int layer, const uint16_t* qn, const uint16_t* kn) {
+    const jl_model* m = c.m;
+    const int group = m->q_heads / m->kv_heads;
+    if (c.rows_cap > 2 || group > 8 || group < 2) {
+        set_error("attention on raw q|k|v takes passes of at most 2 rows and GQA groups of 2..8");
+        return JL_ERR_INVALID_ARG;
+    }
+    const dim3 g2(m->kv_heads, c.rows_cap), blk(32 * group);
+    const int qw = m->q_heads * HEAD;
+    AttnRaw raw;
+    raw.qn = qn;
+    raw.kn = kn;
+    raw.rope = (const float2*)m->rope;
+    raw.k_off = qw;
+    raw.v_off = qw + m->kv_heads * HEAD;
+    if (m->kv.dtype == JL_KV_F32)
+        return launch_pdl(k_attn_decode<1, 1>, g2, blk, att_smem(1), c.stream, m->pass, (const float*)m->s.qkv,
+                          qkv_ld(m), group, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr,
+                          (uint8_t*)nullptr, 0, raw);
+    return launch_pdl(k_attn_decode<0, 1>, g2, blk, att_smem(0), c.stream, m->pass, (const float*)m->s.qkv,
+                      qkv_ld(m), group, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr, (uint8_t*)nullptr,
+                      0, raw);
 }
 
 jl_status launch_argmax(const PassCtx& c) {
