@@ -593,9 +593,17 @@ __device__ __forceinline__ void norm_rope4(float& a0, float& a1, float& a2, floa
     a0 = b0; a1 = b1; a2 = b2; a3 = b3;
 }
 
+// `split` warps serve each query head, taking every split-th 32-position
+// chunk with their own running max and sum; the head's first warp merges
+// them in warp order at the end.
+constexpr int ATT_MAXWARPS = 16;
+
+// Warps per query head: up to 4, at most 16 warps in the CTA.
+__host__ __device__ constexpr int att_split(int group) { return group >= 8 ? 2 : 4; }
+
 template <int F32, int RAW>
-__global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __restrict__ qkv, int ld,
-                                                     int group, KvView kv, float* __restrict__ out,
+__global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __restrict__ qkv, int ld,
+                                                     int group, int split, KvView kv, float* __restrict__ out,
                                                      int out_ld, uint8_t* __restrict__ bout,
                                                      uint8_t* __restrict__ sfout, int bN, AttnRaw raw) {
     static_assert(PAGE % 32 == 0, "chunks of 32 positions stay inside a page");
@@ -604,13 +612,17 @@ __global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __
     constexpr int PB = att_page_bytes(F32);
     extern __shared__ __align__(128) uint8_t kvs[];  // [ATT_WIN][K|V][PAGE][HEAD]
     __shared__ __align__(16) float qsh[8][HEAD];
+    __shared__ float cm[ATT_MAXWARPS], cl[ATT_MAXWARPS];  // per-warp running max and sum
+    __shared__ __align__(16) float cacc[ATT_MAXWARPS][HEAD];
     __shared__ uint64_t bar;
     __shared__ int page_s[ATT_WIN];
     const int g = blockIdx.x, row = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = g * group + warp;
+    const int nw = blockDim.x >> 5;
+    const int hw = warp % group, sub = warp / group;  // query head of the group, chunk share
+    const int h = g * group + hw;
     const int kvh = g;
-    float* qw = qsh[warp];
+    float* qw = qsh[hw];
     // The pass's rows and page tables were written before this pass began,
     // and the cache rows before this row's position by earlier passes: the
     // first window of pages is copied before waiting for the q|k|v kernel,
@@ -651,20 +663,22 @@ __global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __
     __syncthreads();  // the barrier is initialised before anyone waits on it
     ptx::grid_dependency_wait();
     ptx::launch_dependents();
-    if (row < rows && !valid) {  // uniform over the CTA
+    if (row < rows && !valid && sub == 0) {  // uniform over the CTA
         if (threadIdx.x == 0) atomicOr(kv.err, 2);
         *(float4*)(out + (size_t)row * out_ld + h * HEAD + 4 * lane) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (!valid) {
-        if (bout) mx::emit_pieces_smem(qw, HEAD, 4, row, 0, 1, lane, 32, h * HEAD, bN, bout, sfout);
+        if (bout && sub == 0) mx::emit_pieces_smem(qw, HEAD, 4, row, 0, 1, lane, 32, h * HEAD, bN, bout, sfout);
         return;
     }
     if (RAW) {
-        const float* qr = qkv + (size_t)row * ld + h * HEAD;
-        float a0 = qr[lane], a1 = qr[lane + 32], a2 = qr[lane + 64], a3 = qr[lane + 96];
-        norm_rope4(a0, a1, a2, a3, raw.qn, raw.rope[(size_t)rd.pos * HALF + lane],
-                   raw.rope[(size_t)rd.pos * HALF + lane + 32], lane);
-        qw[lane] = a0; qw[lane + 32] = a1; qw[lane + 64] = a2; qw[lane + 96] = a3;
+        if (sub == 0) {
+            const float* qr = qkv + (size_t)row * ld + h * HEAD;
+            float a0 = qr[lane], a1 = qr[lane + 32], a2 = qr[lane + 64], a3 = qr[lane + 96];
+            norm_rope4(a0, a1, a2, a3, raw.qn, raw.rope[(size_t)rd.pos * HALF + lane],
+                       raw.rope[(size_t)rd.pos * HALF + lane + 32], lane);
+            qw[lane] = a0; qw[lane + 32] = a1; qw[lane + 64] = a2; qw[lane + 96] = a3;
+        }
         if (warp <= row && warp < 2) {  // row j = warp of this pass (same sequence)
             const int j = warp;
             const RowDesc rj = pb.row[j];
@@ -700,7 +714,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __
             }
         }
         __syncthreads();  // nk, nv, npos
-    } else {
+    } else if (sub == 0) {
         *(float4*)(qw + 4 * lane) = *(const float4*)(qkv + (size_t)row * ld + h * HEAD + 4 * lane);
     }
     const float scale = sqrtf(128.0f);
@@ -714,7 +728,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __
         if (RAW) {
             // this pass's rows (computed above, in the cache's element type)
             // over the early copy
-            for (int j = warp; j <= row && j < 2; j += group) {
+            for (int j = warp; j <= row && j < 2; j += nw) {
                 const int p = npos[j];
                 const int i = p / PAGE - w0;
                 if (p < 0 || i < 0 || i >= wn) continue;
@@ -735,7 +749,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __
         // fetch them again over the early copy.
             constexpr int RB = HEAD * (F32 ? 4 : 2);  // bytes of one row: 256 or 512
             const int lo = max(rd.pos - row, w0 * PAGE), hi = min(rd.pos, (w0 + wn) * PAGE - 1);
-            for (int p = lo + warp; p <= hi; p += group) {
+            for (int p = lo + warp; p <= hi; p += nw) {
                 const int pg = pt[p / PAGE];
                 if ((unsigned)pg >= (unsigned)kv.pages) continue;  // flagged when the window was copied
                 const int i = p / PAGE - w0;
@@ -756,6 +770,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __
                 for (int half = 0; half < PAGE / 32; ++half) {
                     const int c0 = (w0 + i) * PAGE + half * 32;
                     if (c0 >= visible) break;
+                    if ((c0 / 32) % split != sub) continue;  // another warp's chunk
                     const int r = half * 32 + lane;  // row of this lane's position in the page
                     float sc = -INFINITY;
                     if (c0 + lane < visible) {
@@ -825,9 +840,30 @@ __global__ void __launch_bounds__(256) k_attn_decode(PassBuf pb, const float* __
         __syncthreads();  // the window is free for the next copy
     }
     if (!ok && threadIdx.x == 0) atomicOr(kv.err, 4);  // a page copy did not arrive in time
-    float o[4];
+    // merge the head's warps in warp order
+    if (lane == 0) {
+        cm[warp] = m;
+        cl[warp] = l;
+    }
+    *(float4*)(&cacc[warp][4 * lane]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    __syncthreads();
+    if (sub != 0) return;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < split; ++s2) M = fmaxf(M, cm[s2 * group + hw]);
+    float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s2 = 0; s2 < split; ++s2) {
+        const int w2 = s2 * group + hw;
+        if (cm[w2] == -INFINITY) continue;  // no position fell to that warp
+        const float f = expf(cm[w2] - M);
+        L = fmaf(cl[w2], f, L);
+        const float4 a4 = *(const float4*)(&cacc[w2][4 * lane]);
+        o[0] = fmaf(a4.x, f, o[0]);
+        o[1] = fmaf(a4.y, f, o[1]);
+        o[2] = fmaf(a4.z, f, o[2]);
+        o[3] = fmaf(a4.w, f, o[3]);
+    }
 #pragma unroll
-    for (int d = 0; d < 4; ++d) o[d] = __fdiv_rn(acc[d], l);
+    for (int d = 0; d < 4; ++d) o[d] = __fdiv_rn(o[d], L);
     *(float4*)(out + (size_t)row * out_ld + h * HEAD + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
     if (bout) {
         __syncwarp();  // every lane has finished reading q
@@ -1077,16 +1113,17 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     uint8_t* sfout = pieces ? c.m->mx.sfattn : nullptr;
     const int bN = 8 * c.rows_cap;
     if (c.rows_cap <= SMALL_M && group <= 8) {  // decode passes: a warp per query head
-        const dim3 g2(c.m->kv_heads, c.rows_cap), blk(32 * group);
+        const int split = att_split(group);
+        const dim3 g2(c.m->kv_heads, c.rows_cap), blk(32 * group * split);
         const int qw = c.m->q_heads * HEAD;
         const AttnRaw none{};
         if (c.m->kv.dtype == JL_KV_F32)
             return launch_pdl(k_attn_decode<1, 0>, g2, blk, att_smem(1), c.stream, c.m->pass,
-                              (const float*)c.m->s.qkv, qkv_ld(c.m), group, kv_view(c.m, layer), c.m->s.attn, qw,
-                              bout, sfout, bN, none);
+                              (const float*)c.m->s.qkv, qkv_ld(c.m), group, split, kv_view(c.m, layer),
+                              c.m->s.attn, qw, bout, sfout, bN, none);
         return launch_pdl(k_attn_decode<0, 0>, g2, blk, att_smem(0), c.stream, c.m->pass,
-                          (const float*)c.m->s.qkv, qkv_ld(c.m), group, kv_view(c.m, layer), c.m->s.attn, qw,
-                          bout, sfout, bN, none);
+                          (const float*)c.m->s.qkv, qkv_ld(c.m), group, split, kv_view(c.m, layer), c.m->s.attn,
+                          qw, bout, sfout, bN, none);
     }
     if (c.m->kv.dtype == JL_KV_F32)
         return launch_pdl(k_attention<1>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
@@ -1136,7 +1173,8 @@ jl_status launch_attention_raw(const PassCtx& c, int layer, const uint16_t* qn, 
         set_error("attention on raw q|k|v takes passes of at most 2 rows and GQA groups of 2..8");
         return JL_ERR_INVALID_ARG;
     }
-    const dim3 g2(m->kv_heads, c.rows_cap), blk(32 * group);
+    const int split = att_split(group);
+    const dim3 g2(m->kv_heads, c.rows_cap), blk(32 * group * split);
     const int qw = m->q_heads * HEAD;
     AttnRaw raw;
     raw.qn = qn;
@@ -1146,11 +1184,11 @@ jl_status launch_attention_raw(const PassCtx& c, int layer, const uint16_t* qn, 
     raw.v_off = qw + m->kv_heads * HEAD;
     if (m->kv.dtype == JL_KV_F32)
         return launch_pdl(k_attn_decode<1, 1>, g2, blk, att_smem(1), c.stream, m->pass, (const float*)m->s.qkv,
-                          qkv_ld(m), group, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr,
+                          qkv_ld(m), group, split, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr,
                           (uint8_t*)nullptr, 0, raw);
     return launch_pdl(k_attn_decode<0, 1>, g2, blk, att_smem(0), c.stream, m->pass, (const float*)m->s.qkv,
-                      qkv_ld(m), group, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr, (uint8_t*)nullptr,
-                      0, raw);
+                      qkv_ld(m), group, split, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr,
+                      (uint8_t*)nullptr, 0, raw);
 }
 
 jl_status launch_argmax(const PassCtx& c) {
