@@ -343,12 +343,11 @@ jl_status record_fused_pass(const PassCtx& c, int layers) {
     const MxBuffers& B = m->mx;
     const int h = m->hidden, tiles = h / 128;
     JL_TRY(launch_embed(c));
-    if (layers > 0) JL_TRY(mx_norm_pieces(c, m->s.x, h, m->lw[0].in_ln, h, B.bx, B.sfx, B.part));
+    if (layers > 0) JL_TRY(mx_norm_pieces(c, m->s.x, h, m->lw[0].in_ln, h, B.bx, B.part));
     for (int l = 0; l < layers; ++l) {
         const LayerW& L = m->lw[l];
         MxFuse qkv;  // model.rs:174-177, lib.rs:353-396
         qkv.b = B.bx;
-        qkv.sfb = B.sfx;
         qkv.part_in = B.part;
         qkv.part_tiles = tiles;
         qkv.norm_width = h;
@@ -359,27 +358,21 @@ jl_status record_fused_pass(const PassCtx& c, int layers) {
         JL_TRY(launch_attention(c, l, true));  // lib.rs:401-441
         MxFuse o;  // lib.rs:444-449 + residual, then post_attention_layernorm
         o.b = B.battn;
-        o.sfb = B.sfattn;
         o.bout = B.bx;
-        o.sfout = B.sfx;
         o.part_out = B.part;
         o.next_w = L.post_ln;
         JL_TRY(mx_project_fused(c, L.mx_o, MXE_ADD, o, m->s.x, h));
         MxFuse gu;  // lib.rs:459-463
         gu.b = B.bx;
-        gu.sfb = B.sfx;
         gu.part_in = B.part;
         gu.part_tiles = tiles;
         gu.norm_width = h;
         gu.bout = B.bact;
-        gu.sfout = B.sfact;
         JL_TRY(mx_project_fused(c, L.mx_gateup, MXE_SWIGLU, gu, nullptr, m->inter));
         MxFuse dn;  // lib.rs:464-467 + residual, then the next input_layernorm
         dn.b = B.bact;
-        dn.sfb = B.sfact;
         if (l + 1 < layers) {
             dn.bout = B.bx;
-            dn.sfout = B.sfx;
             dn.part_out = B.part;
             dn.next_w = m->lw[l + 1].in_ln;
         }
@@ -560,9 +553,7 @@ jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters
         if (fused && which == 1) {  // o: residual add, pieces and sums of squares out
             MxFuse f;
             f.b = m->mx.battn;
-            f.sfb = m->mx.sfattn;
             f.bout = m->mx.bx;
-            f.sfout = m->mx.sfx;
             f.part_out = m->mx.part;
             f.next_w = L.post_ln;
             return mx_project_fused(c, L.mx_o, MXE_ADD, f, m->s.x, hid);
@@ -570,12 +561,10 @@ jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters
         if (fused && which == 2) {  // gate/up: input RMSNorm, SwiGLU, pieces out
             MxFuse f;
             f.b = m->mx.bx;
-            f.sfb = m->mx.sfx;
             f.part_in = m->mx.part;
             f.part_tiles = tiles;
             f.norm_width = hid;
             f.bout = m->mx.bact;
-            f.sfout = m->mx.sfact;
             return mx_project_fused(c, L.mx_gateup, MXE_SWIGLU, f, nullptr, m->inter);
         }
         if (which == 4 && m->bf_head.a && rows <= mx_max_tokens())  // final norm + bf16 table + argmax
@@ -583,9 +572,7 @@ jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters
         if (fused && which == 3) {  // down: residual add, pieces and sums of squares out
             MxFuse f;
             f.b = m->mx.bact;
-            f.sfb = m->mx.sfact;
             f.bout = m->mx.bx;
-            f.sfout = m->mx.sfx;
             f.part_out = m->mx.part;
             f.next_w = L.in_ln;
             return mx_project_fused(c, L.mx_down, MXE_ADD, f, m->s.x, hid);

@@ -103,29 +103,24 @@ struct Mat {
 // T tiles of 128 weight rows (gate/up: 64 gate + 64 up rows), S stages of 256
 // K-elements, K split into `ksplit` slices across CTAs.
 struct MxProj {
-    const uint8_t* a = nullptr;     // [T][S] swizzled 16 KB weight images
-    const uint8_t* sfa = nullptr;   // [T][S] 1 KB scale atoms
+    const uint8_t* a = nullptr;     // [T][S] swizzled 16 KB weight stages, each then (MXFP4) its scales
     int T = 0, S = 0, K = 0, ksplit = 1, out_rows = 0;
     bool swiglu = false;
 };
 
 struct MxBuffers {
-    uint8_t* bimg = nullptr;   // activation pieces, [S][N*128]
-    uint8_t* sfb = nullptr;    // their scale atoms, [S][1024]
+    uint8_t* bimg = nullptr;   // activation pieces, [S][N*128 + 1024]
     float* ws = nullptr;       // split-K partials
     int* tickets = nullptr;    // split-K arrival counters (kept at zero between launches)
     void* arena = nullptr;     // tiled weights
-    void* scratch = nullptr;   // bimg, sfb, ws, tickets and the fused-pass buffers below
+    void* scratch = nullptr;   // bimg, ws, tickets and the fused-pass buffers below
     // Fused decode pass (every layer MXFP4, widths multiples of 256): piece
     // images of the normalised residual stream (x), the attention output and
     // the SwiGLU activations, and per-tile sums of squares of x.
     bool fused = false;
     uint8_t* bx = nullptr;
-    uint8_t* sfx = nullptr;
     uint8_t* battn = nullptr;
-    uint8_t* sfattn = nullptr;
     uint8_t* bact = nullptr;
-    uint8_t* sfact = nullptr;
     float* part = nullptr;     // [hidden / 128][MX_PART_STRIDE]
     // bf16 output table on the tensor cores: its input pieces and each
     // tile's first maximum per row
@@ -301,14 +296,12 @@ jl_status launch_synth_bf16(uint64_t seed, uint32_t tensor_index, size_t n, uint
 enum MxEpi : int { MXE_STORE = 0, MXE_ADD = 1, MXE_SWIGLU = 2, MXE_QKV = 3 };
 constexpr int MX_PART_STRIDE = 16;  // rows per tile in the sum-of-squares partials
 // Fused decode-pass projection (mx_project_fused): its input pieces are
-// already in (b, sfb), written by the kernel before it.
+// already in b, written by the kernel before it.
 struct MxFuse {
     const uint8_t* b = nullptr;        // input pieces
-    const uint8_t* sfb = nullptr;
     const float* part_in = nullptr;    // input RMSNorm: per-tile sums of squares of x
     int part_tiles = 0, norm_width = 0;
     uint8_t* bout = nullptr;           // pieces of (output * next_w) for the next projection
-    uint8_t* sfout = nullptr;
     float* part_out = nullptr;         // per-tile sums of squares of the output (residual add)
     const uint16_t* next_w = nullptr;
     int layer = 0;                     // q|k|v: cache layer and QK-norm weights
@@ -323,10 +316,10 @@ jl_status mx_build(const Mat* const* mats, int nmats, bool swiglu, uint8_t* dst,
 jl_status mx_project(const PassCtx& c, const MxProj& p, int epi, int use_head, const float* x,
                      int ldx, const uint16_t* norm, float* y, int ldy);
 // Scratch one launch of `p` over `mcap` rows needs when the caller supplies
-// it: split-K tickets (zero at launch), piece scale atoms, piece images and
-// split-K partials, in that order, each 256-byte aligned.
+// it: split-K tickets (zero at launch), the piece image and split-K
+// partials, in that order, each 256-byte aligned.
 struct MxScratchPlan {
-    size_t tickets = 0, sfb = 0, bimg = 0, ws = 0, total = 0;
+    size_t tickets = 0, bimg = 0, ws = 0, total = 0;
 };
 MxScratchPlan mx_scratch_plan(const MxProj& p, int mcap);
 jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxFuse& f, float* y,
@@ -334,7 +327,7 @@ jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxF
 // Pieces of x * w and per-tile sums of squares of x for the first projection
 // of a fused pass (after the embedding).
 jl_status mx_norm_pieces(const PassCtx& c, const float* x, int ldx, const uint16_t* w, int width,
-                         uint8_t* bout, uint8_t* sfout, float* part);
+                         uint8_t* bout, float* part);
 // bf16 output table on the tensor cores (kind::f16): load-time tiles, and the
 // fused final norm + logits + argmax of a decode pass.
 size_t bf16_tile_bytes(int rows, int K);

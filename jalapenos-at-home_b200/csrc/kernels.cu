@@ -461,7 +461,7 @@ template <int F32>
 __global__ void __launch_bounds__(128) k_attention(PassBuf pb, const float* __restrict__ qkv,
                                                    int ld, int q_heads, int group, KvView kv,
                                                    float* __restrict__ out, uint8_t* __restrict__ bout,
-                                                   uint8_t* __restrict__ sfout, int bN) {
+                                                   int bN) {
     __shared__ __align__(16) float qs[HEAD];
     __shared__ float pr[128];
     __shared__ float red[32];
@@ -470,7 +470,7 @@ __global__ void __launch_bounds__(128) k_attention(PassBuf pb, const float* __re
     const int h = blockIdx.x, row = blockIdx.y;
     const int t = threadIdx.x;
     if (row >= pb.hdr->rows) {
-        if (bout) mx::emit_pieces_smem(qs, HEAD, 4, row, 0, 1, t, 128, h * HEAD, bN, bout, sfout);
+        if (bout) mx::emit_pieces_smem(qs, HEAD, 4, row, 0, 1, t, 128, h * HEAD, bN, bout);
         return;
     }
     const RowDesc rd = pb.row[row];
@@ -478,7 +478,7 @@ __global__ void __launch_bounds__(128) k_attention(PassBuf pb, const float* __re
     if (rd.pos < 0 || rd.pos >= kv.max_pos || (unsigned)rd.seq >= (unsigned)MAX_SEQS) {
         if (t == 0) atomicOr(kv.err, 2);
         out[(size_t)row * (q_heads * HEAD) + h * HEAD + t] = 0.f;
-        if (bout) mx::emit_pieces_smem(qs, HEAD, 4, row, 0, 1, t, 128, h * HEAD, bN, bout, sfout);
+        if (bout) mx::emit_pieces_smem(qs, HEAD, 4, row, 0, 1, t, 128, h * HEAD, bN, bout);
         return;
     }
     const int visible = rd.pos + 1;
@@ -542,7 +542,7 @@ __global__ void __launch_bounds__(128) k_attention(PassBuf pb, const float* __re
     if (bout) {  // every thread is past its last read of qs (the loop ends on a barrier)
         qs[t] = o;
         __syncthreads();
-        mx::emit_pieces_smem(qs, HEAD, 4, row, 1, 1, t, 128, h * HEAD, bN, bout, sfout);
+        mx::emit_pieces_smem(qs, HEAD, 4, row, 1, 1, t, 128, h * HEAD, bN, bout);
     }
 }
 
@@ -604,8 +604,8 @@ __host__ __device__ constexpr int att_split(int group) { return group >= 8 ? 2 :
 template <int F32, int RAW>
 __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __restrict__ qkv, int ld,
                                                      int group, int split, KvView kv, float* __restrict__ out,
-                                                     int out_ld, uint8_t* __restrict__ bout,
-                                                     uint8_t* __restrict__ sfout, int bN, AttnRaw raw) {
+                                                     int out_ld, uint8_t* __restrict__ bout, int bN,
+                                                     AttnRaw raw) {
     static_assert(PAGE % 32 == 0, "chunks of 32 positions stay inside a page");
     __shared__ float nk[2][HEAD], nv[2][HEAD];  // RAW: this pass's rows of this KV head
     __shared__ int npos[2];
@@ -668,7 +668,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
         *(float4*)(out + (size_t)row * out_ld + h * HEAD + 4 * lane) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (!valid) {
-        if (bout && sub == 0) mx::emit_pieces_smem(qw, HEAD, 4, row, 0, 1, lane, 32, h * HEAD, bN, bout, sfout);
+        if (bout && sub == 0) mx::emit_pieces_smem(qw, HEAD, 4, row, 0, 1, lane, 32, h * HEAD, bN, bout);
         return;
     }
     if (RAW) {
@@ -869,7 +869,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
         __syncwarp();  // every lane has finished reading q
         *(float4*)(qw + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
         __syncwarp();
-        mx::emit_pieces_smem(qw, HEAD, 4, row, 1, 1, lane, 32, h * HEAD, bN, bout, sfout);
+        mx::emit_pieces_smem(qw, HEAD, 4, row, 1, 1, lane, 32, h * HEAD, bN, bout);
     }
 }
 
@@ -1110,7 +1110,6 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     dim3 grid(c.m->q_heads, c.rows_cap);
     const int group = c.m->q_heads / c.m->kv_heads;
     uint8_t* bout = pieces ? c.m->mx.battn : nullptr;
-    uint8_t* sfout = pieces ? c.m->mx.sfattn : nullptr;
     const int bN = 8 * c.rows_cap;
     if (c.rows_cap <= SMALL_M && group <= 8) {  // decode passes: a warp per query head
         const int split = att_split(group);
@@ -1120,16 +1119,16 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
         if (c.m->kv.dtype == JL_KV_F32)
             return launch_pdl(k_attn_decode<1, 0>, g2, blk, att_smem(1), c.stream, c.m->pass,
                               (const float*)c.m->s.qkv, qkv_ld(c.m), group, split, kv_view(c.m, layer),
-                              c.m->s.attn, qw, bout, sfout, bN, none);
+                              c.m->s.attn, qw, bout, bN, none);
         return launch_pdl(k_attn_decode<0, 0>, g2, blk, att_smem(0), c.stream, c.m->pass,
                           (const float*)c.m->s.qkv, qkv_ld(c.m), group, split, kv_view(c.m, layer), c.m->s.attn,
-                          qw, bout, sfout, bN, none);
+                          qw, bout, bN, none);
     }
     if (c.m->kv.dtype == JL_KV_F32)
         return launch_pdl(k_attention<1>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
-                          qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn, bout, sfout, bN);
+                          qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn, bout, bN);
     return launch_pdl(k_attention<0>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
-                      qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn, bout, sfout, bN);
+                      qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn, bout, bN);
 }
 
 jl_status launch_o(const PassCtx& c, const LayerW& L) {
@@ -1184,11 +1183,11 @@ jl_status launch_attention_raw(const PassCtx& c, int layer, const uint16_t* qn, 
     raw.v_off = qw + m->kv_heads * HEAD;
     if (m->kv.dtype == JL_KV_F32)
         return launch_pdl(k_attn_decode<1, 1>, g2, blk, att_smem(1), c.stream, m->pass, (const float*)m->s.qkv,
-                          qkv_ld(m), group, split, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr,
-                          (uint8_t*)nullptr, 0, raw);
+                          qkv_ld(m), group, split, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr, 0,
+                          raw);
     return launch_pdl(k_attn_decode<0, 1>, g2, blk, att_smem(0), c.stream, m->pass, (const float*)m->s.qkv,
-                      qkv_ld(m), group, split, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr,
-                      (uint8_t*)nullptr, 0, raw);
+                      qkv_ld(m), group, split, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr, 0,
+                      raw);
 }
 
 jl_status launch_argmax(const PassCtx& c) {

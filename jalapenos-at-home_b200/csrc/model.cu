@@ -231,21 +231,17 @@ jl_status build_mx(jl_model* m) {
     if (head_bf) JL_TRY(mx_build_bf16(m->head, base + bfh_off, &m->bf_head, 0));
     m->dec_ok = dec_supported(m);
     Plan sp;
-    const size_t off_b = sp.take((size_t)maxS * mx_max_tokens() * 8 * 128);
-    const size_t off_sf = sp.take((size_t)maxS * 1024);
+    // piece images: per 256-element stage, up to 16 rows x 8 pieces x 128
+    // bytes of codes, then 1 KB of scale atoms
+    const size_t img_stage = (size_t)mx_max_tokens() * 8 * 128 + 1024;
+    const size_t off_b = sp.take((size_t)maxS * img_stage);
     const size_t off_ws = sp.take(ws_floats * sizeof(float));
     const size_t off_t = sp.take((size_t)maxT * sizeof(int));
-    const size_t img_x = (size_t)(m->hidden / 256) * mx_max_tokens() * 8 * 128;
-    const size_t img_a = (size_t)(QW / 256) * mx_max_tokens() * 8 * 128;
-    const size_t img_f = (size_t)(m->inter / 256) * mx_max_tokens() * 8 * 128;
-    size_t off_fx = 0, off_fsx = 0, off_fa = 0, off_fsa = 0, off_ff = 0, off_fsf = 0, off_fp = 0;
+    size_t off_fx = 0, off_fa = 0, off_ff = 0, off_fp = 0;
     if (fused) {
-        off_fx = sp.take(img_x);
-        off_fsx = sp.take((size_t)(m->hidden / 256) * 1024);
-        off_fa = sp.take(img_a);
-        off_fsa = sp.take((size_t)(QW / 256) * 1024);
-        off_ff = sp.take(img_f);
-        off_fsf = sp.take((size_t)(m->inter / 256) * 1024);
+        off_fx = sp.take((size_t)(m->hidden / 256) * img_stage);
+        off_fa = sp.take((size_t)(QW / 256) * img_stage);
+        off_ff = sp.take((size_t)(m->inter / 256) * img_stage);
         off_fp = sp.take((size_t)(m->hidden / 128) * MX_PART_STRIDE * sizeof(float));
     }
     size_t off_bh = 0, off_av = 0, off_ai = 0;
@@ -262,17 +258,13 @@ jl_status build_mx(jl_model* m) {
     JL_CUDA(cudaMemset(m->mx.scratch, 0, sp.bytes));
     uint8_t* s = (uint8_t*)m->mx.scratch;
     m->mx.bimg = s + off_b;
-    m->mx.sfb = s + off_sf;
     m->mx.ws = (float*)(s + off_ws);
     m->mx.tickets = (int*)(s + off_t);
     if (fused) {
         m->mx.fused = true;
         m->mx.bx = s + off_fx;
-        m->mx.sfx = s + off_fsx;
         m->mx.battn = s + off_fa;
-        m->mx.sfattn = s + off_fsa;
         m->mx.bact = s + off_ff;
-        m->mx.sfact = s + off_fsf;
         m->mx.part = (float*)(s + off_fp);
     }
     if (head_bf) {

@@ -14,12 +14,15 @@
 //
 // Layouts, all built once at load time:
 //  * weight tile (t, s): 128 weight rows x 256 K-elements (128 bytes per
-//    row), 16 KB in the 128-byte-swizzled K-major layout the MMA reads;
-//  * its scales: two 512-byte atoms (128 rows x 4 blocks of 32), byte
-//    16*(r%32) + 4*(r/32) + kb, which tcgen05.cp broadcasts into 4 TMEM
-//    columns;
-//  * activation pieces for stage s: N rows x 128 bytes, same swizzle, and
-//    their scale atoms (N <= 128).
+//    row), 16 KB in the 128-byte-swizzled K-major layout the MMA reads,
+//    followed by its scales: two 512-byte atoms (128 rows x 4 blocks of 32),
+//    byte 16*(r%32) + 4*(r/32) + kb, which tcgen05.cp broadcasts into 4 TMEM
+//    columns.  The stages of a tile are contiguous ([T][S][17 KB]);
+//  * activation pieces for stage s: N rows x 128 bytes, same swizzle, then
+//    their scale atoms (N <= 128), stages contiguous too.
+// A bulk copy costs a few hundred nanoseconds of a CTA's copy engine
+// whatever its size, so the ring moves GROUP stages of weights as one copy
+// and their activation stages as a second one.
 // Split-K partials go to a workspace; the last CTA of a tile (atomic ticket)
 // adds them in a fixed order and runs the epilogue, so a row's result does
 // not depend on timing or on how many tokens share the pass.
@@ -57,8 +60,7 @@ constexpr int ACC_COL = 0, SFA_COL = 128, SFB_COL = 136;
 // p of token m is row 8m+p of the B operand.
 __global__ void __launch_bounds__(256) k_mx_pieces(const PassHdr* __restrict__ hdr, int use_head,
                                                    int mcap, const float* __restrict__ x, int ldx,
-                                                   int K, int S, int N, uint8_t* __restrict__ bimg,
-                                                   uint8_t* __restrict__ sfb) {
+                                                   int K, int S, int N, uint8_t* __restrict__ bimg) {
     ptx::grid_dependency_wait();  // x comes from the previous kernel; bimg may still be read by it
     ptx::launch_dependents();
     const int lane = threadIdx.x & 31;
@@ -69,7 +71,7 @@ __global__ void __launch_bounds__(256) k_mx_pieces(const PassHdr* __restrict__ h
     const int M = min(use_head ? hdr->head_rows : hdr->rows, mcap);
     const int k = kb * 32 + lane;
     float r = (m < M && k < K) ? x[(size_t)m * ldx + k] : 0.f;
-    mx::emit_pieces(r, lane, m, kb * 32, N, bimg, sfb);
+    mx::emit_pieces(r, lane, m, kb * 32, N, bimg);
 }
 
 // Pieces of x * w for a projection that follows an RMSNorm, plus the
@@ -79,8 +81,7 @@ __global__ void __launch_bounds__(256) k_mx_pieces(const PassHdr* __restrict__ h
 __global__ void __launch_bounds__(128) k_norm_pieces(const PassHdr* __restrict__ hdr, int mcap,
                                                      const float* __restrict__ x, int ldx,
                                                      const uint16_t* __restrict__ w, int width, int N,
-                                                     uint8_t* __restrict__ bout, uint8_t* __restrict__ sfout,
-                                                     float* __restrict__ part) {
+                                                     uint8_t* __restrict__ bout, float* __restrict__ part) {
     __shared__ float red[4];
     ptx::grid_dependency_wait();
     ptx::launch_dependents();
@@ -90,7 +91,7 @@ __global__ void __launch_bounds__(128) k_norm_pieces(const PassHdr* __restrict__
     const int k = t * 128 + threadIdx.x;
     const float v = (m < M && k < width) ? x[(size_t)m * ldx + k] : 0.f;
     const float wk = k < width ? bf16f(w[k]) : 0.f;
-    mx::emit_pieces(__fmul_rn(v, wk), lane, m, t * 128 + warp * 32, N, bout, sfout);
+    mx::emit_pieces(__fmul_rn(v, wk), lane, m, t * 128 + warp * 32, N, bout);
     const float ss = warp_sum(__fmul_rn(v, v));
     if (lane == 0) red[warp] = ss;
     __syncthreads();
@@ -207,12 +208,11 @@ __global__ void k_bf16_tile(const uint16_t* __restrict__ src, int rows, int K, i
 // the projection
 
 struct MxArgs {
-    const uint8_t* a;      // [T][S][A_STAGE]
-    const uint8_t* sfa;    // [T][S][SF_STAGE]
-    const uint8_t* b;      // [S][N*128]
-    const uint8_t* sfb;    // [S][SF_STAGE]
+    const uint8_t* a;      // [T][S][w_stage]: codes, then (MXFP4) scale atoms
+    const uint8_t* b;      // [S][b_stage]: pieces, then (MXFP4) their scale atoms
     int T, S, ksplit, N, mcap;
-    int nbuf, stages;      // TMEM accumulator buffers (1 or 2), ring depth
+    int nbuf, stages;      // TMEM accumulator buffers (1 or 2), ring slots
+    int group;             // K stages per ring slot (1 or 2)
     const PassHdr* hdr;
     int use_head;
     float* y;
@@ -226,11 +226,10 @@ struct MxArgs {
     // per-tile sums of squares (part_in, part_tiles tiles of MX_MAXTOK).
     const float* part_in;
     int part_tiles, norm_width;
-    // Output pieces for the next projection (bout/sfout, bN columns) and,
+    // Output pieces for the next projection (bout, bN columns) and,
     // after a residual add, the sums of squares of the new x (part_out) and
     // the next RMSNorm weight (next_w) the pieces are scaled by.
     uint8_t* bout;
-    uint8_t* sfout;
     int bN;
     float* part_out;
     const uint16_t* next_w;
@@ -258,8 +257,19 @@ constexpr int MX_THREADS = 192;     // warp 0 loads, warp 1 MMAs, warps 2-5 epil
 static_assert(MX_PART_STRIDE >= MX_MAXTOK, "partials hold every row of a pass");
 static_assert(MX_MAXTOK == 16, "emit_pieces_all takes 16 rows");
 
-__host__ __device__ constexpr int mx_stage_bytes(int N, int kind = KIND_MX) {
-    return A_STAGE + N * 128 + (kind == KIND_MX ? 2 * SF_STAGE : 0);
+// Bytes of one K stage of a weight tile and of an activation image.
+__host__ __device__ constexpr int w_stage(int kind) { return A_STAGE + (kind == KIND_MX ? SF_STAGE : 0); }
+__host__ __device__ constexpr int b_stage(int N, int kind) {
+    return N * 128 + (kind == KIND_MX ? SF_STAGE : 0);
+}
+// One ring slot: `group` weight stages, then their activation stages.
+__host__ __device__ constexpr int mx_slot_bytes(int N, int kind, int group) {
+    return group * (w_stage(kind) + b_stage(N, kind));
+}
+// First K stage of split kc of ks: splits start on a slot boundary.
+__host__ __device__ inline int split_stage(int S, int group, int ks, int kc) {
+    const int slots = (S + group - 1) / group;
+    return min(S, group * (int)((long long)kc * slots / ks));
 }
 // MMA columns one row occupies (its pieces, then padding).
 __host__ __device__ constexpr int cols_per_row(int kind) { return kind == KIND_MX ? 8 : 4; }
@@ -303,17 +313,20 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 // epilogue overlaps the next tile's streaming.  Warp w reads TMEM lanes
 // 32*(w%4).., weight rows 32*(w%4).. of the tile.
 //
-// Split-K reduction through distributed shared memory: ranks 1.. write their
-// partial tile into their own shared-memory slot and arrive on the leader's
-// red_full barrier; the leader (rank 0) adds the slots in rank order (a
-// fixed order, so results do not depend on timing or on the row count), then
-// frees them (slot_free) and runs the epilogue.
+// Split-K reduction through distributed shared memory: ranks 1.. push their
+// partial tile into the leader's reduction buffer with st.async, whose bytes
+// complete the leader's red_full barrier; the leader (rank 0) adds the
+// partials in rank order (a fixed order, so results do not depend on timing
+// or on the row count) and runs the epilogue.  When the cluster has another
+// tile, each leader warp frees the buffer with a 4-byte st.async onto every
+// peer's slot_free barrier.  No thread waits on a remote acknowledgement.
 template <int EPI, int KIND>
 __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     __shared__ uint64_t full[MX_MAXSTAGES], empty[MX_MAXSTAGES], tfull[2], tempty[2];
     __shared__ uint64_t red_full, slot_free;
+    __shared__ uint32_t free_sig;            // target of the leader's slot_free stores
     __shared__ uint32_t tmem_base_s;
     __shared__ float red_s[4][MX_MAXTOK];    // per-warp sums of squares / row maxima
     __shared__ int redi_s[4][MX_MAXTOK];     // per-warp arg maxima
@@ -322,18 +335,22 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
     __shared__ int kvpos_s[MX_MAXTOK];       // q|k|v: position of each row, -1 if invalid
     __shared__ int kvpage_s[MX_MAXTOK];      //   and its cache page
 
-    const int N = a.N, ST = a.stages, NB = a.nbuf;
-    const int sbytes = mx_stage_bytes(N, KIND);
+    const int N = a.N, ST = a.stages, NB = a.nbuf, G = a.group;
+    constexpr int WS = w_stage(KIND);
+    const int BS = b_stage(N, KIND);
+    const int sbytes = mx_slot_bytes(N, KIND, G);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ks = a.ksplit;
     const int kc = ks > 1 ? (int)ptx::cluster_ctarank() : 0;
     const int cid = blockIdx.x / ks, NC = gridDim.x / ks;
-    const int s0 = (int)((long long)kc * a.S / ks), s1 = (int)((long long)(kc + 1) * a.S / ks);
-    // this CTA's split-K partial [128][mcap rounded up to 4]; the leader
-    // never publishes its own, so there the region is epilogue scratch
-    // (staged outputs [m][128], SwiGLU up halves and RoPE partners xs[m][64])
+    const int s0 = split_stage(a.S, G, ks, kc), s1 = split_stage(a.S, G, ks, kc + 1);
+    // epilogue scratch (staged outputs [m][128], SwiGLU up halves and RoPE
+    // partners xs[m][64]), then the leader's reduction buffer: for each peer
+    // rank and group of four rows of the pass, [128 tile rows][4] floats
+    const int RB = (a.mcap + 3) >> 2;
     float* slot = (float*)(smem + ST * sbytes);
     float(*xs)[64] = (float(*)[64])slot;
+    float* red = slot + RB * 4 * 128;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < ST; ++i) {
@@ -344,8 +361,8 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
             ptx::mbar_init(&tfull[i], 1);
             ptx::mbar_init(&tempty[i], 4);
         }
-        ptx::mbar_init(&red_full, 4 * (ks > 1 ? ks - 1 : 1));  // four warps of every other rank
-        ptx::mbar_init(&slot_free, 4);                         // the leader's four warps
+        ptx::mbar_init(&red_full, 1);   // the leader's expect_tx, then the peers' bytes
+        ptx::mbar_init(&slot_free, 1);  // a peer's expect_tx, then the leader warps' bytes
         ptx::fence_barrier_init();
     }
     if (warp == 1) {
@@ -365,18 +382,18 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
     if (warp == 0) {
         if (lane == 0) {
             // Prefetch the first ring slots' weights, then wait for the
-            // kernel that produces the activation pieces.
+            // kernel that produces the activation pieces.  A slot holds the
+            // stages [s, min(s + G, s1)) of one tile: one copy of their
+            // weights, one of their activations.
             int pre = 0;
             {
                 int g = 0;
                 for (int t = cid; t < a.T && g < ST; t += NC) {
-                    for (int s = s0; s < s1 && g < ST; ++s, ++g) {
-                        uint8_t* base = smem + g * sbytes;
-                        ptx::mbar_arrive_expect_tx(&full[g], (uint32_t)sbytes);
-                        ptx::bulk_g2s(base, a.a + ((size_t)t * a.S + s) * A_STAGE, A_STAGE, &full[g]);
-                        if (KIND == KIND_MX)
-                            ptx::bulk_g2s(base + A_STAGE + N * 128, a.sfa + ((size_t)t * a.S + s) * SF_STAGE,
-                                          SF_STAGE, &full[g]);
+                    for (int s = s0; s < s1 && g < ST; s += G, ++g) {
+                        const int n = min(G, s1 - s);
+                        ptx::mbar_arrive_expect_tx(&full[g], (uint32_t)(n * (WS + BS)));
+                        ptx::bulk_g2s(smem + g * sbytes, a.a + ((size_t)t * a.S + s) * WS, (uint32_t)(n * WS),
+                                      &full[g]);
                     }
                 }
                 pre = g;
@@ -384,24 +401,18 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
             ptx::grid_dependency_wait();
             int g = 0;
             for (int t = cid; t < a.T && ok; t += NC) {
-                for (int s = s0; s < s1; ++s, ++g) {
-                    const int slot = g % ST;
+                for (int s = s0; s < s1; s += G, ++g) {
+                    const int slot = g % ST, n = min(G, s1 - s);
                     uint8_t* base = smem + slot * sbytes;
                     if (g >= pre) {
                         if (g >= ST && !ptx::mbar_wait(&empty[slot], ((g / ST) - 1) & 1, WAIT_LIMIT)) {
                             ok = false;
                             break;
                         }
-                        ptx::mbar_arrive_expect_tx(&full[slot], (uint32_t)sbytes);
-                        ptx::bulk_g2s(base, a.a + ((size_t)t * a.S + s) * A_STAGE, A_STAGE, &full[slot]);
-                        if (KIND == KIND_MX)
-                            ptx::bulk_g2s(base + A_STAGE + N * 128, a.sfa + ((size_t)t * a.S + s) * SF_STAGE,
-                                          SF_STAGE, &full[slot]);
+                        ptx::mbar_arrive_expect_tx(&full[slot], (uint32_t)(n * (WS + BS)));
+                        ptx::bulk_g2s(base, a.a + ((size_t)t * a.S + s) * WS, (uint32_t)(n * WS), &full[slot]);
                     }
-                    ptx::bulk_g2s(base + A_STAGE, a.b + (size_t)s * N * 128, (uint32_t)(N * 128), &full[slot]);
-                    if (KIND == KIND_MX)
-                        ptx::bulk_g2s(base + A_STAGE + N * 128 + SF_STAGE, a.sfb + (size_t)s * SF_STAGE,
-                                      SF_STAGE, &full[slot]);
+                    ptx::bulk_g2s(base + G * WS, a.b + (size_t)s * BS, (uint32_t)(n * BS), &full[slot]);
                 }
             }
             // every load is issued: the next kernel may start prefetching
@@ -420,7 +431,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                 }
                 ptx::tc_fence_after();
                 const uint32_t d_tmem = tmem + ACC_COL + buf * 64;
-                for (int s = s0; s < s1; ++s, ++g) {
+                for (int s = s0; s < s1; s += G, ++g) {
                     const int slot = g % ST;
                     if (!ptx::mbar_wait(&full[slot], (g / ST) & 1, WAIT_LIMIT)) {
                         ok = false;
@@ -428,30 +439,35 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                     }
                     ptx::tc_fence_after();
                     uint8_t* base = smem + slot * sbytes;
-                    const uint32_t a_addr = ptx::smem_u32(base);
-                    const uint32_t b_addr = ptx::smem_u32(base + A_STAGE);
-                    if (KIND == KIND_MX) {
-                        const uint32_t sfa_addr = ptx::smem_u32(base + A_STAGE + N * 128);
-                        const uint32_t sfb_addr = sfa_addr + SF_STAGE;
-                        ptx::tmem_cp_32x128b_warpx4(tmem + SFA_COL, ptx::smem_desc(sfa_addr, 16, 128, 0));
-                        ptx::tmem_cp_32x128b_warpx4(tmem + SFA_COL + 4, ptx::smem_desc(sfa_addr + 512, 16, 128, 0));
-                        ptx::tmem_cp_32x128b_warpx4(tmem + SFB_COL, ptx::smem_desc(sfb_addr, 16, 128, 0));
-                        ptx::tmem_cp_32x128b_warpx4(tmem + SFB_COL + 4, ptx::smem_desc(sfb_addr + 512, 16, 128, 0));
-                    }
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        // 32 bytes of K per instruction: 64 E2M1 codes or 16 bf16 values
-                        const uint64_t ad = ptx::smem_desc(a_addr + 32 * q, 16, 1024, 2);
-                        const uint64_t bd = ptx::smem_desc(b_addr + 32 * q, 16, 1024, 2);
+                    const int n = min(G, s1 - s);
+                    for (int i = 0; i < n; ++i) {
+                        const uint32_t a_addr = ptx::smem_u32(base + i * WS);
+                        const uint32_t b_addr = ptx::smem_u32(base + G * WS + i * BS);
                         if (KIND == KIND_MX) {
-                            const uint32_t sf_id = (uint32_t)(q & 1) * 2;
-                            const uint32_t sfa_t = (tmem + SFA_COL + (q >> 1) * 4) | (sf_id << 30);
-                            const uint32_t sfb_t = (tmem + SFB_COL + (q >> 1) * 4) | (sf_id << 30);
-                            ptx::mma_mxf4(d_tmem, ad, bd, ptx::mxf4_idesc(128, (uint32_t)N, sf_id, sf_id), sfa_t,
-                                          sfb_t, (s > s0 || q > 0) ? 1u : 0u);
-                        } else {
-                            ptx::mma_bf16(d_tmem, ad, bd, ptx::bf16_idesc(128, (uint32_t)N),
-                                          (s > s0 || q > 0) ? 1u : 0u);
+                            const uint32_t sfa_addr = a_addr + A_STAGE;
+                            const uint32_t sfb_addr = b_addr + N * 128;
+                            ptx::tmem_cp_32x128b_warpx4(tmem + SFA_COL, ptx::smem_desc(sfa_addr, 16, 128, 0));
+                            ptx::tmem_cp_32x128b_warpx4(tmem + SFA_COL + 4,
+                                                        ptx::smem_desc(sfa_addr + 512, 16, 128, 0));
+                            ptx::tmem_cp_32x128b_warpx4(tmem + SFB_COL, ptx::smem_desc(sfb_addr, 16, 128, 0));
+                            ptx::tmem_cp_32x128b_warpx4(tmem + SFB_COL + 4,
+                                                        ptx::smem_desc(sfb_addr + 512, 16, 128, 0));
+                        }
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            // 32 bytes of K per instruction: 64 E2M1 codes or 16 bf16 values
+                            const uint64_t ad = ptx::smem_desc(a_addr + 32 * q, 16, 1024, 2);
+                            const uint64_t bd = ptx::smem_desc(b_addr + 32 * q, 16, 1024, 2);
+                            const uint32_t acc = (s + i > s0 || q > 0) ? 1u : 0u;
+                            if (KIND == KIND_MX) {
+                                const uint32_t sf_id = (uint32_t)(q & 1) * 2;
+                                const uint32_t sfa_t = (tmem + SFA_COL + (q >> 1) * 4) | (sf_id << 30);
+                                const uint32_t sfb_t = (tmem + SFB_COL + (q >> 1) * 4) | (sf_id << 30);
+                                ptx::mma_mxf4(d_tmem, ad, bd, ptx::mxf4_idesc(128, (uint32_t)N, sf_id, sf_id),
+                                              sfa_t, sfb_t, acc);
+                            } else {
+                                ptx::mma_bf16(d_tmem, ad, bd, ptx::bf16_idesc(128, (uint32_t)N), acc);
+                            }
                         }
                     }
                     ptx::tc_commit(&empty[slot]);
@@ -541,30 +557,33 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
             if (lane == 0) ptx::mbar_arrive(&tempty[buf]);
 
             if (ks > 1) {
-                // slot layout [row][sst]: a row's partials for 4 tokens are one 16-byte word
-                const int sst = (a.mcap + 3) & ~3;
+                const bool more = t + NC < a.T;  // this cluster has another tile
                 if (kc > 0) {
-                    // publish this K slice's partial to the leader
+                    // push this K slice's partial into the leader's buffer
                     if (j > 0 && !ptx::mbar_wait_cluster(&slot_free, (j - 1) & 1, WAIT_LIMIT)) ok = false;
+                    const uint32_t bar = ptx::mapa(ptx::smem_u32(&red_full), 0);
+                    const uint32_t dst =
+                        ptx::mapa(ptx::smem_u32(red + ((size_t)(kc - 1) * RB * 128 + row) * 4), 0);
 #pragma unroll
                     for (int m4 = 0; m4 < MX_MAXTOK; m4 += 4)
                         if (m4 < a.mcap)
-                            *(float4*)(slot + row * sst + m4) =
-                                make_float4(val[m4], val[m4 + 1], val[m4 + 2], val[m4 + 3]);
-                    __syncwarp();
-                    if (lane == 0) ptx::mbar_arrive_remote(ptx::mapa(ptx::smem_u32(&red_full), 0));
+                            ptx::st_async_v4(dst + (uint32_t)(m4 / 4) * 128 * 16,
+                                             make_float4(val[m4], val[m4 + 1], val[m4 + 2], val[m4 + 3]), bar);
+                    // the leader's four warps free the buffer before the next tile
+                    if (more && threadIdx.x == 64) ptx::mbar_arrive_expect_tx(&slot_free, 16);
                     continue;
                 }
+                if (threadIdx.x == 64) ptx::mbar_arrive_expect_tx(&red_full, (uint32_t)((ks - 1) * RB * 128 * 16));
                 if (!ptx::mbar_wait_cluster(&red_full, j & 1, WAIT_LIMIT)) ok = false;
-                const uint32_t mine = ptx::smem_u32(slot) + (uint32_t)(row * sst) * 4;
 #pragma unroll
                 for (int m4 = 0; m4 < MX_MAXTOK; m4 += 4) {
                     if (m4 >= a.mcap) continue;
-                    // every rank's word first (one round trip), then the sums in rank order
+                    // every rank's word first, then the sums in rank order
                     float4 part[MX_MAXCLUSTER - 1];
 #pragma unroll
                     for (int r = 1; r < MX_MAXCLUSTER; ++r)
-                        if (r < ks) part[r - 1] = ptx::ld_shared_cluster_v4(ptx::mapa(mine + (uint32_t)m4 * 4, (uint32_t)r));
+                        if (r < ks)
+                            part[r - 1] = *(const float4*)(red + (((size_t)(r - 1) * RB + m4 / 4) * 128 + row) * 4);
 #pragma unroll
                     for (int r = 1; r < MX_MAXCLUSTER; ++r) {
                         if (r >= ks) continue;
@@ -574,11 +593,11 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                         val[m4 + 3] = __fadd_rn(val[m4 + 3], part[r - 1].w);
                     }
                 }
-                // the other ranks only wait for their slot when this cluster has
-                // another tile; at exit the cluster barrier keeps every slot alive
+                // this warp has read its rows: one 4-byte store per peer
                 __syncwarp();
-                if (lane == 0 && t + NC < a.T)
-                    for (int r = 1; r < ks; ++r) ptx::mbar_arrive_remote(ptx::mapa(ptx::smem_u32(&slot_free), r));
+                if (more && lane >= 1 && lane < ks)
+                    ptx::st_async_u32(ptx::mapa(ptx::smem_u32(&free_sig), (uint32_t)lane), 0u,
+                                      ptx::mapa(ptx::smem_u32(&slot_free), (uint32_t)lane));
             }
             if (a.part_in) {  // input RMSNorm: scale by 1 / the row's RMS (lib.rs:268-290)
 #pragma unroll
@@ -614,8 +633,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                             if (m < a.mcap) xs[m][row] = val[m];
                     }
                     epi_bar();
-                    mx::emit_pieces_smem(&xs[0][0], 64, 2, 0, a.mcap, a.mcap, row, 128, t * 64, a.bN, a.bout,
-                                         a.sfout);
+                    mx::emit_pieces_smem(&xs[0][0], 64, 2, 0, a.mcap, a.mcap, row, 128, t * 64, a.bN, a.bout);
                 }
                 epi_bar();  // xs is reused by the next unit
             } else if (EPI == MX_QKV) {
@@ -743,8 +761,8 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
                     for (int m = 0; m < MX_MAXTOK; ++m)
                         if (m < a.mcap) slot[m * 128 + row] = __fmul_rn(val[m], wnext);
                     epi_bar();
-                    mx::emit_pieces_smem(slot, 128, 4, 0, a.mcap, a.mcap, row, 128, t * TILE_ROWS, a.bN, a.bout,
-                                         a.sfout);
+                    mx::emit_pieces_smem(slot, 128, 4, 0, a.mcap, a.mcap, row, 128, t * TILE_ROWS, a.bN,
+                                         a.bout);
                     epi_bar();  // the staging area is reused by the next tile
                 }
                 if (a.part_out) {  // sum of squares of this tile's 128 outputs, per row
@@ -761,7 +779,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
     ptx::launch_dependents();
     ptx::tc_fence_before();
     __syncthreads();
-    if (ks > 1) {  // no CTA leaves while a peer may still read its slot
+    if (ks > 1) {  // no CTA leaves while a store to or from it may be in flight
         ptx::cluster_arrive();
         ptx::cluster_wait();
     }
@@ -803,8 +821,7 @@ __device__ __forceinline__ bool tile_row(const TileSrc& src, int swiglu, int t, 
     return false;
 }
 
-__global__ void k_mx_tile(TileSrc src, int swiglu, int K, int T, int S, uint8_t* __restrict__ a,
-                          uint8_t* __restrict__ sfa) {
+__global__ void k_mx_tile(TileSrc src, int swiglu, int K, int T, int S, uint8_t* __restrict__ a) {
     const size_t chunks = (size_t)T * S * TILE_ROWS * 8;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < chunks;
          i += (size_t)gridDim.x * blockDim.x) {
@@ -821,9 +838,9 @@ __global__ void k_mx_tile(TileSrc src, int swiglu, int K, int T, int S, uint8_t*
             v = *reinterpret_cast<const uint4*>(src.packed[mat] + (size_t)local * (K / 2) + k0 / 2);
             sc = src.scales[mat][(size_t)local * (K / 32) + k0 / 32];
         }
-        uint8_t* tile = a + ((size_t)t * S + s) * A_STAGE;
+        uint8_t* tile = a + ((size_t)t * S + s) * w_stage(KIND_MX);
         *reinterpret_cast<uint4*>(tile + swz128((uint32_t)r, (uint32_t)c16 * 16)) = v;
-        sfa[((size_t)t * S + s) * SF_STAGE + sf_offset((uint32_t)r, (uint32_t)c16)] = sc;
+        tile[A_STAGE + sf_offset((uint32_t)r, (uint32_t)c16)] = sc;
     }
 }
 
@@ -844,18 +861,19 @@ int mx_clusters(int ks) {
 // wait, the rest stream at its share of HBM bandwidth (at most what one SM
 // pulls); a tile costs about a microsecond of epilogue, and a split the
 // reduction through distributed shared memory.  The choice depends only on
-// the matrix shape, never on the token count.
+// the matrix shape, never on the token count.  A split holds at least one
+// two-stage slot.
 constexpr int MX_PREFETCH = 4;           // ring stages issued before the dependency wait
 constexpr double MX_STAGE_KB = 17.0;     // weight bytes of a stage (codes + scales)
 constexpr double MX_HBM_GBS = 6000.0;
-constexpr double MX_SM_GBS = 120.0;
+constexpr double MX_SM_GBS = 60.0;       // one CTA's copy rate with two-stage copies
 constexpr double MX_EPI_US = 1.0;
 constexpr double MX_REDUCE_US = 1.5;
 
 int mx_ksplit(int T, int S) {
     int best = 1;
     double best_cost = 1e30;
-    for (int ks = 1; ks <= std::min(S, MX_MAXCLUSTER); ++ks) {
+    for (int ks = 1; ks <= std::min((S + 1) / 2, MX_MAXCLUSTER); ++ks) {
         const int nc = std::min(mx_clusters(ks), T);
         const int tiles = (T + nc - 1) / nc;            // per cluster
         const int stages = tiles * ((S + ks - 1) / ks);  // per CTA
@@ -870,27 +888,33 @@ int mx_ksplit(int T, int S) {
     return best;
 }
 
-// Ring depth and accumulator buffers for N MMA columns: two accumulators of
-// up to 64 columns, or one of up to 128; about 105 KB of stages, so a CTA of
-// the next projection fits on the same SM (programmatic dependent launch).
-void mx_shape(int N, int* stages, int* nbuf) {
+// Ring slots, stages per slot and accumulator buffers for N MMA columns:
+// two accumulators of up to 64 columns and two slots of two stages, or one
+// accumulator of up to 128 and three one-stage slots; at most about 105 KB
+// of ring, so a CTA of the next projection fits on the same SM
+// (programmatic dependent launch).
+void mx_shape(int N, int* stages, int* nbuf, int* group) {
     *nbuf = N <= 64 ? 2 : 1;
-    *stages = N <= 64 ? 4 : 3;
+    *stages = N <= 64 ? 2 : 3;
+    *group = N <= 64 ? 2 : 1;
 }
 
-// Stages, then the split-K slot (N / 8 rows x 128 f32), then alignment slack.
-// Stages, then the split-K slot (mcap rows x 128 f32), then alignment slack.
-size_t mx_smem(int N, int kind, int mcap) {
-    int st, nb;
-    mx_shape(N, &st, &nb);
-    return (size_t)st * mx_stage_bytes(N, kind) + (size_t)((mcap + 3) & ~3) * 512 + 1024;
+// Ring slots, epilogue scratch (mcap rows rounded up to 4, x 128 f32), the
+// leader's split-K buffer (ks - 1 partials of the same size), then alignment
+// slack.  At five rows and up to four-way splits this stays under half an SM.
+size_t mx_smem(int N, int kind, int mcap, int ks) {
+    int st, nb, gr;
+    mx_shape(N, &st, &nb, &gr);
+    const size_t part = (size_t)((mcap + 3) & ~3) * 512;
+    return (size_t)st * mx_slot_bytes(N, kind, gr) + part * ks + 1024;
 }
 
 constexpr int MX_PROBE_SMEM = 120 * 1024;  // more than half an SM: one CTA per SM
 
 template <int EPI, int KIND>
 jl_status configure_mx() {
-    const size_t most = std::max(mx_smem(64, KIND, MX_MAXTOK), mx_smem(8 * MX_MAXTOK, KIND, MX_MAXTOK));
+    const size_t most = std::max(mx_smem(64, KIND, MX_MAXTOK, MX_MAXCLUSTER),
+                                 mx_smem(8 * MX_MAXTOK, KIND, MX_MAXTOK, MX_MAXCLUSTER));
     JL_CUDA(cudaFuncSetAttribute(k_mx_gemv<EPI, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)std::max<size_t>(MX_PROBE_SMEM, most)));
     JL_CUDA(cudaFuncSetAttribute(k_mx_gemv<EPI, KIND>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
@@ -903,7 +927,7 @@ jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(nc * a.ksplit);
     cfg.blockDim = dim3(MX_THREADS);
-    cfg.dynamicSmemBytes = mx_smem(a.N, KIND, a.mcap);
+    cfg.dynamicSmemBytes = mx_smem(a.N, KIND, a.mcap, a.ksplit);
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1001,13 +1025,11 @@ jl_status mx_build(const Mat* const* mats, int nmats, bool swiglu, uint8_t* dst,
     p.swiglu = swiglu;
     p.out_rows = out_rows;
     p.a = dst;
-    p.sfa = dst + (size_t)p.T * p.S * A_STAGE;
     p.ksplit = mx_ksplit(p.T, p.S);
     (void)sms;
     const size_t chunks = (size_t)p.T * p.S * TILE_ROWS * 8;
     const int grid = (int)std::min<size_t>((chunks + 255) / 256, (size_t)sms * 8);
-    k_mx_tile<<<grid, 256, 0, stream>>>(src, swiglu ? 1 : 0, K, p.T, p.S, (uint8_t*)p.a,
-                                        (uint8_t*)p.sfa);
+    k_mx_tile<<<grid, 256, 0, stream>>>(src, swiglu ? 1 : 0, K, p.T, p.S, (uint8_t*)p.a);
     JL_CUDA(cudaGetLastError());
     *out = p;
     return JL_OK;
@@ -1025,19 +1047,16 @@ jl_status mx_project(const PassCtx& c, const MxProj& p, int epi, int use_head, c
     (void)norm;  // inputs arrive normalised; see launch_rmsnorm
     const int items = mcap * p.S * (STAGE_K / 32);
     JL_TRY(launch_pdl(k_mx_pieces, dim3((items + 7) / 8), dim3(256), 0, c.stream,
-                      (const PassHdr*)m->pass.hdr, use_head, mcap, x, ldx, p.K, p.S, N, m->mx.bimg,
-                      m->mx.sfb));
+                      (const PassHdr*)m->pass.hdr, use_head, mcap, x, ldx, p.K, p.S, N, m->mx.bimg));
     MxArgs a = {};
     a.a = p.a;
-    a.sfa = p.sfa;
     a.b = m->mx.bimg;
-    a.sfb = m->mx.sfb;
     a.T = p.T;
     a.S = p.S;
     a.ksplit = p.ksplit;
     a.N = N;
     a.mcap = mcap;
-    mx_shape(N, &a.stages, &a.nbuf);
+    mx_shape(N, &a.stages, &a.nbuf, &a.group);
     a.hdr = m->pass.hdr;
     a.use_head = use_head;
     a.y = y;
@@ -1050,14 +1069,14 @@ jl_status mx_project(const PassCtx& c, const MxProj& p, int epi, int use_head, c
 }
 
 jl_status mx_norm_pieces(const PassCtx& c, const float* x, int ldx, const uint16_t* w, int width,
-                         uint8_t* bout, uint8_t* sfout, float* part) {
+                         uint8_t* bout, float* part) {
     const int mcap = c.rows_cap;
     if (mcap < 1 || mcap > MX_MAXTOK || width % STAGE_K) {
         set_error("norm pieces take 1..%d rows and a width that is a multiple of %d", MX_MAXTOK, STAGE_K);
         return JL_ERR_INVALID_ARG;
     }
     return launch_pdl(k_norm_pieces, dim3(width / 128, mcap), dim3(128), 0, c.stream,
-                      (const PassHdr*)c.m->pass.hdr, mcap, x, ldx, w, width, PIECES * mcap, bout, sfout, part);
+                      (const PassHdr*)c.m->pass.hdr, mcap, x, ldx, w, width, PIECES * mcap, bout, part);
 }
 
 jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxFuse& f, float* y,
@@ -1071,15 +1090,13 @@ jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxF
     const int N = PIECES * mcap;
     MxArgs a = {};
     a.a = p.a;
-    a.sfa = p.sfa;
     a.b = f.b;
-    a.sfb = f.sfb;
     a.T = p.T;
     a.S = p.S;
     a.ksplit = p.ksplit;
     a.N = N;
     a.mcap = mcap;
-    mx_shape(N, &a.stages, &a.nbuf);
+    mx_shape(N, &a.stages, &a.nbuf, &a.group);
     a.hdr = m->pass.hdr;
     a.use_head = 0;
     a.y = y;
@@ -1092,7 +1109,6 @@ jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxF
     a.part_tiles = f.part_tiles;
     a.norm_width = f.norm_width;
     a.bout = f.bout;
-    a.sfout = f.sfout;
     a.bN = N;
     a.part_out = f.part_out;
     a.next_w = f.next_w;
@@ -1113,10 +1129,9 @@ MxScratchPlan mx_scratch_plan(const MxProj& p, int mcap) {
     auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
     MxScratchPlan s;
     s.tickets = up((size_t)p.T * sizeof(int));
-    s.sfb = up((size_t)p.S * SF_STAGE);
-    s.bimg = up((size_t)p.S * PIECES * mcap * 128);
+    s.bimg = up((size_t)p.S * mx::img_stage(PIECES * mcap));
     s.ws = p.ksplit > 1 ? up((size_t)p.T * p.ksplit * mcap * 128 * sizeof(float)) : 0;
-    s.total = s.tickets + s.sfb + s.bimg + s.ws;
+    s.total = s.tickets + s.bimg + s.ws;
     return s;
 }
 
@@ -1129,24 +1144,21 @@ jl_status mx_project_with(const MxProj& p, int epi, const PassHdr* hdr, int mcap
     }
     const MxScratchPlan plan = mx_scratch_plan(p, mcap);
     int* tickets = (int*)scratch;
-    uint8_t* sfb = scratch + plan.tickets;
-    uint8_t* bimg = sfb + plan.sfb;
+    uint8_t* bimg = scratch + plan.tickets;
     float* ws = (float*)(bimg + plan.bimg);
     const int N = PIECES * mcap;
     const int items = mcap * p.S * (STAGE_K / 32);
     JL_TRY(launch_pdl(k_mx_pieces, dim3((items + 7) / 8), dim3(256), 0, stream, hdr, 0, mcap, x, ldx,
-                      p.K, p.S, N, bimg, sfb));
+                      p.K, p.S, N, bimg));
     MxArgs a = {};
     a.a = p.a;
-    a.sfa = p.sfa;
     a.b = bimg;
-    a.sfb = sfb;
     a.T = p.T;
     a.S = p.S;
     a.ksplit = p.ksplit;
     a.N = N;
     a.mcap = mcap;
-    mx_shape(N, &a.stages, &a.nbuf);
+    mx_shape(N, &a.stages, &a.nbuf, &a.group);
     a.hdr = hdr;
     a.use_head = 0;
     a.y = y;
@@ -1174,7 +1186,6 @@ jl_status mx_build_bf16(const Mat& w, uint8_t* dst, MxProj* out, cudaStream_t st
     p.K = w.cols;
     p.out_rows = w.rows;
     p.a = dst;
-    p.sfa = nullptr;
     p.ksplit = mx_ksplit(p.T, p.S);
     const size_t chunks = (size_t)p.T * p.S * TILE_ROWS * 8;
     const int grid = (int)std::min<size_t>((chunks + 255) / 256, 148 * 8);
@@ -1203,7 +1214,7 @@ jl_status mx_head_fused(const PassCtx& c, const MxProj& p, const uint16_t* norm,
     a.ksplit = p.ksplit;
     a.N = N;
     a.mcap = mcap;
-    mx_shape(N, &a.stages, &a.nbuf);
+    mx_shape(N, &a.stages, &a.nbuf, &a.group);
     a.hdr = m->pass.hdr;
     a.use_head = 1;
     a.y = logits;

@@ -6,13 +6,15 @@
 // pieces carry an activation with relative error about 3e-8.
 //
 // Image layout for a projection with K input elements and N = PIECES * rows
-// MMA columns: S = K / STAGE_K stages, stage s holding
+// MMA columns: S = K / STAGE_K stages of img_stage(N) bytes each, stage s
+// holding
 //   * N rows x 128 bytes of E2M1 codes (two per byte, even element in the
 //     low nibble), row n = PIECES * token + piece, in the 128-byte-swizzled
 //     K-major layout the MMA descriptor reads (swz128);
-//   * one 1 KB scale region: two 512-byte atoms, byte sf_offset(n, kb) = the
-//     E8M0 exponent of block kb (0..7) of row n, the layout tcgen05.cp
-//     32x128b.warpx4 broadcasts into TMEM.
+//   * right after them, one 1 KB scale region: two 512-byte atoms, byte
+//     sf_offset(n, kb) = the E8M0 exponent of block kb (0..7) of row n, the
+//     layout tcgen05.cp 32x128b.warpx4 broadcasts into TMEM.
+// Consecutive stages are contiguous, so a run of them is one bulk copy.
 // Any kernel holding one 32-element block in a warp (one element per lane)
 // emits its pieces with emit_pieces / emit_pieces_all.
 #pragma once
@@ -29,6 +31,10 @@ constexpr int PIECES = 8;
 constexpr int STAGE_K = 256;   // K elements per pipeline stage
 constexpr int SF_STAGE = 1024;  // two scale atoms
 
+// Bytes of one stage of an activation image with N MMA columns (N % 8 == 0
+// keeps every stage 1024-byte aligned, as the swizzled layout needs).
+__host__ __device__ constexpr int img_stage(int N) { return N * 128 + SF_STAGE; }
+
 __device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t byte) {
     // byte offset of (row, byte-in-row) in a 128B-swizzled K-major image
     return (row >> 3) * 1024 + (row & 7) * 128 + ((((byte >> 4) ^ (row & 7)) & 7) << 4) + (byte & 15);
@@ -44,17 +50,19 @@ __device__ __forceinline__ float pow2i(int e) {
     return e >= -126 ? __uint_as_float((uint32_t)(e + 127) << 23) : __uint_as_float(0x00400000u);
 }
 
-// Smallest E8M0 exponent e with amax <= 6 * 2^e (amax >= 0), clamped to the
-// E8M0 range; -127 for an all-zero block.
+// Smallest E8M0 exponent e with amax <= 6 * 2^e (amax >= 0, finite),
+// clamped below at -127; -127 for an all-zero block.  amax = 1.f * 2^(eb-127):
+// 6 * 2^(eb-129) = 1.5 * 2^(eb-127) suffices when the significand is at most
+// 1.5, else 2^(eb-128) * 6 = 3 * 2^(eb-127) does.  Zero and subnormal amax
+// (eb = 0) land below -127 and are clamped: 6 * 2^-127 covers them.
 __device__ __forceinline__ int piece_exponent(float amax) {
     const uint32_t b = __float_as_uint(amax);
-    const int eb = (int)((b >> 23) & 0xFF);
-    if (eb == 0) return -127;  // zero or subnormal: 6 * 2^-127 covers it
-    // amax = 1.f * 2^(eb-127): 6 * 2^(eb-130) = 0.75 * 2^(eb-127) suffices when
-    // the significand is at most 1.5
-    const int e = (b & 0x7FFFFFu) <= 0x400000u ? eb - 129 : eb - 128;
-    return e < -127 ? -127 : (e > 127 ? 127 : e);
+    const int e = (int)(b >> 23) - 129 + ((b & 0x7FFFFFu) > 0x400000u ? 1 : 0);
+    return max(e, -127);
 }
+
+// 2^-e for e from piece_exponent (e <= 126, so 2^-e is a normal float).
+__device__ __forceinline__ float pow2_neg(int e) { return __uint_as_float((uint32_t)(127 - e) << 23); }
 
 // max |v| over the warp: non-negative floats order like their bit patterns,
 // so one redux.sync does it.
@@ -77,16 +85,15 @@ __device__ __forceinline__ float e2m1_level(uint32_t c) {
 
 // The pieces of one 32-element block (lane i holds element k0 + i) for MT
 // tokens at once: token m0 + m has its values in r[m] and is written when
-// m < count.  Output goes to the image at (bimg, sfb) for N MMA columns.
+// m < count.  Output goes to the image at bimg for N MMA columns.
 // Tokens advance through the pieces together, so their dependent chains
 // overlap.  k0 is a multiple of 32.  The whole warp calls it.
 template <int MT>
 __device__ __forceinline__ void emit_pieces_rows(float (&r)[MT], int m0, int count, int lane, int k0,
-                                                 int N, uint8_t* __restrict__ bimg,
-                                                 uint8_t* __restrict__ sfb) {
+                                                 int N, uint8_t* __restrict__ bimg) {
     const int s = k0 / STAGE_K, kbl = (k0 % STAGE_K) / 32;
-    uint8_t* img = bimg + (size_t)s * N * 128;
-    uint8_t* sf = sfb + (size_t)s * SF_STAGE;
+    uint8_t* img = bimg + (size_t)s * img_stage(N);
+    uint8_t* sf = img + N * 128;
     const uint32_t byte = (uint32_t)(kbl * 16 + (lane >> 1));
 #pragma unroll 1
     for (int p = 0; p < PIECES; ++p) {
@@ -108,61 +115,60 @@ __device__ __forceinline__ void emit_pieces_rows(float (&r)[MT], int m0, int cou
 
 // One token's block.
 __device__ __forceinline__ void emit_pieces(float r, int lane, int m, int k0, int N,
-                                            uint8_t* __restrict__ bimg, uint8_t* __restrict__ sfb) {
+                                            uint8_t* __restrict__ bimg) {
     float rr[1] = {r};
-    emit_pieces_rows<1>(rr, m, 1, lane, k0, N, bimg, sfb);
+    emit_pieces_rows<1>(rr, m, 1, lane, k0, N, bimg);
 }
 
 // Token buckets: the pieces of tokens 0..count-1 (count <= 16) of one block,
 // with the token loop unrolled to the smallest bucket of 1, 2, 4, 8 or 16.
 __device__ __forceinline__ void emit_pieces_all(const float (&v)[16], int count, int lane, int k0, int N,
-                                                uint8_t* __restrict__ bimg, uint8_t* __restrict__ sfb) {
+                                                uint8_t* __restrict__ bimg) {
     if (count <= 1) {
         float r[1] = {v[0]};
-        emit_pieces_rows<1>(r, 0, count, lane, k0, N, bimg, sfb);
+        emit_pieces_rows<1>(r, 0, count, lane, k0, N, bimg);
     } else if (count <= 2) {
         float r[2] = {v[0], v[1]};
-        emit_pieces_rows<2>(r, 0, count, lane, k0, N, bimg, sfb);
+        emit_pieces_rows<2>(r, 0, count, lane, k0, N, bimg);
     } else if (count <= 4) {
         float r[4] = {v[0], v[1], v[2], v[3]};
-        emit_pieces_rows<4>(r, 0, count, lane, k0, N, bimg, sfb);
+        emit_pieces_rows<4>(r, 0, count, lane, k0, N, bimg);
     } else if (count <= 8) {
         float r[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) r[i] = v[i];
-        emit_pieces_rows<8>(r, 0, count, lane, k0, N, bimg, sfb);
+        emit_pieces_rows<8>(r, 0, count, lane, k0, N, bimg);
     } else {
         float r[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) r[i] = v[i];
-        emit_pieces_rows<16>(r, 0, count, lane, k0, N, bimg, sfb);
+        emit_pieces_rows<16>(r, 0, count, lane, k0, N, bimg);
     }
 }
 
 // Tokens m0 .. m0+count-1 of one block whose values sit in shared memory,
 // vals[m][col] (row stride `ld` floats), bucketed like emit_pieces_all.
 __device__ __forceinline__ void emit_pieces_range(const float* vals, int ld, int col, int m0, int count,
-                                                  int lane, int k0, int N, uint8_t* __restrict__ bimg,
-                                                  uint8_t* __restrict__ sfb) {
+                                                  int lane, int k0, int N, uint8_t* __restrict__ bimg) {
     if (count <= 0) return;
     if (count <= 1) {
         float r[1] = {vals[m0 * ld + col]};
-        emit_pieces_rows<1>(r, m0, count, lane, k0, N, bimg, sfb);
+        emit_pieces_rows<1>(r, m0, count, lane, k0, N, bimg);
     } else if (count <= 2) {
         float r[2];
 #pragma unroll
         for (int i = 0; i < 2; ++i) r[i] = vals[(m0 + i) * ld + col];
-        emit_pieces_rows<2>(r, m0, count, lane, k0, N, bimg, sfb);
+        emit_pieces_rows<2>(r, m0, count, lane, k0, N, bimg);
     } else if (count <= 4) {
         float r[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) r[i] = i < count ? vals[(m0 + i) * ld + col] : 0.f;
-        emit_pieces_rows<4>(r, m0, count, lane, k0, N, bimg, sfb);
+        emit_pieces_rows<4>(r, m0, count, lane, k0, N, bimg);
     } else {
         float r[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) r[i] = i < count ? vals[(m0 + i) * ld + col] : 0.f;
-        emit_pieces_rows<8>(r, m0, count, lane, k0, N, bimg, sfb);
+        emit_pieces_rows<8>(r, m0, count, lane, k0, N, bimg);
     }
 }
 
@@ -190,8 +196,7 @@ __device__ __forceinline__ float2 e2m1x2_levels(uint32_t byte) {
 // them, all of each warp).
 __device__ __forceinline__ void emit_pieces_smem(const float* vals, int stride, int nblocks, int m0,
                                                  int count, int mcap, int tid, int nthreads, int k0,
-                                                 int N, uint8_t* __restrict__ bimg,
-                                                 uint8_t* __restrict__ sfb) {
+                                                 int N, uint8_t* __restrict__ bimg) {
     const int groups = mcap * nblocks;
     const int q = tid & 3;
     const int rounds = (groups + nthreads / 4 - 1) / (nthreads / 4);
@@ -211,17 +216,19 @@ __device__ __forceinline__ void emit_pieces_smem(const float* vals, int stride, 
         }
         const int kk = k0 + 32 * b;
         const int s = kk / STAGE_K, kbl = (kk % STAGE_K) / 32;
-        uint8_t* img = bimg + (size_t)s * N * 128;
-        uint8_t* sf = sfb + (size_t)s * SF_STAGE;
         float amax = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(r[i]));
-#pragma unroll 1
+        // the piece words stay in registers until the chain is done, so no
+        // store sits between one piece's residual and the next maximum
+        uint32_t words[PIECES];
+        int exps[PIECES];
+#pragma unroll
         for (int p = 0; p < PIECES; ++p) {
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
             const int e = piece_exponent(amax);
-            const float down = pow2i(-e), up = pow2i(e);
+            const float down = pow2_neg(e), up = pow2i(e);
             uint32_t word = 0;
             float next = 0.f;
 #pragma unroll
@@ -235,10 +242,17 @@ __device__ __forceinline__ void emit_pieces_smem(const float* vals, int stride, 
                 word |= byte << (8 * i);
             }
             amax = next;
-            if (live) {
+            words[p] = word;
+            exps[p] = e;
+        }
+        if (live) {
+            uint8_t* img = bimg + (size_t)s * img_stage(N);
+            uint8_t* sf = img + N * 128;
+#pragma unroll
+            for (int p = 0; p < PIECES; ++p) {
                 const uint32_t n = (uint32_t)((m0 + m) * PIECES + p);
-                *(uint32_t*)(img + swz128(n, (uint32_t)(kbl * 16 + 4 * q))) = word;
-                if (q == 0) sf[sf_offset(n, (uint32_t)kbl)] = (uint8_t)(e + 127);
+                *(uint32_t*)(img + swz128(n, (uint32_t)(kbl * 16 + 4 * q))) = words[p];
+                if (q == 0) sf[sf_offset(n, (uint32_t)kbl)] = (uint8_t)(exps[p] + 127);
             }
         }
     }

@@ -76,6 +76,21 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
                  : "memory");
 }
 
+// Asynchronous store into another CTA's shared memory (cluster addresses
+// from mapa): the bytes count against that CTA's mbarrier (complete_tx),
+// whose phase then makes them visible to its waiters.  The issuing thread
+// does not wait for it.
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float4 v, uint32_t cluster_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+                 ::"r"(cluster_addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(cluster_bar)
+                 : "memory");
+}
+__device__ __forceinline__ void st_async_u32(uint32_t cluster_addr, uint32_t v, uint32_t cluster_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.u32 [%0], %1, [%2];"
+                 ::"r"(cluster_addr), "r"(v), "r"(cluster_bar)
+                 : "memory");
+}
+
 // Wait (bounded) for a phase of a local mbarrier whose arrivals come from
 // other CTAs: acquire at cluster scope.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t limit) {
