@@ -56,11 +56,23 @@ __device__ __forceinline__ void dec_copy_rows(const DecTile& t, int r0, int n, i
 // layout; with `w` set, as the RMSNorm x / sqrt(mean(x^2) + 1e-6) * w
 // (lib.rs:268-290).  Whole CTA.
 // Each thread holds at most DEC_XCHUNKS float4 chunks of a row in registers,
-// so x is read from global memory once.
+// so x is read from global memory once.  The thread's norm weights (wv, from
+// dec_norm_weights) are fetched before the dependency wait: they never depend
+// on the previous kernel.
 constexpr int DEC_XCHUNKS = 4;
 
+__device__ __forceinline__ void dec_norm_weights(const uint16_t* __restrict__ w, int K,
+                                                 uint2 (&wv)[DEC_XCHUNKS]) {
+#pragma unroll
+    for (int i = 0; i < DEC_XCHUNKS; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        wv[i] = (w && c < K / 4) ? *reinterpret_cast<const uint2*>(w + 4 * c) : make_uint2(0u, 0u);
+    }
+}
+
 __device__ __forceinline__ void dec_load_x(const float* __restrict__ x, int ldx, int M, int K,
-                                           const uint16_t* __restrict__ w, float4* xs4, float* red) {
+                                           const uint16_t* __restrict__ w, const uint2 (&wv)[DEC_XCHUNKS],
+                                           float4* xs4, float* red) {
     const int K4 = K / 4;
     for (int m = 0; m < M; ++m) {
         const float* xr = x + (size_t)m * ldx;
@@ -90,60 +102,74 @@ __device__ __forceinline__ void dec_load_x(const float* __restrict__ x, int ldx,
             const int c = threadIdx.x + i * blockDim.x;
             if (c >= K4) continue;
             if (w) {
-                const uint2 wv = *reinterpret_cast<const uint2*>(w + 4 * c);
-                v[i].x = __fmul_rn(__fdiv_rn(v[i].x, size), bf16f(wv.x & 0xffffu));
-                v[i].y = __fmul_rn(__fdiv_rn(v[i].y, size), bf16f(wv.x >> 16));
-                v[i].z = __fmul_rn(__fdiv_rn(v[i].z, size), bf16f(wv.y & 0xffffu));
-                v[i].w = __fmul_rn(__fdiv_rn(v[i].w, size), bf16f(wv.y >> 16));
+                v[i].x = __fmul_rn(__fdiv_rn(v[i].x, size), bf16f(wv[i].x & 0xffffu));
+                v[i].y = __fmul_rn(__fdiv_rn(v[i].y, size), bf16f(wv[i].x >> 16));
+                v[i].z = __fmul_rn(__fdiv_rn(v[i].z, size), bf16f(wv[i].y & 0xffffu));
+                v[i].w = __fmul_rn(__fdiv_rn(v[i].w, size), bf16f(wv[i].y >> 16));
             }
             xs4[m * K4 + dec_swz(c)] = v[i];
         }
     }
 }
 
-// Dot products of one weight row (codes `wr`, scales `sr`, width K) with the
-// M staged input rows; every lane gets the totals.  Whole warp.
-template <int M>
-__device__ __forceinline__ void dec_dot(const uint8_t* wr, const uint8_t* sr, int K, const float4* xs4,
-                                        int lane, float (&out)[M]) {
+// Dot products of R weight rows (codes wr[i], scales sr[i], width K) with
+// the M staged input rows; every lane gets the totals out[i][m].  The rows'
+// dependent chains are independent, so one pass over K interleaves them;
+// each row's arithmetic is the same as on its own.  Whole warp.
+template <int R, int M>
+__device__ __forceinline__ void dec_dot(const uint8_t* const (&wr)[R], const uint8_t* const (&sr)[R], int K,
+                                        const float4* xs4, int lane, float (&out)[R][M]) {
     const int nb = K / 32, K4 = K / 4;
-    float acc[M];
+    float acc[R][M];
 #pragma unroll
-    for (int m = 0; m < M; ++m) acc[m] = 0.f;
+    for (int i = 0; i < R; ++i)
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[i][m] = 0.f;
     for (int b = lane; b < nb; b += 32) {
-        const uint4 w = *reinterpret_cast<const uint4*>(wr + (size_t)b * 16);
-        const float sc = e8m0(sr[b]);
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-        float part[M];
+        float4 xa[4][M], xb[4][M];
 #pragma unroll
-        for (int m = 0; m < M; ++m) part[m] = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {  // 8 codes = 8 elements per word
-            const float2 l01 = mx::e2m1x2_levels(words[q] & 0xffu);
-            const float2 l23 = mx::e2m1x2_levels((words[q] >> 8) & 0xffu);
-            const float2 l45 = mx::e2m1x2_levels((words[q] >> 16) & 0xffu);
-            const float2 l67 = mx::e2m1x2_levels(words[q] >> 24);
+        for (int q = 0; q < 4; ++q)
 #pragma unroll
             for (int m = 0; m < M; ++m) {
-                const float4 xa = xs4[m * K4 + dec_swz(b * 8 + 2 * q)];
-                const float4 xb = xs4[m * K4 + dec_swz(b * 8 + 2 * q + 1)];
-                float p = part[m];
-                p = fmaf(l01.x, xa.x, p);
-                p = fmaf(l01.y, xa.y, p);
-                p = fmaf(l23.x, xa.z, p);
-                p = fmaf(l23.y, xa.w, p);
-                p = fmaf(l45.x, xb.x, p);
-                p = fmaf(l45.y, xb.y, p);
-                p = fmaf(l67.x, xb.z, p);
-                p = fmaf(l67.y, xb.w, p);
-                part[m] = p;
+                xa[q][m] = xs4[m * K4 + dec_swz(b * 8 + 2 * q)];
+                xb[q][m] = xs4[m * K4 + dec_swz(b * 8 + 2 * q + 1)];
             }
-        }
 #pragma unroll
-        for (int m = 0; m < M; ++m) acc[m] = fmaf(part[m], sc, acc[m]);
+        for (int i = 0; i < R; ++i) {
+            const uint4 w = *reinterpret_cast<const uint4*>(wr[i] + (size_t)b * 16);
+            const float sc = e8m0(sr[i][b]);
+            const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+            float part[M];
+#pragma unroll
+            for (int m = 0; m < M; ++m) part[m] = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {  // 8 codes = 8 elements per word
+                const float2 l01 = mx::e2m1x2_levels(words[q] & 0xffu);
+                const float2 l23 = mx::e2m1x2_levels((words[q] >> 8) & 0xffu);
+                const float2 l45 = mx::e2m1x2_levels((words[q] >> 16) & 0xffu);
+                const float2 l67 = mx::e2m1x2_levels(words[q] >> 24);
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    float p = part[m];
+                    p = fmaf(l01.x, xa[q][m].x, p);
+                    p = fmaf(l01.y, xa[q][m].y, p);
+                    p = fmaf(l23.x, xa[q][m].z, p);
+                    p = fmaf(l23.y, xa[q][m].w, p);
+                    p = fmaf(l45.x, xb[q][m].x, p);
+                    p = fmaf(l45.y, xb[q][m].y, p);
+                    p = fmaf(l67.x, xb[q][m].z, p);
+                    p = fmaf(l67.y, xb[q][m].w, p);
+                    part[m] = p;
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < M; ++m) acc[i][m] = fmaf(part[m], sc, acc[i][m]);
+        }
     }
 #pragma unroll
-    for (int m = 0; m < M; ++m) out[m] = warp_sum(acc[m]);
+    for (int i = 0; i < R; ++i)
+#pragma unroll
+        for (int m = 0; m < M; ++m) out[i][m] = warp_sum(acc[i][m]);
 }
 
 // ---------------------------------------------------------------------------
@@ -192,38 +218,58 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
         if (EPI == DEC_SWIGLU)
             dec_copy_rows(a.w[1], r0, n, K, wsm + DEC_TR * (K / 2), ssm + DEC_TR * (K / 32), &bar);
     }
+    uint2 wv[DEC_XCHUNKS];
+    dec_norm_weights(a.norm, K, wv);
     __syncthreads();  // the barrier is initialised before anyone waits on it
     ptx::grid_dependency_wait();
     ptx::launch_dependents();
     const int rows = min(a.hdr->rows, a.mcap);
-    dec_load_x(a.x, K, M, K, a.norm, xs4, red);
+    dec_load_x(a.x, K, M, K, a.norm, wv, xs4, red);
     const bool ok = ptx::mbar_wait(&bar, 0, DEC_WAIT);
     __syncthreads();
     if (!ok) {
         if (threadIdx.x == 0) atomicOr(a.err, 4);
         return;
     }
-    for (int r = warp; r < n; r += 8) {
-        float o[M];
-        dec_dot<M>(wsm + (size_t)r * (K / 2), ssm + (size_t)r * (K / 32), K, xs4, lane, o);
-        if (EPI == DEC_SWIGLU) {
-            float u[M];
-            dec_dot<M>(wsm + (size_t)(DEC_TR + r) * (K / 2), ssm + (size_t)(DEC_TR + r) * (K / 32), K, xs4,
-                       lane, u);
-            if (lane == 0)
+    // warp w owns tile rows w and w + 8 (rows past n are computed from
+    // unloaded shared memory and dropped)
+    static_assert(DEC_TR == 16, "two rows per warp of an 8-warp CTA");
+    const int ra = warp, rb = warp + 8;
+    if (EPI == DEC_SWIGLU) {
+        const uint8_t* const wr[4] = {wsm + (size_t)ra * (K / 2), wsm + (size_t)rb * (K / 2),
+                                      wsm + (size_t)(DEC_TR + ra) * (K / 2), wsm + (size_t)(DEC_TR + rb) * (K / 2)};
+        const uint8_t* const sr[4] = {ssm + (size_t)ra * (K / 32), ssm + (size_t)rb * (K / 32),
+                                      ssm + (size_t)(DEC_TR + ra) * (K / 32), ssm + (size_t)(DEC_TR + rb) * (K / 32)};
+        float o[4][M];
+        dec_dot<4, M>(wr, sr, K, xs4, lane, o);
+        if (lane == 0)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = h ? rb : ra;
+                if (r >= n) continue;
 #pragma unroll
                 for (int m = 0; m < M; ++m)  // lib.rs:459-463
                     if (m < rows)
                         a.y[(size_t)m * a.ldy + r0 + r] =
-                            __fmul_rn(__fdiv_rn(o[m], __fadd_rn(1.0f, expf(-o[m]))), u[m]);
-        } else if (lane == 0) {
+                            __fmul_rn(__fdiv_rn(o[h][m], __fadd_rn(1.0f, expf(-o[h][m]))), o[2 + h][m]);
+            }
+    } else {
+        const uint8_t* const wr[2] = {wsm + (size_t)ra * (K / 2), wsm + (size_t)rb * (K / 2)};
+        const uint8_t* const sr[2] = {ssm + (size_t)ra * (K / 32), ssm + (size_t)rb * (K / 32)};
+        float o[2][M];
+        dec_dot<2, M>(wr, sr, K, xs4, lane, o);
+        if (lane == 0)
 #pragma unroll
-            for (int m = 0; m < M; ++m)
-                if (m < rows) {
-                    float* d = a.y + (size_t)m * a.ldy + r0 + r;
-                    *d = EPI == DEC_ADD ? __fadd_rn(*d, o[m]) : o[m];  // residual (model.rs:178-186)
-                }
-        }
+            for (int h = 0; h < 2; ++h) {
+                const int r = h ? rb : ra;
+                if (r >= n) continue;
+#pragma unroll
+                for (int m = 0; m < M; ++m)
+                    if (m < rows) {
+                        float* d = a.y + (size_t)m * a.ldy + r0 + r;
+                        *d = EPI == DEC_ADD ? __fadd_rn(*d, o[h][m]) : o[h][m];  // residual (model.rs:178-186)
+                    }
+            }
     }
 }
 

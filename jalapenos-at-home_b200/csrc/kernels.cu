@@ -575,17 +575,34 @@ struct AttnRaw {
     int k_off, v_off;     // columns of k and v in a q|k|v row
 };
 
+// What the QK-RMSNorm and RoPE of one head need besides the head itself:
+// lane l's norm weights for dims (l, l+32, l+64, l+96) and rotation factors
+// for dims l and l+32 at position pos.  None of it depends on the previous
+// kernel, so it is fetched before the dependency wait.
+struct NormRope {
+    float w[4];
+    float2 c0, c1;
+};
+__device__ __forceinline__ NormRope norm_rope_args(const uint16_t* gw, const float2* rope, int pos, int lane) {
+    NormRope r;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r.w[i] = bf16f(gw[lane + 32 * i]);
+    r.c0 = rope[(size_t)pos * HALF + lane];
+    r.c1 = rope[(size_t)pos * HALF + lane + 32];
+    return r;
+}
+
 // QK-RMSNorm and RoPE of one head held as dims (l, l+32, l+64, l+96) by lane
 // l (lib.rs:306-313, 372-388; the arithmetic of k_qk_rope_kv).
-__device__ __forceinline__ void norm_rope4(float& a0, float& a1, float& a2, float& a3, const uint16_t* gw,
-                                           float2 c0, float2 c1, int lane) {
+__device__ __forceinline__ void norm_rope4(float& a0, float& a1, float& a2, float& a3, const NormRope& nr) {
     float ss = fmaf(a0, a0, fmaf(a1, a1, fmaf(a2, a2, a3 * a3)));
     ss = warp_sum(ss);
     const float size = sqrtf(__fadd_rn(__fdiv_rn(ss, 128.0f), 1e-6f));
-    a0 = __fmul_rn(__fdiv_rn(a0, size), bf16f(gw[lane]));
-    a1 = __fmul_rn(__fdiv_rn(a1, size), bf16f(gw[lane + 32]));
-    a2 = __fmul_rn(__fdiv_rn(a2, size), bf16f(gw[lane + 64]));
-    a3 = __fmul_rn(__fdiv_rn(a3, size), bf16f(gw[lane + 96]));
+    const float2 c0 = nr.c0, c1 = nr.c1;
+    a0 = __fmul_rn(__fdiv_rn(a0, size), nr.w[0]);
+    a1 = __fmul_rn(__fdiv_rn(a1, size), nr.w[1]);
+    a2 = __fmul_rn(__fdiv_rn(a2, size), nr.w[2]);
+    a3 = __fmul_rn(__fdiv_rn(a3, size), nr.w[3]);
     const float b0 = __fsub_rn(__fmul_rn(a0, c0.x), __fmul_rn(a2, c0.y));
     const float b2 = __fadd_rn(__fmul_rn(a2, c0.x), __fmul_rn(a0, c0.y));
     const float b1 = __fsub_rn(__fmul_rn(a1, c1.x), __fmul_rn(a3, c1.y));
@@ -660,6 +677,21 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
         }
     };
     if (valid && threadIdx.x == 0) issue_window(0);
+    // RAW: the norm weights, rotation factors, this pass's row descriptors
+    // and the row's cache page, all fixed before the pass began
+    NormRope qnr = {}, knr = {};
+    RowDesc rj = {};
+    bool kgood = false;
+    int kpage = -1;
+    if (RAW && valid) {
+        if (sub == 0) qnr = norm_rope_args(raw.qn, raw.rope, rd.pos, lane);
+        if (warp <= row && warp < 2) {
+            rj = pb.row[warp];
+            kgood = rj.pos >= 0 && rj.pos < kv.max_pos && rj.seq == rd.seq;
+            knr = norm_rope_args(raw.kn, raw.rope, kgood ? rj.pos : 0, lane);
+            if (warp == row && kgood) kpage = pt[rj.pos / PAGE];
+        }
+    }
     __syncthreads();  // the barrier is initialised before anyone waits on it
     ptx::grid_dependency_wait();
     ptx::launch_dependents();
@@ -675,26 +707,22 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
         if (sub == 0) {
             const float* qr = qkv + (size_t)row * ld + h * HEAD;
             float a0 = qr[lane], a1 = qr[lane + 32], a2 = qr[lane + 64], a3 = qr[lane + 96];
-            norm_rope4(a0, a1, a2, a3, raw.qn, raw.rope[(size_t)rd.pos * HALF + lane],
-                       raw.rope[(size_t)rd.pos * HALF + lane + 32], lane);
+            norm_rope4(a0, a1, a2, a3, qnr);
             qw[lane] = a0; qw[lane + 32] = a1; qw[lane + 64] = a2; qw[lane + 96] = a3;
         }
         if (warp <= row && warp < 2) {  // row j = warp of this pass (same sequence)
             const int j = warp;
-            const RowDesc rj = pb.row[j];
-            const bool good = rj.pos >= 0 && rj.pos < kv.max_pos && rj.seq == rd.seq;
+            const bool good = kgood;
             const float* kr = qkv + (size_t)j * ld + raw.k_off + kvh * HEAD;
             const float* vr = qkv + (size_t)j * ld + raw.v_off + kvh * HEAD;
             float k0 = kr[lane], k1 = kr[lane + 32], k2 = kr[lane + 64], k3 = kr[lane + 96];
-            const int pj = good ? rj.pos : 0;
-            norm_rope4(k0, k1, k2, k3, raw.kn, raw.rope[(size_t)pj * HALF + lane],
-                       raw.rope[(size_t)pj * HALF + lane + 32], lane);
             const float v0 = vr[lane], v1 = vr[lane + 32], v2 = vr[lane + 64], v3 = vr[lane + 96];
+            norm_rope4(k0, k1, k2, k3, knr);
             nk[j][lane] = k0; nk[j][lane + 32] = k1; nk[j][lane + 64] = k2; nk[j][lane + 96] = k3;
             nv[j][lane] = v0; nv[j][lane + 32] = v1; nv[j][lane + 64] = v2; nv[j][lane + 96] = v3;
             if (lane == 0) npos[j] = good ? rj.pos : -1;
             if (j == row && good) {  // the row's own K/V go to the cache
-                const int pg = pt[rj.pos / PAGE];
+                const int pg = kpage;
                 if (page_ok(kv, pg)) {
                     const size_t idx = kv_index(pg, kvh, rj.pos % PAGE, kv.kv_heads);
                     if (F32) {
