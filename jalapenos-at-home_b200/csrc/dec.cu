@@ -173,11 +173,14 @@ __device__ __forceinline__ void dec_dot(const uint8_t* const (&wr)[R], const uin
 }
 
 // ---------------------------------------------------------------------------
-// CTA = DEC_TR output rows, 8 warps.  Output rows are numbered across up to
-// three stacked matrices (q | k | v; a tile never straddles two); SwiGLU
-// tiles take DEC_TR gate rows and the matching up rows.
+// CTA = TR output rows (8 or 16), 8 warps of TR / 8 rows each.  Output rows
+// are numbered across up to three stacked matrices (q | k | v; a tile never
+// straddles two); SwiGLU tiles take TR gate rows and the matching up rows.
+// The dot products are latency, not work: o, gate/up and down take one row
+// per warp; q|k|v (the widest output, 4096 rows on the 0.6B) takes two, as
+// 512 CTAs all loading x cost more than a second interleaved row.
 
-constexpr int DEC_TR = 16;
+constexpr int DEC_TR = 16;  // the largest tile
 enum : int { DEC_STORE = 0, DEC_ADD = 1, DEC_SWIGLU = 2 };
 
 struct DecArgs {
@@ -193,30 +196,30 @@ struct DecArgs {
     int* err;
 };
 
-template <int M, int EPI>
+template <int M, int EPI, int TR>
 __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
     extern __shared__ __align__(128) uint8_t dsm[];
     __shared__ uint64_t bar;
     __shared__ float red[32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = a.K;
-    const int r0 = blockIdx.x * DEC_TR;
-    const int n = min(DEC_TR, a.out_rows - r0);
+    const int r0 = blockIdx.x * TR;
+    const int n = min(TR, a.out_rows - r0);
     constexpr int NM = EPI == DEC_SWIGLU ? 2 : 1;
     // the matrix this tile's rows come from, and the first local row
     int mat = 0, lr0 = r0;
     if (EPI != DEC_SWIGLU)
         while (mat < 2 && lr0 >= a.rows[mat]) lr0 -= a.rows[mat++];
-    uint8_t* wsm = dsm;                                   // [NM][DEC_TR][K/2]
-    uint8_t* ssm = dsm + NM * DEC_TR * (K / 2);           // [NM][DEC_TR][K/32]
-    float4* xs4 = reinterpret_cast<float4*>(ssm + NM * DEC_TR * (K / 32));
+    uint8_t* wsm = dsm;                                   // [NM][TR][K/2]
+    uint8_t* ssm = dsm + NM * TR * (K / 2);           // [NM][TR][K/32]
+    float4* xs4 = reinterpret_cast<float4*>(ssm + NM * TR * (K / 32));
     if (threadIdx.x == 0) {
         ptx::mbar_init(&bar, 1);
         ptx::fence_barrier_init();
         ptx::mbar_arrive_expect_tx(&bar, (uint32_t)(NM * n * (K / 2 + K / 32)));
         dec_copy_rows(a.w[mat], lr0, n, K, wsm, ssm, &bar);
         if (EPI == DEC_SWIGLU)
-            dec_copy_rows(a.w[1], r0, n, K, wsm + DEC_TR * (K / 2), ssm + DEC_TR * (K / 32), &bar);
+            dec_copy_rows(a.w[1], r0, n, K, wsm + TR * (K / 2), ssm + TR * (K / 32), &bar);
     }
     uint2 wv[DEC_XCHUNKS];
     dec_norm_weights(a.norm, K, wv);
@@ -231,37 +234,49 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
         if (threadIdx.x == 0) atomicOr(a.err, 4);
         return;
     }
-    // warp w owns tile rows w and w + 8 (rows past n are computed from
-    // unloaded shared memory and dropped)
-    static_assert(DEC_TR == 16, "two rows per warp of an 8-warp CTA");
-    const int ra = warp, rb = warp + 8;
+    // warp w owns tile rows w, w + 8, ... (RPW of them; rows past n are
+    // computed from unloaded shared memory and dropped)
+    constexpr int RPW = TR / 8;
+    static_assert(TR % 8 == 0 && RPW <= 2, "one or two rows per warp of an 8-warp CTA");
+    if (warp >= n) return;
     if (EPI == DEC_SWIGLU) {
-        const uint8_t* const wr[4] = {wsm + (size_t)ra * (K / 2), wsm + (size_t)rb * (K / 2),
-                                      wsm + (size_t)(DEC_TR + ra) * (K / 2), wsm + (size_t)(DEC_TR + rb) * (K / 2)};
-        const uint8_t* const sr[4] = {ssm + (size_t)ra * (K / 32), ssm + (size_t)rb * (K / 32),
-                                      ssm + (size_t)(DEC_TR + ra) * (K / 32), ssm + (size_t)(DEC_TR + rb) * (K / 32)};
-        float o[4][M];
-        dec_dot<4, M>(wr, sr, K, xs4, lane, o);
+        const uint8_t* wr[2 * RPW];
+        const uint8_t* sr[2 * RPW];
+#pragma unroll
+        for (int h = 0; h < RPW; ++h) {
+            const int r = warp + 8 * h;
+            wr[h] = wsm + (size_t)r * (K / 2);
+            sr[h] = ssm + (size_t)r * (K / 32);
+            wr[RPW + h] = wsm + (size_t)(TR + r) * (K / 2);
+            sr[RPW + h] = ssm + (size_t)(TR + r) * (K / 32);
+        }
+        float o[2 * RPW][M];
+        dec_dot<2 * RPW, M>(wr, sr, K, xs4, lane, o);
         if (lane == 0)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int r = h ? rb : ra;
+            for (int h = 0; h < RPW; ++h) {
+                const int r = warp + 8 * h;
                 if (r >= n) continue;
 #pragma unroll
                 for (int m = 0; m < M; ++m)  // lib.rs:459-463
                     if (m < rows)
                         a.y[(size_t)m * a.ldy + r0 + r] =
-                            __fmul_rn(__fdiv_rn(o[h][m], __fadd_rn(1.0f, expf(-o[h][m]))), o[2 + h][m]);
+                            __fmul_rn(__fdiv_rn(o[h][m], __fadd_rn(1.0f, expf(-o[h][m]))), o[RPW + h][m]);
             }
     } else {
-        const uint8_t* const wr[2] = {wsm + (size_t)ra * (K / 2), wsm + (size_t)rb * (K / 2)};
-        const uint8_t* const sr[2] = {ssm + (size_t)ra * (K / 32), ssm + (size_t)rb * (K / 32)};
-        float o[2][M];
-        dec_dot<2, M>(wr, sr, K, xs4, lane, o);
+        const uint8_t* wr[RPW];
+        const uint8_t* sr[RPW];
+#pragma unroll
+        for (int h = 0; h < RPW; ++h) {
+            wr[h] = wsm + (size_t)(warp + 8 * h) * (K / 2);
+            sr[h] = ssm + (size_t)(warp + 8 * h) * (K / 32);
+        }
+        float o[RPW][M];
+        dec_dot<RPW, M>(wr, sr, K, xs4, lane, o);
         if (lane == 0)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int r = h ? rb : ra;
+            for (int h = 0; h < RPW; ++h) {
+                const int r = warp + 8 * h;
                 if (r >= n) continue;
 #pragma unroll
                 for (int m = 0; m < M; ++m)
@@ -275,13 +290,14 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
 
 template <int M, int EPI>
 jl_status configure_dec_proj(int smem) {
-    JL_CUDA(cudaFuncSetAttribute(k_dec_proj<M, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    constexpr int TR = EPI == DEC_STORE ? 16 : 8;
+    JL_CUDA(cudaFuncSetAttribute(k_dec_proj<M, EPI, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     return JL_OK;
 }
 
-size_t dec_proj_smem(int K, bool swiglu) {
+size_t dec_proj_smem(int K, bool swiglu, int tr = DEC_TR) {
     const int nm = swiglu ? 2 : 1;
-    return (size_t)nm * DEC_TR * (K / 2 + K / 32) + (size_t)DEC_MAXROWS * K * 4;
+    return (size_t)nm * tr * (K / 2 + K / 32) + (size_t)DEC_MAXROWS * K * 4;
 }
 
 DecTile tile_of(const Mat& w) { return DecTile{(const uint8_t*)w.data, w.scales}; }
@@ -346,16 +362,17 @@ jl_status record_dec_pass(const PassCtx& c, int layers) {
             d.hdr = m->pass.hdr;
             d.mcap = M;
             d.err = m->counters;
-            const dim3 g((out_rows + DEC_TR - 1) / DEC_TR);
-            const size_t sm = dec_proj_smem(K, epi == DEC_SWIGLU);
+            const int tr = epi == DEC_STORE ? 16 : 8;
+            const dim3 g((out_rows + tr - 1) / tr);
+            const size_t sm = dec_proj_smem(K, epi == DEC_SWIGLU, tr);
             const dim3 b(256);
             switch (epi * 2 + (M - 1)) {
-                case DEC_STORE * 2: return launch_pdl(k_dec_proj<1, DEC_STORE>, g, b, sm, c.stream, d);
-                case DEC_STORE * 2 + 1: return launch_pdl(k_dec_proj<2, DEC_STORE>, g, b, sm, c.stream, d);
-                case DEC_ADD * 2: return launch_pdl(k_dec_proj<1, DEC_ADD>, g, b, sm, c.stream, d);
-                case DEC_ADD * 2 + 1: return launch_pdl(k_dec_proj<2, DEC_ADD>, g, b, sm, c.stream, d);
-                case DEC_SWIGLU * 2: return launch_pdl(k_dec_proj<1, DEC_SWIGLU>, g, b, sm, c.stream, d);
-                default: return launch_pdl(k_dec_proj<2, DEC_SWIGLU>, g, b, sm, c.stream, d);
+                case DEC_STORE * 2: return launch_pdl(k_dec_proj<1, DEC_STORE, 16>, g, b, sm, c.stream, d);
+                case DEC_STORE * 2 + 1: return launch_pdl(k_dec_proj<2, DEC_STORE, 16>, g, b, sm, c.stream, d);
+                case DEC_ADD * 2: return launch_pdl(k_dec_proj<1, DEC_ADD, 8>, g, b, sm, c.stream, d);
+                case DEC_ADD * 2 + 1: return launch_pdl(k_dec_proj<2, DEC_ADD, 8>, g, b, sm, c.stream, d);
+                case DEC_SWIGLU * 2: return launch_pdl(k_dec_proj<1, DEC_SWIGLU, 8>, g, b, sm, c.stream, d);
+                default: return launch_pdl(k_dec_proj<2, DEC_SWIGLU, 8>, g, b, sm, c.stream, d);
             }
         };
         // lib.rs:353-355: raw q | k | v, normalised and rotated by the attention kernel
