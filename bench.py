@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--profile", action="store_true",
                     help="small run for ncu: one k+1-row target pass and one draft pass "
                          "(Model::time_pass), no timing loop")
+    ap.add_argument("--small", action="store_true",
+                    help="with --profile: two layers of each model at full width and an 8192-entry "
+                         "vocabulary (under 0.5 GB on the device), for multi-pass ncu captures")
     return ap.parse_args()
 
 
@@ -70,8 +73,18 @@ def run_profile(args, dist):
     import jalapeno as J
     import oracle as O
 
-    target, draft = make_models(J, dist.local)
-    prompt = O.prompt_ids(args.prompt, 151936, 2)
+    if args.small:
+        opts = dict(kv_pool_tokens=1024, max_pass_rows=64, device=dist.local)
+        small = dict(layers=2, vocab=8192)
+        target = J.Model.synthesize(**{**PRESETS["qwen3-8b"], **small}, seed=0, mxfp4=True,
+                                    name="Qwen3-8B-MXFP4 (2 layers)", **opts)
+        draft = J.Model.synthesize(**{**PRESETS["qwen3-0.6b"], **small}, seed=1, mxfp4=True,
+                                   name="Qwen3-0.6B-MXFP4 (2 layers)", **opts)
+        vocab = 8192
+    else:
+        target, draft = make_models(J, dist.local)
+        vocab = 151936
+    prompt = O.prompt_ids(args.prompt, vocab, 2)
     tw, tg = target.time_pass(prompt, args.gamma + 1, reps=1)
     dw, dg = draft.time_pass_draft(prompt, reps=1)
     print(json.dumps({"profile": True, "target_pass_ms": tg, "draft_pass_ms": dg,
