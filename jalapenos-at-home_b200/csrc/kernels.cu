@@ -692,6 +692,13 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
             if (warp == row && kgood) kpage = pt[rj.pos / PAGE];
         }
     }
+    // Not RAW: the page of the position this warp re-fetches after the wait
+    // (position pos - row + warp: this pass's rows of the sequence)
+    int own_p = -1, own_pg = -1;
+    if (!RAW && valid && warp <= row && rd.pos - row + warp >= 0) {
+        own_p = rd.pos - row + warp;
+        own_pg = pt[own_p / PAGE];
+    }
     __syncthreads();  // the barrier is initialised before anyone waits on it
     ptx::grid_dependency_wait();
     ptx::launch_dependents();
@@ -778,7 +785,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
             constexpr int RB = HEAD * (F32 ? 4 : 2);  // bytes of one row: 256 or 512
             const int lo = max(rd.pos - row, w0 * PAGE), hi = min(rd.pos, (w0 + wn) * PAGE - 1);
             for (int p = lo + warp; p <= hi; p += nw) {
-                const int pg = pt[p / PAGE];
+                const int pg = p == own_p ? own_pg : pt[p / PAGE];
                 if ((unsigned)pg >= (unsigned)kv.pages) continue;  // flagged when the window was copied
                 const int i = p / PAGE - w0;
                 const size_t src = kv_index(pg, kvh, p % PAGE, kv.kv_heads) * (F32 ? 4 : 2);
