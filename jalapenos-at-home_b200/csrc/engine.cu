@@ -20,6 +20,24 @@
 
 namespace jl {
 
+jl_status stage_begin(jl_model* m, StageSlot** out) {
+    StageSlot& sl = m->stage[m->stage_next];
+    m->stage_next = (m->stage_next + 1) % STAGE_SLOTS;
+    if (sl.pending) {
+        JL_CUDA(cudaEventSynchronize(sl.done));
+        sl.pending = false;
+    }
+    *out = &sl;
+    return JL_OK;
+}
+
+jl_status stage_end(jl_model* m, StageSlot* s, cudaStream_t st) {
+    (void)m;
+    JL_CUDA(cudaEventRecord(s->done, st));
+    s->pending = true;
+    return JL_OK;
+}
+
 namespace {
 
 constexpr int HEAD_CAP = 512;  // predicted rows per pass (longer all=true calls are chunked)
@@ -271,26 +289,29 @@ jl_status check_ids(const jl_model* m, const uint32_t* ids, size_t n) {
 // Stages one pass's rows from the host and runs it on m->stream.
 jl_status host_pass(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int head_rows,
                     bool all, int layers, bool draft_step = false) {
-    PassHdr* h = m->host_hdr;
+    StageSlot* sl = nullptr;
+    JL_TRY(stage_begin(m, &sl));
+    PassHdr* h = sl->hdr;
     h->rows = (int32_t)n;
     h->head_rows = head_rows;
     h->pad0 = h->pad1 = 0;
     for (size_t i = 0; i < n; ++i) {
-        m->host_row[i].token = ids[i];
-        m->host_row[i].seq = 0;
-        m->host_row[i].pos = (int32_t)(c->len + i);
-        m->host_row[i].pad = 0;
+        sl->row[i].token = ids[i];
+        sl->row[i].seq = 0;
+        sl->row[i].pos = (int32_t)(c->len + i);
+        sl->row[i].pad = 0;
     }
-    for (int j = 0; j < head_rows; ++j) m->host_head_row[j] = all ? j : (int32_t)n - 1;
-    m->host_page_table[0] = c->d_pages;
+    for (int j = 0; j < head_rows; ++j) sl->head_row[j] = all ? j : (int32_t)n - 1;
+    sl->page_table[0] = c->d_pages;
     cudaStream_t st = m->stream;
     JL_CUDA(cudaMemcpyAsync(m->pass.hdr, h, sizeof(PassHdr), cudaMemcpyHostToDevice, st));
-    JL_CUDA(cudaMemcpyAsync(m->pass.row, m->host_row, n * sizeof(RowDesc), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(m->pass.row, sl->row, n * sizeof(RowDesc), cudaMemcpyHostToDevice, st));
     if (head_rows)
-        JL_CUDA(cudaMemcpyAsync(m->pass.head_row, m->host_head_row, head_rows * sizeof(int32_t),
+        JL_CUDA(cudaMemcpyAsync(m->pass.head_row, sl->head_row, head_rows * sizeof(int32_t),
                                 cudaMemcpyHostToDevice, st));
-    JL_CUDA(cudaMemcpyAsync(m->pass.page_table, m->host_page_table, sizeof(int32_t*),
+    JL_CUDA(cudaMemcpyAsync(m->pass.page_table, sl->page_table, sizeof(int32_t*),
                             cudaMemcpyHostToDevice, st));
+    JL_TRY(stage_end(m, sl, st));
     const bool full = layers == m->layers && head_rows > 0;
     if (full && draft_step && m->dec_ok && n <= 2) {
         // a speculative loop's draft step, captured on its own
@@ -516,8 +537,11 @@ jl_status project(jl_model* m, int layer, int which, const float* x, size_t rows
         default: in = m->s.xh; out = m->s.logits; wout = m->vocab; break;
     }
     PassHdr h{(int32_t)rows, (int32_t)rows, 0, 0};
-    *m->host_hdr = h;
-    JL_CUDA(cudaMemcpyAsync(m->pass.hdr, m->host_hdr, sizeof(PassHdr), cudaMemcpyHostToDevice, st));
+    StageSlot* sl = nullptr;
+    JL_TRY(stage_begin(m, &sl));
+    *sl->hdr = h;
+    JL_CUDA(cudaMemcpyAsync(m->pass.hdr, sl->hdr, sizeof(PassHdr), cudaMemcpyHostToDevice, st));
+    JL_TRY(stage_end(m, sl, st));
     JL_CUDA(cudaMemcpyAsync(in, x, rows * win * sizeof(float), cudaMemcpyHostToDevice, st));
     if (which == 1 || which == 3)  // these add into the residual stream: start it at zero
         JL_CUDA(cudaMemsetAsync(out, 0, rows * wout * sizeof(float), st));
@@ -544,8 +568,11 @@ jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters
     JL_CUDA(cudaSetDevice(m->device));
     const LayerW& L = m->lw[layer];
     PassHdr h{rows, which == 4 ? rows : 0, 0, 0};
-    *m->host_hdr = h;
-    JL_CUDA(cudaMemcpyAsync(m->pass.hdr, m->host_hdr, sizeof(PassHdr), cudaMemcpyHostToDevice, m->stream));
+    StageSlot* sl = nullptr;
+    JL_TRY(stage_begin(m, &sl));
+    *sl->hdr = h;
+    JL_CUDA(cudaMemcpyAsync(m->pass.hdr, sl->hdr, sizeof(PassHdr), cudaMemcpyHostToDevice, m->stream));
+    JL_TRY(stage_end(m, sl, m->stream));
     PassCtx c{m, m->stream, rows, rows};
     const bool fused = m->mx.fused && rows <= mx_max_tokens();
     const int hid = m->hidden, tiles = hid / 128;
@@ -871,17 +898,21 @@ jl_status generate(jl_model* m, const uint32_t* prompt, size_t n, size_t count, 
     cudaStream_t st = m->stream;
     JL_CUDA(cudaMemcpyAsync(g->st, s, sizeof(SpecState), cudaMemcpyHostToDevice, st));
     JL_CUDA(cudaMemcpyAsync(g->tokens, out, (n + 1) * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
-    PassHdr* h = m->host_hdr;
+    StageSlot* sl = nullptr;
+    JL_TRY(stage_begin(m, &sl));
+    PassHdr* h = sl->hdr;
     h->rows = 1;
     h->head_rows = 1;
-    m->host_row[0] = RowDesc{next, 0, (int32_t)c->len, 0};
-    m->host_head_row[0] = 0;
-    m->host_page_table[0] = c->d_pages;
+    h->pad0 = h->pad1 = 0;
+    sl->row[0] = RowDesc{next, 0, (int32_t)c->len, 0};
+    sl->head_row[0] = 0;
+    sl->page_table[0] = c->d_pages;
     JL_CUDA(cudaMemcpyAsync(m->pass.hdr, h, sizeof(PassHdr), cudaMemcpyHostToDevice, st));
-    JL_CUDA(cudaMemcpyAsync(m->pass.row, m->host_row, sizeof(RowDesc), cudaMemcpyHostToDevice, st));
-    JL_CUDA(cudaMemcpyAsync(m->pass.head_row, m->host_head_row, sizeof(int32_t), cudaMemcpyHostToDevice, st));
-    JL_CUDA(cudaMemcpyAsync(m->pass.page_table, m->host_page_table, sizeof(int32_t*),
+    JL_CUDA(cudaMemcpyAsync(m->pass.row, sl->row, sizeof(RowDesc), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(m->pass.head_row, sl->head_row, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(m->pass.page_table, sl->page_table, sizeof(int32_t*),
                             cudaMemcpyHostToDevice, st));
+    JL_TRY(stage_end(m, sl, st));
     JL_CUDA(cudaGraphLaunch(g->exec, st));
     JL_CUDA(cudaMemcpyAsync(s, g->st, sizeof(SpecState), cudaMemcpyDeviceToHost, st));
     JL_CUDA(cudaStreamSynchronize(st));
@@ -1102,12 +1133,17 @@ jl_status generate_speculative(jl_model* T, jl_model* D, const uint32_t* prompt,
     JL_CUDA(cudaMemcpyAsync(g->st, s, sizeof(SpecState), cudaMemcpyHostToDevice, st));
     JL_CUDA(cudaMemcpyAsync(g->tokens, prompt, n * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
     // both models read sequence 0 from their own cache's page table
-    T->host_page_table[0] = tc->d_pages;
-    D->host_page_table[0] = dc->d_pages;
-    JL_CUDA(cudaMemcpyAsync(T->pass.page_table, T->host_page_table, sizeof(int32_t*),
+    StageSlot *ts = nullptr, *ds = nullptr;
+    JL_TRY(stage_begin(T, &ts));
+    JL_TRY(stage_begin(D, &ds));
+    ts->page_table[0] = tc->d_pages;
+    ds->page_table[0] = dc->d_pages;
+    JL_CUDA(cudaMemcpyAsync(T->pass.page_table, ts->page_table, sizeof(int32_t*),
                             cudaMemcpyHostToDevice, st));
-    JL_CUDA(cudaMemcpyAsync(D->pass.page_table, D->host_page_table, sizeof(int32_t*),
+    JL_CUDA(cudaMemcpyAsync(D->pass.page_table, ds->page_table, sizeof(int32_t*),
                             cudaMemcpyHostToDevice, st));
+    JL_TRY(stage_end(T, ts, st));
+    JL_TRY(stage_end(D, ds, st));
     // the draft's stream must not still be using its pass buffers
     JL_CUDA(cudaStreamSynchronize(D->stream));
     JL_CUDA(cudaEventRecord(T->ev0, st));

@@ -161,6 +161,17 @@ struct PassBuf {
     uint32_t* out_ids = nullptr;       // [max_rows]
 };
 
+// One slot of a model's pinned descriptor staging ring.
+constexpr int STAGE_SLOTS = 4;
+struct StageSlot {
+    PassHdr* hdr = nullptr;
+    RowDesc* row = nullptr;                // [max_rows]
+    int32_t* head_row = nullptr;           // [max_rows]
+    const int32_t** page_table = nullptr;  // [MAX_SEQS]
+    cudaEvent_t done = nullptr;            // recorded after the copies that read the slot
+    bool pending = false;
+};
+
 struct Scratch {
     float* x = nullptr;       // [rows, hidden] residual stream
     float* xn = nullptr;      // [rows, max(hidden, q_width)] normalised input
@@ -203,10 +214,12 @@ struct jl_model {
     jl::KvPool kv;
     int max_rows = 0;
     jl::PassBuf pass;                     // device
-    jl::PassHdr* host_hdr = nullptr;      // pinned staging for jl_predict
-    jl::RowDesc* host_row = nullptr;
-    int32_t* host_head_row = nullptr;
-    const int32_t** host_page_table = nullptr;
+    // Pinned staging of pass descriptors: a ring of slots (jl::stage_begin /
+    // jl::stage_end).  An upload's copies run only when the stream reaches
+    // them, after the work queued before; a slot is written again only once
+    // they have run, so a pass never reads a later pass's descriptors.
+    jl::StageSlot stage[jl::STAGE_SLOTS];
+    int stage_next = 0;
     uint32_t* host_out = nullptr;
     float* host_logits = nullptr;
     jl::Scratch s;
@@ -220,6 +233,13 @@ struct jl_model {
     int* counters = nullptr;              // zeroed split-K / reduction counters
     std::map<std::string, std::pair<const void*, size_t>> tensor_index;  // name -> device bytes
 };
+namespace jl {
+// The next slot of m's staging ring, once the copies that last read it have
+// run; stage_end records that the copies just queued on `st` read it.
+jl_status stage_begin(jl_model* m, StageSlot** out);
+jl_status stage_end(jl_model* m, StageSlot* s, cudaStream_t st);
+}  // namespace jl
+
 
 struct jl_cache {
     jl_model* m = nullptr;

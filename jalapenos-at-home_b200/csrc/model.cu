@@ -134,10 +134,13 @@ jl_status finish_model(jl_model* m, const jl_model_options& o) {
     m->pass.out_ids = (uint32_t*)(b + off_out);
     m->counters = (int*)(b + off_cnt);
     // pinned staging for host-driven passes
-    JL_CUDA(cudaMallocHost(&m->host_hdr, sizeof(PassHdr)));
-    JL_CUDA(cudaMallocHost(&m->host_row, (size_t)R * sizeof(RowDesc)));
-    JL_CUDA(cudaMallocHost(&m->host_head_row, (size_t)R * sizeof(int32_t)));
-    JL_CUDA(cudaMallocHost(&m->host_page_table, (size_t)MAX_SEQS * sizeof(int32_t*)));
+    for (StageSlot& sl : m->stage) {
+        JL_CUDA(cudaMallocHost(&sl.hdr, sizeof(PassHdr)));
+        JL_CUDA(cudaMallocHost(&sl.row, (size_t)R * sizeof(RowDesc)));
+        JL_CUDA(cudaMallocHost(&sl.head_row, (size_t)R * sizeof(int32_t)));
+        JL_CUDA(cudaMallocHost(&sl.page_table, (size_t)MAX_SEQS * sizeof(int32_t*)));
+        JL_CUDA(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+    }
     JL_CUDA(cudaMallocHost(&m->host_out, (size_t)R * sizeof(uint32_t)));
     return JL_OK;
 }
@@ -564,10 +567,13 @@ void model_free(jl_model* m) {
     cudaFree(m->scratch_arena);
     cudaFree(m->mx.arena);
     cudaFree(m->mx.scratch);
-    cudaFreeHost(m->host_hdr);
-    cudaFreeHost(m->host_row);
-    cudaFreeHost(m->host_head_row);
-    cudaFreeHost(m->host_page_table);
+    for (StageSlot& sl : m->stage) {
+        if (sl.done) cudaEventDestroy(sl.done);
+        cudaFreeHost(sl.hdr);
+        cudaFreeHost(sl.row);
+        cudaFreeHost(sl.head_row);
+        cudaFreeHost((void*)sl.page_table);
+    }
     cudaFreeHost(m->host_out);
     cudaFreeHost(m->host_logits);
     if (m->ev0) cudaEventDestroy(m->ev0);

@@ -102,6 +102,21 @@ def test_logits_match_oracle(oracles, key, kv):
     assert ids == bids
 
 
+@pytest.mark.parametrize("n", [66, 96, 200])
+@pytest.mark.parametrize("key", [("tiny", False), ("tiny", True)])
+def test_multi_chunk_prefill_matches_oracle(oracles, key, n):
+    """One predict call over several passes (16-row chunks), spanning KV pages:
+    each pass's row descriptors reach the GPU intact although the host queues
+    the next pass's before the earlier ones have run."""
+    ref = oracles[key]
+    m = gpu_model(TINY, 0, key[1], kv_dtype=J.KV_F32)
+    prompt = O.prompt_ids(n, 1000, 3)
+    for _ in range(3):  # the host runs ahead of the device differently each time
+        ids, lg = m.predict(prompt, m.cache(), all=False, logits=True)
+        rids, rlg = ref.predict(prompt, ref.cache(), all=False, logits=True)
+        assert rel_l2(lg, rlg) < 1e-5 and ids == rids
+
+
 def test_decode_after_prefill_matches_oracle(oracles):
     ref = oracles[("tiny", True)]
     m = gpu_model(TINY, 0, True, kv_dtype=J.KV_F32)
