@@ -100,12 +100,15 @@ def measured_peaks():
 
 
 class Dist:
-    """Rank bookkeeping; torch.distributed only when launched by torchrun."""
+    """Rank bookkeeping; torch.distributed only when launched by torchrun.
+    The process group is NCCL over the GPUs, or gloo on host cores when
+    JL_DIST_BACKEND=gloo (the multi-process tests, which have no GPU)."""
 
     def __init__(self):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.backend = os.environ.get("JL_DIST_BACKEND", "nccl")
         self.pg = None
         if self.world > 1:
             import datetime
@@ -113,18 +116,25 @@ class Dist:
             import torch
             import torch.distributed as dist
 
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                    device_id=torch.device("cuda", self.local))
+            timeout = datetime.timedelta(seconds=300)
+            if self.backend == "nccl":
+                torch.cuda.set_device(self.local)
+                dist.init_process_group("nccl", timeout=timeout, device_id=torch.device("cuda", self.local))
+            else:
+                dist.init_process_group(self.backend, timeout=timeout)
             self.pg = dist
 
-    def barrier(self):
-        import torch
+    def _sync(self):
+        if self.backend == "nccl":
+            import torch
 
-        torch.cuda.synchronize(self.local)
+            torch.cuda.synchronize(self.local)
+
+    def barrier(self):
+        self._sync()
         if self.pg:
             self.pg.barrier()
-        torch.cuda.synchronize(self.local)
+        self._sync()
 
     def max(self, v: float) -> float:
         return self._reduce(v, "max")
@@ -137,7 +147,8 @@ class Dist:
             return v
         import torch
 
-        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{self.local}")
+        dev = f"cuda:{self.local}" if self.backend == "nccl" else "cpu"
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX if op == "max" else self.pg.ReduceOp.SUM)
         return float(t.item())
 
@@ -280,6 +291,16 @@ def run_reference(args, dist):
     print(json.dumps(line), flush=True)
 
 
+def aggregate(dist, new_tokens: int, decode_ms: float, e2e_s: float):
+    """Whole-job throughput of the replicas: every rank's generated tokens over
+    the slowest rank's time (device decode time, and wall time of the public
+    call for e2e).  Returns (value tok/s, e2e tok/s, total tokens)."""
+    max_decode_ms = dist.max(decode_ms)
+    max_e2e_s = dist.max(e2e_s)
+    all_tokens = dist.sum(new_tokens)
+    return all_tokens / (max_decode_ms / 1000.0), all_tokens / max_e2e_s, all_tokens
+
+
 def workload_config(args):
     return {"workload": "Qwen3-8B MXFP4 target + Qwen3-0.6B MXFP4 draft, greedy speculative decode",
             "k": args.gamma, "batch_per_gpu": 1, "prompt_tokens": args.prompt,
@@ -331,11 +352,7 @@ def main():
     new_tokens = sum(len(r.tokens) - len(prompt) for r, _ in results)
     decode_ms = sum(r.decode_ms for r, _ in results)
     e2e_s = sum(w for _, w in results)
-    max_decode_ms = dist.max(decode_ms)
-    max_e2e_s = dist.max(e2e_s)
-    all_tokens = dist.sum(new_tokens)
-    value = all_tokens / (max_decode_ms / 1000.0)
-    e2e = all_tokens / max_e2e_s
+    value, e2e, all_tokens = aggregate(dist, new_tokens, decode_ms, e2e_s)
     r0 = results[0][0]
     rounds = sum(r.rounds for r, _ in results)
     verify = sum(r.verify.passes for r, _ in results)
