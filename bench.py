@@ -294,11 +294,12 @@ def run_reference(args, dist):
 def aggregate(dist, new_tokens: int, decode_ms: float, e2e_s: float):
     """Whole-job throughput of the replicas: every rank's generated tokens over
     the slowest rank's time (device decode time, and wall time of the public
-    call for e2e).  Returns (value tok/s, e2e tok/s, total tokens)."""
+    call for e2e).  Returns (value tok/s, e2e tok/s, total tokens, the slowest
+    rank's decode ms)."""
     max_decode_ms = dist.max(decode_ms)
     max_e2e_s = dist.max(e2e_s)
     all_tokens = dist.sum(new_tokens)
-    return all_tokens / (max_decode_ms / 1000.0), all_tokens / max_e2e_s, all_tokens
+    return all_tokens / (max_decode_ms / 1000.0), all_tokens / max_e2e_s, all_tokens, max_decode_ms
 
 
 def workload_config(args):
@@ -352,7 +353,7 @@ def main():
     new_tokens = sum(len(r.tokens) - len(prompt) for r, _ in results)
     decode_ms = sum(r.decode_ms for r, _ in results)
     e2e_s = sum(w for _, w in results)
-    value, e2e, all_tokens = aggregate(dist, new_tokens, decode_ms, e2e_s)
+    value, e2e, all_tokens, max_decode_ms = aggregate(dist, new_tokens, decode_ms, e2e_s)
     r0 = results[0][0]
     rounds = sum(r.rounds for r, _ in results)
     verify = sum(r.verify.passes for r, _ in results)

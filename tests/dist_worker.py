@@ -12,8 +12,8 @@ dist = bench.Dist()
 r = dist.rank
 dist.barrier()
 # rank r generated 64 + r tokens in 100 * (r + 1) ms of device time and 1 + r s of wall time
-value, e2e, tokens = bench.aggregate(dist, 64 + r, 100.0 * (r + 1), 1.0 + r)
+value, e2e, tokens, slowest_ms = bench.aggregate(dist, 64 + r, 100.0 * (r + 1), 1.0 + r)
 dist.barrier()
 out = Path(os.environ["JL_DIST_OUT"]) / f"rank{r}.json"
-out.write_text(json.dumps({"rank": r, "world": dist.world, "value": value, "e2e": e2e, "tokens": tokens}))
+out.write_text(json.dumps({"rank": r, "world": dist.world, "value": value, "e2e": e2e, "tokens": tokens, "slowest_ms": slowest_ms}))
 dist.close()

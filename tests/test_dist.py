@@ -32,3 +32,4 @@ def test_two_ranks_aggregate_over_gloo(tmp_path):
         # every rank's tokens over the slowest rank's time (200 ms device, 2 s wall)
         assert abs(x["value"] - 129 / 0.2) < 1e-9
         assert abs(x["e2e"] - 129 / 2.0) < 1e-9
+        assert x["slowest_ms"] == 200.0
