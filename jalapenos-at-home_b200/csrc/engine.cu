@@ -20,6 +20,14 @@
 
 namespace jl {
 
+int att_splits_for(const jl_model* m, size_t max_ctx) {
+    const size_t pages = (max_ctx + PAGE - 1) / PAGE;
+    const int need = (int)std::max<size_t>(1, (pages + ATT_WIN - 1) / ATT_WIN);
+    int s = 1;
+    while (s < need) s <<= 1;
+    return std::min(s, std::max(1, m->att_smax));
+}
+
 jl_status stage_begin(jl_model* m, StageSlot** out) {
     StageSlot& sl = m->stage[m->stage_next];
     m->stage_next = (m->stage_next + 1) % STAGE_SLOTS;
@@ -313,19 +321,27 @@ jl_status host_pass(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int
                             cudaMemcpyHostToDevice, st));
     JL_TRY(stage_end(m, sl, st));
     const bool full = layers == m->layers && head_rows > 0;
+    // window CTAs the attention needs for this pass's longest context; a
+    // captured pass is captured again when it was built for fewer
+    const int splits = att_splits_for(m, c->len + n);
     if (full && draft_step && m->dec_ok && n <= 2) {
         // a speculative loop's draft step, captured on its own
         cudaGraphExec_t& exec = m->draft_graph[n - 1];
+        if (exec && m->draft_graph_splits[n - 1] < splits) {
+            cudaGraphExecDestroy(exec);
+            exec = nullptr;
+        }
         if (!exec) {
             cudaGraph_t g;
             JL_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-            PassCtx ctx{m, st, (int)n, (int)n, true};
+            PassCtx ctx{m, st, (int)n, (int)n, true, splits};
             jl_status rs = record_pass_ctx(ctx, m->layers, true);
             cudaError_t ce = cudaStreamEndCapture(st, &g);
             if (rs != JL_OK) return rs;
             JL_CUDA(ce);
             JL_CUDA(cudaGraphInstantiate(&exec, g, 0));
             cudaGraphDestroy(g);
+            m->draft_graph_splits[n - 1] = splits;
         }
         JL_CUDA(cudaGraphLaunch(exec, st));
         return JL_OK;
@@ -335,20 +351,26 @@ jl_status host_pass(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int
         int b = 0;
         while ((1 << b) < (int)n) ++b;
         cudaGraphExec_t& exec = m->small_graph[b];
+        if (exec && m->small_graph_splits[b] < splits) {
+            cudaGraphExecDestroy(exec);
+            exec = nullptr;
+        }
         if (!exec) {
             cudaGraph_t g;
             JL_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-            jl_status rs = record_pass(m, st, 1 << b, m->layers, true);
+            PassCtx ctx{m, st, 1 << b, 1 << b, false, splits};
+            jl_status rs = record_pass_ctx(ctx, m->layers, true);
             cudaError_t ce = cudaStreamEndCapture(st, &g);
             if (rs != JL_OK) return rs;
             JL_CUDA(ce);
             JL_CUDA(cudaGraphInstantiate(&exec, g, 0));
             cudaGraphDestroy(g);
+            m->small_graph_splits[b] = splits;
         }
         JL_CUDA(cudaGraphLaunch(exec, st));
         return JL_OK;
     }
-    PassCtx ctx{m, st, (int)n, std::max(head_rows, 1)};
+    PassCtx ctx{m, st, (int)n, std::max(head_rows, 1), false, splits};
     return record_pass_ctx(ctx, layers, head_rows > 0);
 }
 
@@ -437,10 +459,6 @@ jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head) {
     return JL_OK;
 }
 
-jl_status record_pass(jl_model* m, cudaStream_t stream, int rows_cap, int layers, bool with_head) {
-    PassCtx c{m, stream, rows_cap, rows_cap};
-    return record_pass_ctx(c, layers, with_head);
-}
 
 jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool all,
                   uint32_t* out_ids, float* out_logits, bool draft_step) {
@@ -675,6 +693,7 @@ struct SpecGraph {
     jl_model* target = nullptr;
     jl_model* draft = nullptr;  // null for the greedy loop
     int G = 0;
+    int splits = 1;             // attention window CTAs per row the graph was built with
     cudaGraphExec_t exec = nullptr;
     SpecState* st = nullptr;
     uint32_t* tokens = nullptr;
@@ -772,7 +791,7 @@ jl_status build_spec_graph(SpecGraph* g) {
         JL_TRY(add_conditional(body, &prev, 1, h_step[i], cudaGraphCondTypeIf, &ifn, &ifb));
         const cudaGraphConditionalHandle nxt = i + 1 < G ? h_step[i + 1] : 0;
         JL_TRY(capture_into(ifb, st, nullptr, [&]() -> jl_status {
-            PassCtx c{D, st, 1, 1, true};
+            PassCtx c{D, st, 1, 1, true, g->splits};
             JL_TRY(record_pass_ctx(c, D->layers, true));
             k_draft_step<<<1, 1, 0, st>>>(g->st, D->pass, g->oracle_args, i, nxt);
             JL_CUDA(cudaGetLastError());
@@ -784,7 +803,7 @@ jl_status build_spec_graph(SpecGraph* g) {
     JL_TRY(capture_into(body, st, &prev, [&]() -> jl_status {
         k_verify_setup<<<1, 1, 0, st>>>(g->st, T->pass);
         JL_CUDA(cudaGetLastError());
-        PassCtx c{T, st, G + 1, G + 1};
+        PassCtx c{T, st, G + 1, G + 1, false, g->splits};
         JL_TRY(record_pass_ctx(c, T->layers, true));
         k_accept<<<1, 1, 0, st>>>(g->st, T->pass, D->pass, g->tokens, g->rounds, g->cap, h_loop, h_catch);
         JL_CUDA(cudaGetLastError());
@@ -797,7 +816,7 @@ jl_status build_spec_graph(SpecGraph* g) {
         cudaGraph_t ifb;
         JL_TRY(add_conditional(body, &prev, 1, h_catch, cudaGraphCondTypeIf, &ifn, &ifb));
         JL_TRY(capture_into(ifb, st, nullptr, [&]() -> jl_status {
-            PassCtx c{D, st, 2, 1, true};
+            PassCtx c{D, st, 2, 1, true, g->splits};
             JL_TRY(record_pass_ctx(c, D->layers, true));
             k_catchup_done<<<1, 1, 0, st>>>(g->st, D->pass, g->oracle_args);
             JL_CUDA(cudaGetLastError());
@@ -820,7 +839,7 @@ jl_status build_greedy_graph(SpecGraph* g) {
     cudaGraph_t body;
     JL_TRY(add_conditional(top, nullptr, 0, h_loop, cudaGraphCondTypeWhile, &loop_node, &body));
     JL_TRY(capture_into(body, st, nullptr, [&]() -> jl_status {
-        PassCtx c{T, st, 1, 1};
+        PassCtx c{T, st, 1, 1, false, g->splits};
         JL_TRY(record_pass_ctx(c, T->layers, true));
         k_greedy_step<<<1, 1, 0, st>>>(g->st, T->pass, g->tokens, h_loop);
         JL_CUDA(cudaGetLastError());
@@ -830,9 +849,17 @@ jl_status build_greedy_graph(SpecGraph* g) {
     return JL_OK;
 }
 
-jl_status get_graph(jl_model* target, jl_model* draft, int G, SpecGraph** out) {
+// The loop graph of (target, draft, G), built with at least `splits`
+// attention window CTAs per row (captured again when it had fewer).
+jl_status get_graph(jl_model* target, jl_model* draft, int G, int splits, SpecGraph** out) {
     for (auto* g : target->spec_graphs)
         if (g->draft == draft && g->G == G) {
+            if (g->splits < splits) {
+                if (g->exec) cudaGraphExecDestroy(g->exec);
+                g->exec = nullptr;
+                g->splits = splits;
+                JL_TRY(draft ? build_spec_graph(g) : build_greedy_graph(g));
+            }
             *out = g;
             return JL_OK;
         }
@@ -840,6 +867,7 @@ jl_status get_graph(jl_model* target, jl_model* draft, int G, SpecGraph** out) {
     g->target = target;
     g->draft = draft;
     g->G = G;
+    g->splits = splits;
     g->cap = target->max_positions + 2 * MAX_GAMMA + 8;
     JL_CUDA(cudaMalloc(&g->st, sizeof(SpecState)));
     JL_CUDA(cudaMalloc(&g->tokens, (size_t)g->cap * sizeof(uint32_t)));
@@ -891,7 +919,7 @@ jl_status generate(jl_model* m, const uint32_t* prompt, size_t n, size_t count, 
     if ((int32_t)next == m->eos || count == 1) return JL_OK;
     // the rest of the loop runs on the device
     SpecGraph* g = nullptr;
-    JL_TRY(get_graph(m, nullptr, 0, &g));
+    JL_TRY(get_graph(m, nullptr, 0, att_splits_for(m, n + count), &g));
     JL_TRY(cache_reserve(c, n + count, m->stream));
     SpecState* s = g->host_st;
     memset(s, 0, sizeof(SpecState));
@@ -1101,7 +1129,7 @@ jl_status generate_speculative(jl_model* T, jl_model* D, const uint32_t* prompt,
     dnext = oracle_token(host_oracle, (int32_t)dc->len, dnext);
 
     SpecGraph* g = nullptr;
-    JL_TRY(get_graph(T, D, G, &g));
+    JL_TRY(get_graph(T, D, G, std::max(att_splits_for(T, limit + G + 1), att_splits_for(D, limit + G + 1)), &g));
     // pages for every position the loop can reach
     JL_TRY(cache_reserve(tc, limit + G + 1, st));
     JL_TRY(cache_reserve(dc, limit + G + 1, st));

@@ -32,6 +32,8 @@ constexpr int HEAD = 128;        // head_dim of every Qwen3 model (engine/src/li
 constexpr int HALF = 64;         // RoPE rotates (i, i + 64) pairs (engine/src/lib.rs:297)
 constexpr int PAGE = 64;         // tokens per KV page
 constexpr int SMALL_M = 16;      // passes up to this many rows use the decode kernels (tensor-core MXFP4)
+constexpr int ATT_WIN = 2;       // KV pages per decode-attention window (one CTA per window over long contexts)
+constexpr int ATT_PART = 4 + HEAD;  // floats of one window's partial: max, sum, 2 pad, 128 outputs
 constexpr int MAX_SEQS = 64;     // sequences one pass may touch
 constexpr int MAX_GAMMA = 16;    // largest draft length of the device-resident loop
 
@@ -220,6 +222,14 @@ struct jl_model {
     // they have run, so a pass never reads a later pass's descriptors.
     jl::StageSlot stage[jl::STAGE_SLOTS];
     int stage_next = 0;
+    // decode attention over long contexts: one CTA per window of pages, a
+    // partial-sum workspace [kv_heads][16 rows][att_smax][group][4 + 128] f32
+    // and per (kv head, row) arrival counters (zero between launches)
+    int att_smax = 1;
+    float* att_ws = nullptr;
+    int* att_cnt = nullptr;
+    int small_graph_splits[5] = {};       // att_splits each small_graph was captured with
+    int draft_graph_splits[2] = {};
     uint32_t* host_out = nullptr;
     float* host_logits = nullptr;
     jl::Scratch s;
@@ -265,7 +275,6 @@ jl_status cache_reserve(jl_cache* c, size_t tokens, cudaStream_t stream);
 // Records the kernels of one forward pass on `stream`.  rows_cap bounds the
 // rows the pass may have; `layers` < m->layers stops early (Model::hidden);
 // with_head adds final norm, lm_head and argmax.
-jl_status record_pass(jl_model* m, cudaStream_t stream, int rows_cap, int layers, bool with_head);
 struct PassCtx;
 jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head);
 // Sets kernel attributes once per device, before any stream capture.
@@ -293,7 +302,12 @@ struct PassCtx {
     int rows_cap;   // rows the pass may hold
     int head_cap;   // predicted rows the pass may hold
     bool draft = false;  // a speculative loop's draft step (may take the CUDA-core path)
+    int att_splits = 1;  // decode attention: window CTAs per row in the launch grid (att_splits_for)
 };
+// Window CTAs per row a decode attention launch needs to cover contexts of
+// up to max_ctx positions: a power of two (so graphs rebuild rarely), at most
+// the model's att_smax.
+int att_splits_for(const jl_model* m, size_t max_ctx);
 jl_status launch_embed(const PassCtx& c);
 jl_status launch_rmsnorm(const PassCtx& c, const float* x, const uint16_t* w, float* out,
                          bool head_rows);

@@ -557,7 +557,6 @@ __global__ void __launch_bounds__(128) k_attention(PassBuf pb, const float* __re
 // dimensions to accumulate the 32 V rows.  The output row also goes out as
 // the o projection's input pieces; rows past the pass's row count get zero
 // pieces.
-constexpr int ATT_WIN = 2;              // pages per shared-memory window
 constexpr uint32_t ATT_WAIT = 1u << 22;  // polls before the page copy reports failure
 
 __host__ __device__ constexpr int att_page_bytes(int f32) { return PAGE * HEAD * (f32 ? 4 : 2); }
@@ -592,6 +591,15 @@ __device__ __forceinline__ NormRope norm_rope_args(const uint16_t* gw, const flo
     return r;
 }
 
+// Position-split workspace of the decode attention: per (kv head, row slot,
+// window, query head) the window's softmax max, sum and unnormalised output
+// (ATT_PART floats), and per (kv head, row slot) an arrival counter that the
+// last window CTA resets to zero.
+struct AttnSplit {
+    float* ws;
+    int* cnt;
+};
+
 // QK-RMSNorm and RoPE of one head held as dims (l, l+32, l+64, l+96) by lane
 // l (lib.rs:306-313, 372-388; the arithmetic of k_qk_rope_kv).
 __device__ __forceinline__ void norm_rope4(float& a0, float& a1, float& a2, float& a3, const NormRope& nr) {
@@ -622,7 +630,7 @@ template <int F32, int RAW>
 __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __restrict__ qkv, int ld,
                                                      int group, int split, KvView kv, float* __restrict__ out,
                                                      int out_ld, uint8_t* __restrict__ bout, int bN,
-                                                     AttnRaw raw) {
+                                                     AttnRaw raw, AttnSplit sp) {
     static_assert(PAGE % 32 == 0, "chunks of 32 positions stay inside a page");
     __shared__ float nk[2][HEAD], nv[2][HEAD];  // RAW: this pass's rows of this KV head
     __shared__ int npos[2];
@@ -653,6 +661,19 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
     }
     const int visible = valid ? rd.pos + 1 : 0;
     const int npages = (visible + PAGE - 1) / PAGE;
+    // Position splits (blockIdx.z): a row whose context spans more than one
+    // window of ATT_WIN pages takes one CTA per window, and the last of them
+    // to finish merges their partial softmax sums in window order; a row
+    // within one window is done by CTA z = 0 alone, as a whole.  The split
+    // depends only on the row's position; the host sizes every grid for its
+    // pass's longest row (a grid too small for a row, which no launch here
+    // makes, falls back to CTA z = 0 doing every window).
+    const int nwin = max(1, (npages + ATT_WIN - 1) / ATT_WIN);
+    const int nsplit = nwin <= (int)gridDim.z ? nwin : 1;
+    const int zs = blockIdx.z;
+    if (zs >= (valid ? nsplit : 1)) return;  // uniform over the CTA
+    const int w_lo = nsplit > 1 ? zs * ATT_WIN : 0;
+    const int w_hi = nsplit > 1 ? min(npages, w_lo + ATT_WIN) : npages;
     const int32_t* pt = valid ? pb.page_table[rd.seq] : nullptr;
     if (valid && threadIdx.x == 0) {
         ptx::mbar_init(&bar, 1);
@@ -676,7 +697,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
             ptx::bulk_g2s(kvs + (2 * i + 1) * PB, (const uint8_t*)kv.v + off, PB, &bar);
         }
     };
-    if (valid && threadIdx.x == 0) issue_window(0);
+    if (valid && threadIdx.x == 0) issue_window(w_lo);
     // RAW: the norm weights, rotation factors, this pass's row descriptors
     // and the row's cache page, all fixed before the pass began
     NormRope qnr = {}, knr = {};
@@ -689,7 +710,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
             rj = pb.row[warp];
             kgood = rj.pos >= 0 && rj.pos < kv.max_pos && rj.seq == rd.seq;
             knr = norm_rope_args(raw.kn, raw.rope, kgood ? rj.pos : 0, lane);
-            if (warp == row && kgood) kpage = pt[rj.pos / PAGE];
+            if (warp == row && kgood && zs == nsplit - 1) kpage = pt[rj.pos / PAGE];
         }
     }
     // Not RAW: the page of the position this warp re-fetches after the wait
@@ -728,7 +749,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
             nk[j][lane] = k0; nk[j][lane + 32] = k1; nk[j][lane + 64] = k2; nk[j][lane + 96] = k3;
             nv[j][lane] = v0; nv[j][lane + 32] = v1; nv[j][lane + 64] = v2; nv[j][lane + 96] = v3;
             if (lane == 0) npos[j] = good ? rj.pos : -1;
-            if (j == row && good) {  // the row's own K/V go to the cache
+            if (j == row && good && zs == nsplit - 1) {  // the row's own K/V go to the cache (once)
                 const int pg = kpage;
                 if (page_ok(kv, pg)) {
                     const size_t idx = kv_index(pg, kvh, rj.pos % PAGE, kv.kv_heads);
@@ -756,9 +777,9 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
     float m = -INFINITY, l = 0.f;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     bool ok = true;
-    for (int w0 = 0, it = 0; w0 < npages; w0 += ATT_WIN, ++it) {
+    for (int w0 = w_lo, it = 0; w0 < w_hi; w0 += ATT_WIN, ++it) {
         const int wn = min(ATT_WIN, npages - w0);
-        if (threadIdx.x == 0 && w0 > 0) issue_window(w0);
+        if (threadIdx.x == 0 && w0 > w_lo) issue_window(w0);
         if (!ptx::mbar_wait(&bar, it & 1, ATT_WAIT)) ok = false;
         if (RAW) {
             // this pass's rows (computed above, in the cache's element type)
@@ -882,21 +903,65 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
     }
     *(float4*)(&cacc[warp][4 * lane]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
     __syncthreads();
-    if (sub != 0) return;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < split; ++s2) M = fmaxf(M, cm[s2 * group + hw]);
-    float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int s2 = 0; s2 < split; ++s2) {
-        const int w2 = s2 * group + hw;
-        if (cm[w2] == -INFINITY) continue;  // no position fell to that warp
-        const float f = expf(cm[w2] - M);
-        L = fmaf(cl[w2], f, L);
-        const float4 a4 = *(const float4*)(&cacc[w2][4 * lane]);
-        o[0] = fmaf(a4.x, f, o[0]);
-        o[1] = fmaf(a4.y, f, o[1]);
-        o[2] = fmaf(a4.z, f, o[2]);
-        o[3] = fmaf(a4.w, f, o[3]);
+    // merge the head's warps in warp order (sub == 0 warps)
+    float M = -INFINITY, L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+    if (sub == 0) {
+        for (int s2 = 0; s2 < split; ++s2) M = fmaxf(M, cm[s2 * group + hw]);
+        for (int s2 = 0; s2 < split; ++s2) {
+            const int w2 = s2 * group + hw;
+            if (cm[w2] == -INFINITY) continue;  // no position fell to that warp
+            const float f = expf(cm[w2] - M);
+            L = fmaf(cl[w2], f, L);
+            const float4 a4 = *(const float4*)(&cacc[w2][4 * lane]);
+            o[0] = fmaf(a4.x, f, o[0]);
+            o[1] = fmaf(a4.y, f, o[1]);
+            o[2] = fmaf(a4.z, f, o[2]);
+            o[3] = fmaf(a4.w, f, o[3]);
+        }
     }
+    if (nsplit > 1) {
+        // publish this window's (max, sum, unnormalised output) per head;
+        // the last window CTA of the row to arrive merges them all
+        __shared__ int last_s;
+        float* part = sp.ws + (((size_t)(g * gridDim.y + row) * gridDim.z) * group) * ATT_PART;
+        if (sub == 0) {
+            float* P = part + ((size_t)zs * group + hw) * ATT_PART;
+            if (lane == 0) {
+                P[0] = M;
+                P[1] = L;
+            }
+            *(float4*)(P + 4 + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int* cnt = sp.cnt + g * gridDim.y + row;
+            const int t = atomicAdd(cnt, 1);
+            last_s = t == nsplit - 1;
+            if (last_s) *cnt = 0;  // every window has arrived: ready for the next pass
+        }
+        __syncthreads();
+        if (!last_s) return;
+        __threadfence();  // the other windows' partials are visible
+        if (sub != 0) return;
+        M = -INFINITY;
+        for (int z = 0; z < nsplit; ++z) M = fmaxf(M, __ldcg(part + ((size_t)z * group + hw) * ATT_PART));
+        L = 0.f;
+        o[0] = o[1] = o[2] = o[3] = 0.f;
+        for (int z = 0; z < nsplit; ++z) {
+            const float* P = part + ((size_t)z * group + hw) * ATT_PART;
+            const float mz = __ldcg(P);
+            if (mz == -INFINITY) continue;  // a window whose pages were all flagged
+            const float f = expf(mz - M);
+            L = fmaf(__ldcg(P + 1), f, L);
+            const float4 a4 = __ldcg((const float4*)(P + 4 + 4 * lane));
+            o[0] = fmaf(a4.x, f, o[0]);
+            o[1] = fmaf(a4.y, f, o[1]);
+            o[2] = fmaf(a4.z, f, o[2]);
+            o[3] = fmaf(a4.w, f, o[3]);
+        }
+    }
+    if (sub != 0) return;
 #pragma unroll
     for (int d = 0; d < 4; ++d) o[d] = __fdiv_rn(o[d], L);
     *(float4*)(out + (size_t)row * out_ld + h * HEAD + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
@@ -1141,6 +1206,10 @@ jl_status launch_qk_rope_kv(const PassCtx& c, int layer, const LayerW& L) {
                       kv_view(c.m, layer));
 }
 
+// Window CTAs per row in a decode attention launch: what the pass context
+// asks for, within the workspace the model holds.
+int att_grid_splits(const PassCtx& c) { return std::max(1, std::min(c.att_splits, c.m->att_smax)); }
+
 jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     dim3 grid(c.m->q_heads, c.rows_cap);
     const int group = c.m->q_heads / c.m->kv_heads;
@@ -1148,16 +1217,17 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     const int bN = 8 * c.rows_cap;
     if (c.rows_cap <= SMALL_M && group <= 8) {  // decode passes: a warp per query head
         const int split = att_split(group);
-        const dim3 g2(c.m->kv_heads, c.rows_cap), blk(32 * group * split);
+        const dim3 g2(c.m->kv_heads, c.rows_cap, att_grid_splits(c)), blk(32 * group * split);
         const int qw = c.m->q_heads * HEAD;
         const AttnRaw none{};
+        const AttnSplit sp{c.m->att_ws, c.m->att_cnt};
         if (c.m->kv.dtype == JL_KV_F32)
             return launch_pdl(k_attn_decode<1, 0>, g2, blk, att_smem(1), c.stream, c.m->pass,
                               (const float*)c.m->s.qkv, qkv_ld(c.m), group, split, kv_view(c.m, layer),
-                              c.m->s.attn, qw, bout, bN, none);
+                              c.m->s.attn, qw, bout, bN, none, sp);
         return launch_pdl(k_attn_decode<0, 0>, g2, blk, att_smem(0), c.stream, c.m->pass,
                           (const float*)c.m->s.qkv, qkv_ld(c.m), group, split, kv_view(c.m, layer), c.m->s.attn,
-                          qw, bout, bN, none);
+                          qw, bout, bN, none, sp);
     }
     if (c.m->kv.dtype == JL_KV_F32)
         return launch_pdl(k_attention<1>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
@@ -1208,8 +1278,9 @@ jl_status launch_attention_raw(const PassCtx& c, int layer, const uint16_t* qn, 
         return JL_ERR_INVALID_ARG;
     }
     const int split = att_split(group);
-    const dim3 g2(m->kv_heads, c.rows_cap), blk(32 * group * split);
+    const dim3 g2(m->kv_heads, c.rows_cap, att_grid_splits(c)), blk(32 * group * split);
     const int qw = m->q_heads * HEAD;
+    const AttnSplit sp{m->att_ws, m->att_cnt};
     AttnRaw raw;
     raw.qn = qn;
     raw.kn = kn;
@@ -1219,10 +1290,10 @@ jl_status launch_attention_raw(const PassCtx& c, int layer, const uint16_t* qn, 
     if (m->kv.dtype == JL_KV_F32)
         return launch_pdl(k_attn_decode<1, 1>, g2, blk, att_smem(1), c.stream, m->pass, (const float*)m->s.qkv,
                           qkv_ld(m), group, split, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr, 0,
-                          raw);
+                          raw, sp);
     return launch_pdl(k_attn_decode<0, 1>, g2, blk, att_smem(0), c.stream, m->pass, (const float*)m->s.qkv,
                       qkv_ld(m), group, split, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr, 0,
-                      raw);
+                      raw, sp);
 }
 
 jl_status launch_argmax(const PassCtx& c) {

@@ -96,6 +96,20 @@ jl_status finish_model(jl_model* m, const jl_model_options& o) {
     }
     m->kv.free_list.resize(m->kv.pages);
     for (size_t i = 0; i < m->kv.pages; ++i) m->kv.free_list[i] = (int32_t)(m->kv.pages - 1 - i);
+    // decode attention over long contexts: a window CTA's partial sums for
+    // every window a sequence of the pool can span
+    m->att_smax = (int)std::max<size_t>(1, (m->kv.pages + ATT_WIN - 1) / ATT_WIN);
+    {
+        const size_t group = (size_t)m->q_heads / m->kv_heads;
+        const size_t floats = (size_t)m->kv_heads * SMALL_M * m->att_smax * group * ATT_PART;
+        if (cudaMalloc(&m->att_ws, floats * sizeof(float)) != cudaSuccess ||
+            cudaMalloc(&m->att_cnt, (size_t)m->kv_heads * SMALL_M * sizeof(int)) != cudaSuccess) {
+            cudaGetLastError();
+            set_error("cannot allocate the attention split workspace");
+            return JL_ERR_OOM;
+        }
+        JL_CUDA(cudaMemset(m->att_cnt, 0, (size_t)m->kv_heads * SMALL_M * sizeof(int)));
+    }
     // scratch
     const int R = m->max_rows = o.max_pass_rows ? (int)o.max_pass_rows : 4096;
     const size_t H = m->hidden, QW = (size_t)m->q_heads * HEAD, KVW = (size_t)m->kv_heads * HEAD;
@@ -567,6 +581,8 @@ void model_free(jl_model* m) {
     cudaFree(m->scratch_arena);
     cudaFree(m->mx.arena);
     cudaFree(m->mx.scratch);
+    cudaFree(m->att_ws);
+    cudaFree(m->att_cnt);
     for (StageSlot& sl : m->stage) {
         if (sl.done) cudaEventDestroy(sl.done);
         cudaFreeHost(sl.hdr);

@@ -55,3 +55,20 @@ def test_qwen3_8b_speculative_properties():
     assert r.tokens == greedy and r.accepted == r.drafted
     _, lg = target.predict(PROMPT[:4], target.cache(), logits=True)
     assert np.isfinite(lg).all()
+
+
+def test_long_context_draft_and_verify_attention():
+    """A 600-token context: the draft's one-row steps (CUDA-core projections,
+    attention on raw q|k|v) and the target's 5-row verify passes both split
+    each row's attention over 128-position windows; speculative output must
+    still equal greedy output, and the 0.6B's own greedy stream must agree
+    with the draft path's proposals when p = 0 (every proposal accepted)."""
+    target = J.Model.from_config(O.PRESETS["qwen3-8b"], 0, mxfp4=True, kv_pool_tokens=2048)
+    draft = J.Model.from_config(O.PRESETS["qwen3-0.6b"], 1, mxfp4=True, kv_pool_tokens=2048)
+    prompt = O.prompt_ids(600, 151936, 3)
+    greedy = target.generate(prompt, 16)
+    r = J.generate_speculative(target, draft, prompt, 16, 4, oracle_stream=greedy, oracle_p=0.25,
+                               oracle_seed=5)
+    assert r.tokens == greedy
+    r = J.generate_speculative(target, draft, prompt, 16, 4)
+    assert r.tokens == greedy

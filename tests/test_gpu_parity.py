@@ -117,6 +117,32 @@ def test_multi_chunk_prefill_matches_oracle(oracles, key, n):
         assert rel_l2(lg, rlg) < 1e-5 and ids == rids
 
 
+@pytest.mark.parametrize("n", [300, 480])
+@pytest.mark.parametrize("key", [("tiny", False), ("tiny", True)])
+def test_long_context_attention_windows_match_oracle(oracles, key, n):
+    """Rows past 128 positions: one CTA per 128-position window, partial
+    softmax sums merged by the last window to finish.  Logits of the prompt's
+    last row, then greedy decoding on top of the long context."""
+    ref = oracles[key]
+    m = gpu_model(TINY, 0, key[1], kv_dtype=J.KV_F32)
+    prompt = O.prompt_ids(n, 1000, 4)
+    ids, lg = m.predict(prompt, m.cache(), all=False, logits=True)
+    rids, rlg = ref.predict(prompt, ref.cache(), all=False, logits=True)
+    assert rel_l2(lg, rlg) < 1e-5 and ids == rids
+    assert compare_streams(m.generate(prompt, 12), ref, prompt, 12) >= 6
+
+
+def test_long_context_speculative_equals_greedy():
+    target = gpu_model(TINY, 0, True)
+    draft = gpu_model(DRAFT, 1, True)
+    prompt = O.prompt_ids(300, 1000, 4)
+    greedy = target.generate(prompt, 24)
+    for p in (0.0, 0.5):
+        r = J.generate_speculative(target, draft, prompt, 24, 3, oracle_stream=greedy, oracle_p=p,
+                                   oracle_seed=7)
+        assert r.tokens == greedy
+
+
 def test_decode_after_prefill_matches_oracle(oracles):
     ref = oracles[("tiny", True)]
     m = gpu_model(TINY, 0, True, kv_dtype=J.KV_F32)
