@@ -430,10 +430,30 @@ def main():
             n = len(r.tokens) - len(prompt)
             sweep["real draft" if not stream else f"oracle p={p}"] = {
                 "tok_s": n / (r.decode_ms / 1000.0), "accepted": r.accepted, "drafted": r.drafted}
+        # the configuration's other draft lengths (same prompt and oracle stream)
+        for k in (2, 8):
+            r = J.generate_speculative(target, draft, prompt, args.new, k, oracle_stream=greedy,
+                                       oracle_p=args.p, oracle_seed=5)
+            assert r.tokens == greedy, "speculative output differs from greedy"
+            sweep[f"k={k} oracle p={args.p}"] = {
+                "tok_s": (len(r.tokens) - len(prompt)) / (r.decode_ms / 1000.0), "accepted": r.accepted,
+                "drafted": r.drafted}
         # greedy decode of the target alone, same device loop
         t0 = time.perf_counter()
         target.generate(prompt, args.new)
         sweep["greedy (no draft) e2e tok/s"] = args.new / (time.perf_counter() - t0)
+        # the configuration's long-context setting: a prefilled 2048-token context
+        if args.prompt < 2048:
+            lp = O.prompt_ids(2048, ti.vocab, 3 + dist.rank)
+            lg = target.generate(lp, args.new)
+            J.generate_speculative(target, draft, lp, args.new, args.gamma, oracle_stream=lg,
+                                   oracle_p=args.p, oracle_seed=5)  # warm: graphs for the longer context
+            r = J.generate_speculative(target, draft, lp, args.new, args.gamma, oracle_stream=lg,
+                                       oracle_p=args.p, oracle_seed=5)
+            assert r.tokens == lg, "speculative output differs from greedy"
+            sweep[f"context 2048, k={args.gamma} oracle p={args.p}"] = {
+                "tok_s": (len(r.tokens) - len(lp)) / (r.decode_ms / 1000.0), "accepted": r.accepted,
+                "drafted": r.drafted}
         line["sweep"] = sweep
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(J, O, target, draft, prompt, greedy, args, args.cpu_seconds)
