@@ -291,6 +291,45 @@ jl_status jl_generate_speculative(jl_model* target, jl_model* draft, const uint3
                                   size_t n, size_t count, const jl_schedule* schedule,
                                   const jl_spec_options* opts, jl_spec_result* result);
 
+/* ------------------------------------------------------------------------
+ * A batch of independent sequences on one GPU, decoded in lockstep rounds
+ * (the benchmark configuration with a per-GPU batch of sequences).  The
+ * reference engine has no batch call: it decodes one sequence per call
+ * (model.rs:268-285, speculative.rs:43-143), and each sequence here gets
+ * exactly the tokens and counters that call gives it alone.  Weights are
+ * read once per round for the whole batch.
+ * ---------------------------------------------------------------------- */
+#define JL_MAX_BATCH 64
+
+typedef struct jl_batch_stats {
+    double prefill_ms;       /* every sequence's prefill, GPU time */
+    double decode_ms;        /* the batched loop, GPU time */
+    size_t rounds;           /* lockstep rounds */
+    size_t target_passes;    /* target passes of up to 16 rows */
+    size_t draft_passes;     /* draft passes of up to 16 rows */
+} jl_batch_stats;
+
+/* Greedy decode of `batch` sequences (1..JL_MAX_BATCH): prompts[i] holds
+ * prompt_lens[i] ids.  results[i].tokens (capacity tokens_cap, at least
+ * prompt_lens[i] + count or the context limit) receives prompt + generated
+ * ids and n_tokens its length; the other result fields are zero except
+ * verify_passes (passes the sequence took part in), prefill_ms and
+ * decode_ms (the whole batch's).  stats may be NULL. */
+jl_status jl_generate_batch(jl_model* m, size_t batch, const uint32_t* const* prompts,
+                            const size_t* prompt_lens, size_t count, jl_spec_result* results,
+                            jl_batch_stats* stats);
+
+/* jl_generate_speculative for each of `batch` sequences: schedules[i] and
+ * opts[i] (opts may be NULL; its mode is ignored, the loop runs on the
+ * device) belong to sequence i, and results[i] is filled as that call
+ * fills it, with prefill_ms and decode_ms the whole batch's.  batch x
+ * (largest max_gamma + 1) must not exceed 512.  stats may be NULL. */
+jl_status jl_generate_speculative_batch(jl_model* target, jl_model* draft, size_t batch,
+                                        const uint32_t* const* prompts, const size_t* prompt_lens,
+                                        size_t count, const jl_schedule* schedules,
+                                        const jl_spec_options* opts, jl_spec_result* results,
+                                        jl_batch_stats* stats);
+
 #ifdef __cplusplus
 }
 #endif

@@ -355,4 +355,24 @@ jl_status jl_generate_speculative(jl_model* target, jl_model* draft, const uint3
     JL_GUARD({ return generate_speculative(target, draft, prompt, n, count, *schedule, o, result); })
 }
 
+jl_status jl_generate_batch(jl_model* m, size_t batch, const uint32_t* const* prompts,
+                            const size_t* prompt_lens, size_t count, jl_spec_result* results,
+                            jl_batch_stats* stats) {
+    JL_NEED(m && prompts && prompt_lens && results, "model, prompts, prompt_lens and results must be non-null");
+    JL_GUARD({ return generate_batch(m, batch, prompts, prompt_lens, count, results, stats); })
+}
+
+jl_status jl_generate_speculative_batch(jl_model* target, jl_model* draft, size_t batch,
+                                        const uint32_t* const* prompts, const size_t* prompt_lens,
+                                        size_t count, const jl_schedule* schedules,
+                                        const jl_spec_options* opts, jl_spec_result* results,
+                                        jl_batch_stats* stats) {
+    JL_NEED(target && draft && prompts && prompt_lens && schedules && results,
+            "target, draft, prompts, prompt_lens, schedules and results must be non-null");
+    JL_GUARD({
+        return generate_speculative_batch(target, draft, batch, prompts, prompt_lens, count, schedules, opts,
+                                          results, stats);
+    })
+}
+
 }  // extern "C"

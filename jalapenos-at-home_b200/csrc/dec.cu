@@ -359,7 +359,7 @@ jl_status record_dec_pass(const PassCtx& c, int layers) {
             d.norm = norm;
             d.y = y;
             d.ldy = ldy;
-            d.hdr = m->pass.hdr;
+            d.hdr = c.pass().hdr;
             d.mcap = M;
             d.err = m->counters;
             const int tr = epi == DEC_STORE ? 16 : 8;

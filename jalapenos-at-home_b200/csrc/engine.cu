@@ -17,8 +17,22 @@
 
 #include "jl_internal.h"
 #include "kernels.cuh"
+#include "loop.cuh"
 
 namespace jl {
+
+jl_status add_conditional(cudaGraph_t graph, cudaGraphNode_t* deps, size_t ndeps,
+                          cudaGraphConditionalHandle h, cudaGraphConditionalNodeType type,
+                          cudaGraphNode_t* node, cudaGraph_t* body) {
+    cudaGraphNodeParams p = {};
+    p.type = cudaGraphNodeTypeConditional;
+    p.conditional.handle = h;
+    p.conditional.type = type;
+    p.conditional.size = 1;
+    JL_CUDA(cudaGraphAddNode(node, graph, deps, ndeps, &p));
+    *body = p.conditional.phGraph_out[0];
+    return JL_OK;
+}
 
 int att_splits_for(const jl_model* m, size_t max_ctx) {
     const size_t pages = (max_ctx + PAGE - 1) / PAGE;
@@ -45,224 +59,6 @@ jl_status stage_end(jl_model* m, StageSlot* s, cudaStream_t st) {
     s->pending = true;
     return JL_OK;
 }
-
-namespace {
-
-constexpr int HEAD_CAP = 512;  // predicted rows per pass (longer all=true calls are chunked)
-
-__host__ __device__ inline void philox10_hd(uint32_t c[4], uint32_t k0, uint32_t k1) {
-    for (int r = 0; r < 10; ++r) {
-        if (r) { k0 += 0x9E3779B9u; k1 += 0xBB67AE85u; }
-        const uint64_t p0 = (uint64_t)0xD2511F53u * c[0];
-        const uint64_t p1 = (uint64_t)0xCD9E8D57u * c[2];
-        const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0, n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
-        c[0] = n0; c[1] = (uint32_t)p1; c[2] = n2; c[3] = (uint32_t)p0;
-    }
-}
-
-// Oracle-draft proposal for `position`: the scripted stream's token, or with
-// probability p a uniform id, both drawn from one Philox block keyed by the
-// seed and the position.  `own` is the draft model's prediction.
-struct Oracle {
-    const uint32_t* stream;  // device or host, matching the caller
-    int32_t len;
-    double p;
-    uint64_t seed;
-    int32_t vocab;
-};
-
-__host__ __device__ inline uint32_t oracle_token(const Oracle& o, int32_t position, uint32_t own) {
-    if (!o.stream || position >= o.len) return own;
-    uint32_t c[4] = {(uint32_t)position, 0u, 0u, 0x6f726163u};
-    philox10_hd(c, (uint32_t)o.seed, 0x64726166u);
-    if ((double)c[0] + 0.5 < o.p * 4294967296.0) return c[1] % (uint32_t)o.vocab;
-    return o.stream[position];
-}
-
-// ---------------------------------------------------------------------------
-// device-side state of the generation loops
-
-struct SpecState {
-    int32_t n_tokens, limit, eos, start;
-    int32_t gamma, max_gamma, adaptive, budget;
-    int32_t n_proposed, pending, first_pred, draft_next;
-    int32_t target_len, draft_len, done, catch_rows;
-    int32_t drafted, accepted, rounds, draft_passes, verify_passes;
-    int32_t iterations;  // loop bodies entered; every round adds >= 1 token, so <= limit
-    int32_t fault;       // set when a guard stopped the loop
-    int32_t proposed[MAX_GAMMA];
-};
-
-__device__ inline void set_row(PassBuf pb, int i, uint32_t token, int32_t pos) {
-    RowDesc r;
-    r.token = token;
-    r.seq = 0;
-    r.pos = pos;
-    r.pad = 0;
-    pb.row[i] = r;
-}
-
-// Conditional handles of one round: IF nodes of draft steps 1..G-1.  Their
-// values persist across WHILE iterations, so every round clears them first.
-struct StepHandles {
-    cudaGraphConditionalHandle h[MAX_GAMMA];
-    int n;
-};
-
-// speculative.rs:79-93, first iteration: propose draft_next, then decide
-// whether the draft runs again.
-__global__ void k_round_begin(SpecState* st, PassBuf draft, cudaGraphConditionalHandle loop,
-                              StepHandles steps, cudaGraphConditionalHandle catchup) {
-    SpecState& s = *st;
-    cudaGraphSetConditional(catchup, 0);
-    for (int i = 1; i < steps.n; ++i) cudaGraphSetConditional(steps.h[i], 0);
-    s.iterations += 1;
-    if (s.iterations > s.limit + 1) s.fault = 1;  // cannot happen: each round adds a token
-    if (s.done || s.fault || s.n_tokens >= s.limit) {
-        s.done = 1;
-        cudaGraphSetConditional(loop, 0);
-        return;
-    }
-    s.start = s.n_tokens;
-    s.budget = min(s.gamma, s.limit - s.start);
-    s.proposed[0] = s.draft_next;
-    s.n_proposed = 1;
-    const bool more = !(s.budget == 1 || s.draft_next == s.eos);
-    if (more) {
-        draft.hdr->rows = 1;
-        draft.hdr->head_rows = 1;
-        draft.head_row[0] = 0;
-        set_row(draft, 0, (uint32_t)s.draft_next, s.draft_len);
-    }
-    if (steps.n > 1) cudaGraphSetConditional(steps.h[1], more ? 1 : 0);
-}
-
-// After draft pass i of a round (speculative.rs:84-92).
-__global__ void k_draft_step(SpecState* st, PassBuf draft, Oracle o, int i,
-                             cudaGraphConditionalHandle next) {
-    SpecState& s = *st;
-    s.draft_len += 1;
-    s.draft_passes += 1;
-    const uint32_t tok = oracle_token(o, s.draft_len, draft.out_ids[0]);
-    s.draft_next = (int32_t)tok;
-    s.proposed[i] = (int32_t)tok;
-    s.n_proposed = i + 1;
-    const bool more = !(i + 1 == s.budget || (int32_t)tok == s.eos);
-    if (more) set_row(draft, 0, tok, s.draft_len);
-    if (next) cudaGraphSetConditional(next, more ? 1 : 0);
-}
-
-// speculative.rs:95-97: [pending correction] + proposals, predict after every row.
-__global__ void k_verify_setup(SpecState* st, PassBuf target) {
-    SpecState& s = *st;
-    int rows = 0;
-    if (s.pending >= 0) set_row(target, rows++, (uint32_t)s.pending, s.target_len);
-    for (int j = 0; j < s.n_proposed; ++j) {
-        set_row(target, rows, (uint32_t)s.proposed[j], s.target_len + rows);
-        ++rows;
-    }
-    target.hdr->rows = rows;
-    target.hdr->head_rows = rows;
-    for (int j = 0; j < rows; ++j) target.head_row[j] = j;
-}
-
-// speculative.rs:99-140: greedy acceptance, schedule feedback, rollback by
-// length, correction / bonus token and the draft catch-up rows.
-__global__ void k_accept(SpecState* st, PassBuf target, PassBuf draft, uint32_t* tokens,
-                         jl_round_stats* rounds, int32_t rounds_cap,
-                         cudaGraphConditionalHandle loop, cudaGraphConditionalHandle catchup) {
-    SpecState& s = *st;
-    const int rows = target.hdr->rows;
-    s.target_len += rows;
-    s.verify_passes += 1;
-    int32_t preds[MAX_GAMMA + 2];
-    int np = 0;
-    if (s.first_pred >= 0) preds[np++] = s.first_pred;
-    for (int j = 0; j < rows; ++j) preds[np++] = (int32_t)target.out_ids[j];
-    s.first_pred = -1;
-    s.pending = -1;
-    int accepted = 0;
-    int32_t next = preds[0];
-    while (accepted < s.n_proposed && s.proposed[accepted] == next) {
-        ++accepted;
-        next = preds[accepted];
-    }
-    // DraftSchedule::observe (scheduler.rs:33-44)
-    const int gamma = s.gamma, drafted = s.n_proposed;
-    if (s.adaptive && drafted == s.gamma) {
-        if (accepted == drafted) s.gamma = min(s.gamma + 1, s.max_gamma);
-        else if (accepted < (drafted + 1) / 2) s.gamma = max(s.gamma / 2, 1);
-    }
-    if (s.rounds < rounds_cap) {
-        jl_round_stats r;
-        r.gamma = (uint32_t)gamma;
-        r.drafted = (uint32_t)drafted;
-        r.accepted = (uint32_t)accepted;
-        r.next_gamma = (uint32_t)s.gamma;
-        rounds[s.rounds] = r;
-    }
-    s.rounds += 1;
-    s.drafted += drafted;
-    s.accepted += accepted;
-    // budget <= limit - start keeps n_tokens <= limit; the guards only bound writes
-    for (int j = 0; j < accepted && s.n_tokens < s.limit; ++j) tokens[s.n_tokens++] = (uint32_t)s.proposed[j];
-    bool stop = (accepted > 0 && (int32_t)tokens[s.n_tokens - 1] == s.eos) || s.n_tokens >= s.limit;
-    if (!stop) {
-        s.target_len = s.start + accepted;
-        s.draft_len = min(s.start + accepted, s.draft_len);
-        tokens[s.n_tokens++] = (uint32_t)next;
-        stop = next == s.eos || s.n_tokens >= s.limit;
-    }
-    if (stop) {
-        s.done = 1;
-        cudaGraphSetConditional(loop, 0);
-        cudaGraphSetConditional(catchup, 0);
-        return;
-    }
-    s.pending = next;
-    // The last accepted proposal may not be in the draft cache yet: feed it
-    // together with the bonus token (speculative.rs:134-138).
-    const int tail = s.n_tokens - s.draft_len;
-    if (tail < 1 || tail > 2) {  // cannot happen; stop rather than run a malformed pass
-        s.fault = 1;
-        s.done = 1;
-        cudaGraphSetConditional(loop, 0);
-        cudaGraphSetConditional(catchup, 0);
-        return;
-    }
-    s.catch_rows = tail;
-    for (int j = 0; j < tail; ++j) set_row(draft, j, tokens[s.draft_len + j], s.draft_len + j);
-    draft.hdr->rows = tail;
-    draft.hdr->head_rows = 1;
-    draft.head_row[0] = tail - 1;
-    cudaGraphSetConditional(catchup, 1);
-}
-
-__global__ void k_catchup_done(SpecState* st, PassBuf draft, Oracle o) {
-    SpecState& s = *st;
-    s.draft_len += s.catch_rows;
-    s.draft_passes += 1;
-    s.draft_next = (int32_t)oracle_token(o, s.draft_len, draft.out_ids[0]);
-}
-
-// Greedy loop (model.rs:277-283): after each single-row pass, append the
-// prediction and stop at eos or the count.
-__global__ void k_greedy_step(SpecState* st, PassBuf pb, uint32_t* tokens,
-                              cudaGraphConditionalHandle loop) {
-    SpecState& s = *st;
-    s.target_len += 1;
-    s.iterations += 1;
-    const uint32_t nxt = pb.out_ids[0];
-    if (s.n_tokens < s.limit) tokens[s.n_tokens++] = nxt;
-    if ((int32_t)nxt == s.eos || s.n_tokens >= s.limit || s.iterations > s.limit) {
-        s.done = 1;
-        cudaGraphSetConditional(loop, 0);
-        return;
-    }
-    set_row(pb, 0, nxt, s.target_len);
-}
-
-// ---------------------------------------------------------------------------
 
 double elapsed_ms(cudaEvent_t a, cudaEvent_t b) {
     float ms = 0.f;
@@ -292,6 +88,99 @@ jl_status check_ids(const jl_model* m, const uint32_t* ids, size_t n) {
             return JL_ERR_INVALID_ARG;
         }
     return JL_OK;
+}
+
+namespace {
+
+constexpr int HEAD_CAP = 512;  // predicted rows per pass (longer all=true calls are chunked)
+
+__device__ inline void set_row(PassBuf pb, int i, uint32_t token, int32_t pos) {
+    int n = i;
+    put_row(pb.row, n, token, pos, 0);
+}
+
+// Conditional handles of one round: IF nodes of draft steps 1..G-1.  Their
+// values persist across WHILE iterations, so every round clears them first.
+struct StepHandles {
+    cudaGraphConditionalHandle h[MAX_GAMMA];
+    int n;
+};
+
+// speculative.rs:79-93, first iteration: propose draft_next, then decide
+// whether the draft runs again.
+__global__ void k_round_begin(SpecState* st, PassBuf draft, cudaGraphConditionalHandle loop,
+                              StepHandles steps, cudaGraphConditionalHandle catchup) {
+    SpecState& s = *st;
+    cudaGraphSetConditional(catchup, 0);
+    for (int i = 1; i < steps.n; ++i) cudaGraphSetConditional(steps.h[i], 0);
+    s.iterations += 1;
+    if (s.iterations > s.limit + 1) s.fault = 1;  // cannot happen: each round adds a token
+    int n = 0;
+    if (!seq_round_begin(s, draft.row, n, 0)) {
+        cudaGraphSetConditional(loop, 0);
+        return;
+    }
+    if (n) {
+        draft.hdr->rows = 1;
+        draft.hdr->head_rows = 1;
+        draft.head_row[0] = 0;
+    }
+    if (steps.n > 1) cudaGraphSetConditional(steps.h[1], n ? 1 : 0);
+}
+
+// After draft pass i of a round (speculative.rs:84-92).
+__global__ void k_draft_step(SpecState* st, PassBuf draft, Oracle o, int i,
+                             cudaGraphConditionalHandle next) {
+    int n = 0;
+    seq_draft_step(*st, o, i, draft.out_ids[0], draft.row, n, 0);
+    if (next) cudaGraphSetConditional(next, n ? 1 : 0);
+}
+
+// speculative.rs:95-97: [pending correction] + proposals, predict after every row.
+__global__ void k_verify_setup(SpecState* st, PassBuf target) {
+    int rows = 0;
+    seq_verify_rows(*st, target.row, rows, 0);
+    target.hdr->rows = rows;
+    target.hdr->head_rows = rows;
+    for (int j = 0; j < rows; ++j) target.head_row[j] = j;
+}
+
+// speculative.rs:99-140: greedy acceptance, schedule feedback, rollback by
+// length, correction / bonus token and the draft catch-up rows.
+__global__ void k_accept(SpecState* st, PassBuf target, PassBuf draft, uint32_t* tokens,
+                         jl_round_stats* rounds, int32_t rounds_cap,
+                         cudaGraphConditionalHandle loop, cudaGraphConditionalHandle catchup) {
+    int n = 0;
+    if (!seq_accept(*st, target.out_ids, tokens, rounds, rounds_cap, draft.row, n, 0)) {
+        cudaGraphSetConditional(loop, 0);
+        cudaGraphSetConditional(catchup, 0);
+        return;
+    }
+    draft.hdr->rows = n;
+    draft.hdr->head_rows = 1;
+    draft.head_row[0] = n - 1;
+    cudaGraphSetConditional(catchup, 1);
+}
+
+__global__ void k_catchup_done(SpecState* st, PassBuf draft, Oracle o) {
+    seq_catchup_done(*st, o, draft.out_ids[0]);
+}
+
+// Greedy loop (model.rs:277-283): after each single-row pass, append the
+// prediction and stop at eos or the count.
+__global__ void k_greedy_step(SpecState* st, PassBuf pb, uint32_t* tokens,
+                              cudaGraphConditionalHandle loop) {
+    SpecState& s = *st;
+    s.target_len += 1;
+    s.iterations += 1;
+    const uint32_t nxt = pb.out_ids[0];
+    if (s.n_tokens < s.limit) tokens[s.n_tokens++] = nxt;
+    if ((int32_t)nxt == s.eos || s.n_tokens >= s.limit || s.iterations > s.limit) {
+        s.done = 1;
+        cudaGraphSetConditional(loop, 0);
+        return;
+    }
+    set_row(pb, 0, nxt, s.target_len);
 }
 
 // Stages one pass's rows from the host and runs it on m->stream.
@@ -717,41 +606,6 @@ void spec_graph_free(SpecGraph* g) {
 }
 
 namespace {
-
-jl_status add_conditional(cudaGraph_t graph, cudaGraphNode_t* deps, size_t ndeps,
-                          cudaGraphConditionalHandle h, cudaGraphConditionalNodeType type,
-                          cudaGraphNode_t* node, cudaGraph_t* body) {
-    cudaGraphNodeParams p = {};
-    p.type = cudaGraphNodeTypeConditional;
-    p.conditional.handle = h;
-    p.conditional.type = type;
-    p.conditional.size = 1;
-    JL_CUDA(cudaGraphAddNode(node, graph, deps, ndeps, &p));
-    *body = p.conditional.phGraph_out[0];
-    return JL_OK;
-}
-
-// Captures the kernels that `fn` launches on `stream` into `graph`, after
-// `dep` (or as roots when dep is null); returns the capture's last nodes.
-template <class F>
-jl_status capture_into(cudaGraph_t graph, cudaStream_t stream, cudaGraphNode_t* dep, F fn,
-                       std::vector<cudaGraphNode_t>* tail) {
-    JL_CUDA(cudaStreamBeginCaptureToGraph(stream, graph, dep, nullptr, dep ? 1 : 0,
-                                          cudaStreamCaptureModeThreadLocal));
-    jl_status rs = fn();
-    if (rs == JL_OK && tail) {
-        cudaStreamCaptureStatus cs;
-        const cudaGraphNode_t* deps = nullptr;
-        size_t nd = 0;
-        cudaError_t e = cudaStreamGetCaptureInfo(stream, &cs, nullptr, nullptr, &deps, &nd);
-        if (e == cudaSuccess) tail->assign(deps, deps + nd);
-    }
-    cudaGraph_t out;
-    cudaError_t ce = cudaStreamEndCapture(stream, &out);
-    if (rs != JL_OK) return rs;
-    JL_CUDA(ce);
-    return JL_OK;
-}
 
 jl_status build_spec_graph(SpecGraph* g) {
     jl_model* T = g->target;

@@ -193,7 +193,8 @@ struct KvPool {
     size_t page_elems = 0;                // kv_heads * PAGE * HEAD
 };
 
-struct SpecGraph;  // device-resident speculative loop (engine.cu)
+struct SpecGraph;   // device-resident speculative loop (engine.cu)
+struct BatchGraph;  // device-resident loop over a batch of sequences (batch.cu)
 
 }  // namespace jl
 
@@ -239,6 +240,7 @@ struct jl_model {
     cudaGraphExec_t small_graph[5] = {};  // full pass for rows <= 1, 2, 4, 8, 16
     cudaGraphExec_t draft_graph[2] = {};  // draft-step pass of 1 or 2 rows (profiling)
     std::vector<jl::SpecGraph*> spec_graphs;  // owned; freed by model_free
+    std::vector<jl::BatchGraph*> batch_graphs;  // owned; freed by model_free
     std::vector<jl_cache*> caches;              // live caches; detached by model_free
     int* counters = nullptr;              // zeroed split-K / reduction counters
     std::map<std::string, std::pair<const void*, size_t>> tensor_index;  // name -> device bytes
@@ -294,6 +296,14 @@ jl_status generate_speculative(jl_model* target, jl_model* draft, const uint32_t
                                size_t n, size_t count, const jl_schedule& sched,
                                const jl_spec_options& opts, jl_spec_result* res);
 void spec_graph_free(SpecGraph* g);
+// A batch of independent sequences decoded in lockstep rounds (batch.cu).
+jl_status generate_batch(jl_model* m, size_t batch, const uint32_t* const* prompts, const size_t* lens,
+                         size_t count, jl_spec_result* results, jl_batch_stats* stats);
+jl_status generate_speculative_batch(jl_model* target, jl_model* draft, size_t batch,
+                                     const uint32_t* const* prompts, const size_t* lens, size_t count,
+                                     const jl_schedule* schedules, const jl_spec_options* opts,
+                                     jl_spec_result* results, jl_batch_stats* stats);
+void batch_graph_free(BatchGraph* g);
 
 // ---- kernel launchers (kernels.cu) ---------------------------------------------
 struct PassCtx {
@@ -303,6 +313,10 @@ struct PassCtx {
     int head_cap;   // predicted rows the pass may hold
     bool draft = false;  // a speculative loop's draft step (may take the CUDA-core path)
     int att_splits = 1;  // decode attention: window CTAs per row in the launch grid (att_splits_for)
+    // The rows this pass reads: by default the model's own pass buffer; a
+    // batched loop points each 16-row chunk pass at its slice of a larger one.
+    PassBuf view{};
+    const PassBuf& pass() const { return view.hdr ? view : m->pass; }
 };
 // Window CTAs per row a decode attention launch needs to cover contexts of
 // up to max_ctx positions: a power of two (so graphs rebuild rarely), at most

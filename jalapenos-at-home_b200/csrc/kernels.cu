@@ -1121,7 +1121,7 @@ jl_status run_skinny(const PassCtx& c, int use_head, const float* x, int ldx, co
     const int per_sm = smem <= 48 * 1024 ? 4 : (smem <= 100 * 1024 ? 2 : 1);
     int grid = std::min((groups + 7) / 8, sm_count() * per_sm);
     grid = std::max(grid, 1);
-    return launch_pdl(kern, dim3(grid), dim3(256), smem, c.stream, (const PassHdr*)c.m->pass.hdr, use_head,
+    return launch_pdl(kern, dim3(grid), dim3(256), smem, c.stream, (const PassHdr*)c.pass().hdr, use_head,
                       c.m->max_rows, x, ldx, p, y, ldy);
 }
 
@@ -1135,7 +1135,7 @@ jl_status run_proj_kind(const PassCtx& c, int use_head, const float* x, int ldx,
         return run_skinny<KIND, EPI, 2, 2>(c, use_head, x, ldx, p, y, ldy);
     }
     dim3 grid((p.total + 63) / 64, (cap + 63) / 64);
-    return launch_pdl(k_gemm<KIND, EPI>, grid, dim3(256), 0, c.stream, (const PassHdr*)c.m->pass.hdr,
+    return launch_pdl(k_gemm<KIND, EPI>, grid, dim3(256), 0, c.stream, (const PassHdr*)c.pass().hdr,
                       use_head, cap, x, ldx, p, y, ldy);
 }
 
@@ -1181,7 +1181,7 @@ jl_status configure_kernels() {
 }
 
 jl_status launch_embed(const PassCtx& c) {
-    return launch_pdl(k_embed, dim3(c.rows_cap), dim3(256), 0, c.stream, c.m->pass, c.m->embed, c.m->s.x,
+    return launch_pdl(k_embed, dim3(c.rows_cap), dim3(256), 0, c.stream, c.pass(), c.m->embed, c.m->s.x,
                       c.m->hidden);
 }
 
@@ -1189,7 +1189,7 @@ jl_status launch_rmsnorm(const PassCtx& c, const float* x, const uint16_t* w, fl
                          bool head_rows) {
     const int h = c.m->hidden;
     return launch_pdl(k_rmsnorm, dim3(head_rows ? c.head_cap : c.rows_cap), dim3(256), 0, c.stream,
-                      c.m->pass, x, h, w, out, h, h, head_rows ? 1 : 0);
+                      c.pass(), x, h, w, out, h, h, head_rows ? 1 : 0);
 }
 
 jl_status launch_qkv(const PassCtx& c, const LayerW& L) {
@@ -1201,7 +1201,7 @@ jl_status launch_qkv(const PassCtx& c, const LayerW& L) {
 }
 
 jl_status launch_qk_rope_kv(const PassCtx& c, int layer, const LayerW& L) {
-    return launch_pdl(k_qk_rope_kv, dim3(c.rows_cap), dim3(256), 0, c.stream, c.m->pass, c.m->s.qkv,
+    return launch_pdl(k_qk_rope_kv, dim3(c.rows_cap), dim3(256), 0, c.stream, c.pass(), c.m->s.qkv,
                       qkv_ld(c.m), c.m->q_heads, L.q_norm, L.k_norm, (const float2*)c.m->rope,
                       kv_view(c.m, layer));
 }
@@ -1222,17 +1222,17 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
         const AttnRaw none{};
         const AttnSplit sp{c.m->att_ws, c.m->att_cnt};
         if (c.m->kv.dtype == JL_KV_F32)
-            return launch_pdl(k_attn_decode<1, 0>, g2, blk, att_smem(1), c.stream, c.m->pass,
+            return launch_pdl(k_attn_decode<1, 0>, g2, blk, att_smem(1), c.stream, c.pass(),
                               (const float*)c.m->s.qkv, qkv_ld(c.m), group, split, kv_view(c.m, layer),
                               c.m->s.attn, qw, bout, bN, none, sp);
-        return launch_pdl(k_attn_decode<0, 0>, g2, blk, att_smem(0), c.stream, c.m->pass,
+        return launch_pdl(k_attn_decode<0, 0>, g2, blk, att_smem(0), c.stream, c.pass(),
                           (const float*)c.m->s.qkv, qkv_ld(c.m), group, split, kv_view(c.m, layer), c.m->s.attn,
                           qw, bout, bN, none, sp);
     }
     if (c.m->kv.dtype == JL_KV_F32)
-        return launch_pdl(k_attention<1>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
+        return launch_pdl(k_attention<1>, grid, dim3(128), 0, c.stream, c.pass(), (const float*)c.m->s.qkv,
                           qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn, bout, bN);
-    return launch_pdl(k_attention<0>, grid, dim3(128), 0, c.stream, c.m->pass, (const float*)c.m->s.qkv,
+    return launch_pdl(k_attention<0>, grid, dim3(128), 0, c.stream, c.pass(), (const float*)c.m->s.qkv,
                       qkv_ld(c.m), c.m->q_heads, group, kv_view(c.m, layer), c.m->s.attn, bout, bN);
 }
 
@@ -1288,16 +1288,16 @@ jl_status launch_attention_raw(const PassCtx& c, int layer, const uint16_t* qn, 
     raw.k_off = qw;
     raw.v_off = qw + m->kv_heads * HEAD;
     if (m->kv.dtype == JL_KV_F32)
-        return launch_pdl(k_attn_decode<1, 1>, g2, blk, att_smem(1), c.stream, m->pass, (const float*)m->s.qkv,
+        return launch_pdl(k_attn_decode<1, 1>, g2, blk, att_smem(1), c.stream, c.pass(), (const float*)m->s.qkv,
                           qkv_ld(m), group, split, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr, 0,
                           raw, sp);
-    return launch_pdl(k_attn_decode<0, 1>, g2, blk, att_smem(0), c.stream, m->pass, (const float*)m->s.qkv,
+    return launch_pdl(k_attn_decode<0, 1>, g2, blk, att_smem(0), c.stream, c.pass(), (const float*)m->s.qkv,
                       qkv_ld(m), group, split, kv_view(m, layer), m->s.attn, qw, (uint8_t*)nullptr, 0,
                       raw, sp);
 }
 
 jl_status launch_argmax(const PassCtx& c) {
-    return launch_pdl(k_argmax, dim3(c.head_cap), dim3(1024), 0, c.stream, c.m->pass,
+    return launch_pdl(k_argmax, dim3(c.head_cap), dim3(1024), 0, c.stream, c.pass(),
                       (const float*)c.m->s.logits, c.m->vocab);
 }
 

@@ -567,6 +567,8 @@ void model_free(jl_model* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     for (auto* g : m->spec_graphs) spec_graph_free(g);
     m->spec_graphs.clear();
+    for (auto* g : m->batch_graphs) batch_graph_free(g);
+    m->batch_graphs.clear();
     // caches may outlive their model (a garbage collector frees both in any
     // order): they keep their own page tables and forget the model
     for (jl_cache* c : m->caches) c->m = nullptr;

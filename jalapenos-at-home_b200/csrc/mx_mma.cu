@@ -1047,7 +1047,7 @@ jl_status mx_project(const PassCtx& c, const MxProj& p, int epi, int use_head, c
     (void)norm;  // inputs arrive normalised; see launch_rmsnorm
     const int items = mcap * p.S * (STAGE_K / 32);
     JL_TRY(launch_pdl(k_mx_pieces, dim3((items + 7) / 8), dim3(256), 0, c.stream,
-                      (const PassHdr*)m->pass.hdr, use_head, mcap, x, ldx, p.K, p.S, N, m->mx.bimg));
+                      (const PassHdr*)c.pass().hdr, use_head, mcap, x, ldx, p.K, p.S, N, m->mx.bimg));
     MxArgs a = {};
     a.a = p.a;
     a.b = m->mx.bimg;
@@ -1057,7 +1057,7 @@ jl_status mx_project(const PassCtx& c, const MxProj& p, int epi, int use_head, c
     a.N = N;
     a.mcap = mcap;
     mx_shape(N, &a.stages, &a.nbuf, &a.group);
-    a.hdr = m->pass.hdr;
+    a.hdr = c.pass().hdr;
     a.use_head = use_head;
     a.y = y;
     a.ldy = ldy;
@@ -1076,7 +1076,7 @@ jl_status mx_norm_pieces(const PassCtx& c, const float* x, int ldx, const uint16
         return JL_ERR_INVALID_ARG;
     }
     return launch_pdl(k_norm_pieces, dim3(width / 128, mcap), dim3(128), 0, c.stream,
-                      (const PassHdr*)c.m->pass.hdr, mcap, x, ldx, w, width, PIECES * mcap, bout, part);
+                      (const PassHdr*)c.pass().hdr, mcap, x, ldx, w, width, PIECES * mcap, bout, part);
 }
 
 jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxFuse& f, float* y,
@@ -1097,7 +1097,7 @@ jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxF
     a.N = N;
     a.mcap = mcap;
     mx_shape(N, &a.stages, &a.nbuf, &a.group);
-    a.hdr = m->pass.hdr;
+    a.hdr = c.pass().hdr;
     a.use_head = 0;
     a.y = y;
     a.ldy = ldy;
@@ -1118,8 +1118,8 @@ jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxF
         a.qn = f.qn;
         a.kn = f.kn;
         a.rope = (const float2*)m->rope;
-        a.rows = m->pass.row;
-        a.page_table = m->pass.page_table;
+        a.rows = c.pass().row;
+        a.page_table = c.pass().page_table;
         a.kv = kv_view(m, f.layer);
     }
     return launch_gemv(epi, a, m->sms, c.stream);
@@ -1204,7 +1204,7 @@ jl_status mx_head_fused(const PassCtx& c, const MxProj& p, const uint16_t* norm,
         return JL_ERR_INVALID_ARG;
     }
     const int N = ((4 * mcap + 7) / 8) * 8;  // four pieces per row, a multiple of 8 columns
-    JL_TRY(launch_pdl(k_head_pieces, dim3(N / 4), dim3(256), 0, c.stream, m->pass, mcap,
+    JL_TRY(launch_pdl(k_head_pieces, dim3(N / 4), dim3(256), 0, c.stream, c.pass(), mcap,
                       (const float*)m->s.x, m->hidden, norm, N, m->mx.bhead));
     MxArgs a = {};
     a.a = p.a;
@@ -1215,7 +1215,7 @@ jl_status mx_head_fused(const PassCtx& c, const MxProj& p, const uint16_t* norm,
     a.N = N;
     a.mcap = mcap;
     mx_shape(N, &a.stages, &a.nbuf, &a.group);
-    a.hdr = m->pass.hdr;
+    a.hdr = c.pass().hdr;
     a.use_head = 1;
     a.y = logits;
     a.ldy = ldy;
@@ -1224,7 +1224,7 @@ jl_status mx_head_fused(const PassCtx& c, const MxProj& p, const uint16_t* norm,
     a.amax_v = m->mx.amax_v;
     a.amax_i = m->mx.amax_i;
     JL_TRY(launch_gemv(MX_HEAD, a, m->sms, c.stream));
-    return launch_pdl(k_argmax_tiles, dim3(mcap), dim3(256), 0, c.stream, m->pass, p.T,
+    return launch_pdl(k_argmax_tiles, dim3(mcap), dim3(256), 0, c.stream, c.pass(), p.T,
                       (const float*)m->mx.amax_v, (const int*)m->mx.amax_i);
 }
 

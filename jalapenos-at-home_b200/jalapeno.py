@@ -36,7 +36,8 @@ EXPORTS = (
     "jl_cache_truncate", "jl_predict", "jl_next_token", "jl_hidden", "jl_generate",
     "jl_schedule_fixed", "jl_schedule_adaptive", "jl_spec_options_default",
     "jl_generate_speculative", "jl_time_pass", "jl_time_projection", "jl_project",
-    "jl_project_noalloc", "jl_pass_kernels", "jl_time_pass_draft",
+    "jl_project_noalloc", "jl_pass_kernels", "jl_time_pass_draft", "jl_generate_batch",
+    "jl_generate_speculative_batch",
 )
 PROJ_QKV, PROJ_O, PROJ_GATE_UP, PROJ_DOWN, PROJ_HEAD = 0, 1, 2, 3, 4
 
@@ -101,6 +102,11 @@ class SpecResult(ctypes.Structure):
                 ("verify_ms", ctypes.c_double)]
 
 
+class BatchStats(ctypes.Structure):
+    _fields_ = [("prefill_ms", ctypes.c_double), ("decode_ms", ctypes.c_double), ("rounds", ctypes.c_size_t),
+                ("target_passes", ctypes.c_size_t), ("draft_passes", ctypes.c_size_t)]
+
+
 def _load():
     if not LIB_PATH.exists():
         raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {HERE}` "
@@ -137,6 +143,11 @@ def _load():
         "jl_spec_options_default": ([ctypes.POINTER(SpecOptions)], None),
         "jl_generate_speculative": ([vp, vp, u32p, sz, sz, ctypes.POINTER(Schedule),
                                      ctypes.POINTER(SpecOptions), ctypes.POINTER(SpecResult)], ctypes.c_int),
+        "jl_generate_batch": ([vp, sz, ctypes.POINTER(u32p), ctypes.POINTER(sz), sz, ctypes.POINTER(SpecResult),
+                               ctypes.POINTER(BatchStats)], ctypes.c_int),
+        "jl_generate_speculative_batch": ([vp, vp, sz, ctypes.POINTER(u32p), ctypes.POINTER(sz), sz,
+                                           ctypes.POINTER(Schedule), ctypes.POINTER(SpecOptions),
+                                           ctypes.POINTER(SpecResult), ctypes.POINTER(BatchStats)], ctypes.c_int),
         "jl_time_pass": ([vp, u32p, sz, sz, sz, ctypes.POINTER(ctypes.c_double),
                           ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
         "jl_time_projection": ([vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -495,3 +506,83 @@ def generate_speculative(target: Model, draft: Model, prompt, count: int, gamma:
                          **kw) -> SpeculativeResult:
     """``generate_speculative`` (speculative.rs:32-40)."""
     return generate_scheduled(target, draft, prompt, count, DraftSchedule.fixed(gamma), **kw)
+
+
+@dataclasses.dataclass
+class BatchResult:
+    """A batched call: one result per sequence, and the batch's own counters."""
+    results: list        # SpeculativeResult per sequence (greedy: tokens and verify passes)
+    prefill_ms: float
+    decode_ms: float
+    rounds: int
+    target_passes: int   # passes of up to 16 rows
+    draft_passes: int
+
+
+def _batch_inputs(prompts, count, rounds_cap=0):
+    ps = [u32(p) for p in prompts]
+    ptrs = (ctypes.POINTER(ctypes.c_uint32) * len(ps))(*[_p(p, ctypes.c_uint32) for p in ps])
+    lens = (ctypes.c_size_t * len(ps))(*[len(p) for p in ps])
+    outs = [np.zeros(len(p) + count + 1, np.uint32) for p in ps]
+    rounds = [(RoundStats * rounds_cap)() for _ in ps] if rounds_cap else []
+    res = (SpecResult * len(ps))()
+    for i, o in enumerate(outs):
+        res[i].tokens = _p(o, ctypes.c_uint32)
+        res[i].tokens_cap = len(o)
+        if rounds_cap:
+            res[i].rounds_out = rounds[i]
+            res[i].rounds_cap = rounds_cap
+    return ps, ptrs, lens, outs, rounds, res
+
+
+def _batch_result(outs, rounds, res, stats) -> BatchResult:
+    seqs = []
+    for i, o in enumerate(outs):
+        r = res[i]
+        n = min(r.rounds, r.rounds_cap)
+        seqs.append(SpeculativeResult(
+            tokens=[int(x) for x in o[: r.n_tokens]], drafted=r.drafted, accepted=r.accepted, rounds=r.rounds,
+            prefill=PhaseStats(r.prefill_passes, r.prefill_ms), draft=PhaseStats(r.draft_passes, r.draft_ms),
+            verify=PhaseStats(r.verify_passes, r.verify_ms),
+            round_stats=[(x.gamma, x.drafted, x.accepted, x.next_gamma) for x in rounds[i][:n]] if rounds else [],
+            decode_ms=r.decode_ms))
+    return BatchResult(seqs, stats.prefill_ms, stats.decode_ms, stats.rounds, stats.target_passes,
+                       stats.draft_passes)
+
+
+def generate_batch(model: Model, prompts, count: int) -> BatchResult:
+    """Greedy ``generate`` (model.rs:268-285) of independent sequences in
+    lockstep rounds: each sequence's tokens equal ``model.generate`` on it."""
+    ps, ptrs, lens, outs, rounds, res = _batch_inputs(prompts, count)
+    stats = BatchStats()
+    check(lib.jl_generate_batch(model._h, len(ps), ptrs, lens, count, res, ctypes.byref(stats)))
+    return _batch_result(outs, rounds, res, stats)
+
+
+def generate_speculative_batch(target: Model, draft: Model, prompts, count: int, schedule,
+                               oracle_streams=None, oracle_p=0.0, oracle_seeds=0) -> BatchResult:
+    """``generate_scheduled`` (speculative.rs:43-143) for each of a batch of
+    sequences in lockstep rounds.  ``schedule``, ``oracle_p`` and
+    ``oracle_seeds`` may be one value for all sequences or one per sequence;
+    ``oracle_streams`` is None or one stream (or None) per sequence."""
+    B = len(prompts)
+    per = lambda v: list(v) if isinstance(v, (list, tuple)) else [v] * B
+    scheds = per(schedule)
+    ps, ptrs, lens, outs, rounds, res = _batch_inputs(prompts, count, rounds_cap=count + 2)
+    sc = (Schedule * B)(*[(s._s if isinstance(s, DraftSchedule) else DraftSchedule.fixed(s)._s) for s in scheds])
+    opts = (SpecOptions * B)()
+    keep = []
+    streams = oracle_streams if oracle_streams is not None else [None] * B
+    for i, (st, p, seed) in enumerate(zip(streams, per(oracle_p), per(oracle_seeds))):
+        lib.jl_spec_options_default(ctypes.byref(opts[i]))
+        if st is not None:
+            a = u32(st)
+            keep.append(a)
+            opts[i].oracle_stream = _p(a, ctypes.c_uint32)
+            opts[i].oracle_len = len(a)
+            opts[i].oracle_p = p
+            opts[i].oracle_seed = seed
+    stats = BatchStats()
+    check(lib.jl_generate_speculative_batch(target._h, draft._h, B, ptrs, lens, count, sc, opts, res,
+                                            ctypes.byref(stats)))
+    return _batch_result(outs, rounds, res, stats)
