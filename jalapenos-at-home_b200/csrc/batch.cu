@@ -27,7 +27,7 @@ constexpr int BATCH_CHUNKS = 32;  // chunks of one batched pass: 512 rows
 struct BatchPass {
     PassHdr* hdr = nullptr;                // [chunks]
     RowDesc* row = nullptr;                // [chunks * SMALL_M]
-    int32_t* ident = nullptr;              // [SMALL_M]: 0, 1, ..., 15
+    int32_t* ident = nullptr;              // [chunks * SMALL_M]: each chunk's rows 0, 1, ..., 15
     const int32_t** page_table = nullptr;  // [MAX_SEQS]: sequence b's cache
     uint32_t* out_ids = nullptr;           // [chunks * SMALL_M]
     int chunks = 0;
@@ -233,10 +233,11 @@ jl_status alloc_pass(BatchGraph* g, BatchPass* p, int rows) {
     JL_TRY(dev_alloc(g, &p->row, (size_t)p->chunks * SMALL_M));
     JL_TRY(dev_alloc(g, &p->out_ids, (size_t)p->chunks * SMALL_M));
     int32_t* ident = nullptr;
-    JL_TRY(dev_alloc(g, &ident, SMALL_M));
-    int32_t h[SMALL_M];
-    for (int j = 0; j < SMALL_M; ++j) h[j] = j;
-    JL_CUDA(cudaMemcpy(ident, h, sizeof(h), cudaMemcpyHostToDevice));
+    const size_t n = (size_t)p->chunks * SMALL_M;
+    JL_TRY(dev_alloc(g, &ident, n));
+    std::vector<int32_t> h(n);
+    for (size_t j = 0; j < n; ++j) h[j] = (int32_t)(j % SMALL_M);
+    JL_CUDA(cudaMemcpy(ident, h.data(), n * sizeof(int32_t), cudaMemcpyHostToDevice));
     p->ident = ident;
     const int32_t** pt = nullptr;
     JL_TRY(dev_alloc(g, &pt, MAX_SEQS));
@@ -247,13 +248,34 @@ jl_status alloc_pass(BatchGraph* g, BatchPass* p, int rows) {
 // Rows of chunk c of a pass over at most `rows` rows.
 int chunk_cap(int rows, int c) { return std::min(SMALL_M, rows - c * SMALL_M); }
 
-// The chunk passes of `m` over at most `rows` rows, each behind the IF node
-// of its handle, inside `graph` after `dep`; returns the last node.
+// Whether `m` runs a pass over `rows` rows as one multi-chunk pass.
+bool multi_chunk(const jl_model* m, int rows) {
+    const int chunks = (rows + SMALL_M - 1) / SMALL_M;
+    return chunks > 1 && m->mx.fused && m->bf_head.a && chunks <= m->mx.chunks;
+}
+
+// The passes of `m` over at most `rows` rows inside `graph` after `dep`:
+// one multi-chunk pass behind the IF node of h[0] (open when chunk 0 has
+// rows), or one pass per 16-row chunk, each behind the IF node of its
+// handle.  Returns the last node.
 jl_status add_chunk_passes(cudaGraph_t graph, cudaStream_t st, cudaGraphNode_t* dep, jl_model* m,
                            const BatchPass& p, int rows, bool draft, int splits,
                            const std::vector<cudaGraphConditionalHandle>& h, cudaGraphNode_t* last) {
     cudaGraphNode_t prev = dep ? *dep : nullptr;
     const int chunks = (rows + SMALL_M - 1) / SMALL_M;
+    if (multi_chunk(m, rows)) {
+        cudaGraphNode_t ifn;
+        cudaGraph_t ifb;
+        JL_TRY(add_conditional(graph, prev ? &prev : nullptr, prev ? 1 : 0, h[0], cudaGraphCondTypeIf, &ifn, &ifb));
+        JL_TRY(capture_into(ifb, st, nullptr, [&]() -> jl_status {
+            PassCtx ctx{m, st, chunks * SMALL_M, chunks * SMALL_M, draft, splits};
+            ctx.chunks = chunks;
+            ctx.view = chunk_view(p, 0);
+            return record_pass_ctx(ctx, m->layers, true);
+        }, nullptr));
+        *last = ifn;
+        return JL_OK;
+    }
     for (int c = 0; c < chunks; ++c) {
         cudaGraphNode_t ifn;
         cudaGraph_t ifb;
@@ -275,6 +297,11 @@ ChunkHandles to_struct(const std::vector<cudaGraphConditionalHandle>& v) {
     h.n = (int)v.size();
     for (size_t i = 0; i < v.size() && i < (size_t)BATCH_CHUNKS; ++i) h.h[i] = v[i];
     return h;
+}
+
+// IF handles of a pass site over `rows` rows of `m`: one per chunk pass.
+int site_handles(const jl_model* m, int rows) {
+    return multi_chunk(m, rows) ? 1 : (rows + SMALL_M - 1) / SMALL_M;
 }
 
 jl_status make_handles(cudaGraph_t graph, int n, std::vector<cudaGraphConditionalHandle>* out) {
@@ -317,10 +344,10 @@ jl_status build_batch_spec(BatchGraph* g) {
 
     const int vrows = B * (G + 1), crows = 2 * B;
     std::vector<std::vector<cudaGraphConditionalHandle>> h_dc(G + 1);
-    for (int i = 1; i < G; ++i) JL_TRY(make_handles(body, (B + SMALL_M - 1) / SMALL_M, &h_dc[i]));
+    for (int i = 1; i < G; ++i) JL_TRY(make_handles(body, site_handles(D, B), &h_dc[i]));
     std::vector<cudaGraphConditionalHandle> h_vc, h_cc;
-    JL_TRY(make_handles(body, (vrows + SMALL_M - 1) / SMALL_M, &h_vc));
-    JL_TRY(make_handles(body, (crows + SMALL_M - 1) / SMALL_M, &h_cc));
+    JL_TRY(make_handles(body, site_handles(T, vrows), &h_vc));
+    JL_TRY(make_handles(body, site_handles(D, crows), &h_cc));
 
     const ChunkHandles first = G > 1 ? to_struct(h_dc[1]) : ChunkHandles{};
     cudaGraphNode_t prev;
@@ -353,7 +380,7 @@ jl_status build_batch_greedy(BatchGraph* g) {
     cudaGraph_t body;
     JL_TRY(add_conditional(top, nullptr, 0, h_loop, cudaGraphCondTypeWhile, &loop_node, &body));
     std::vector<cudaGraphConditionalHandle> h_c;
-    JL_TRY(make_handles(body, (g->B + SMALL_M - 1) / SMALL_M, &h_c));
+    JL_TRY(make_handles(body, site_handles(T, g->B), &h_c));
     const ChunkHandles ch = to_struct(h_c);
     cudaGraphNode_t prev;
     JL_TRY(add_kernel(body, st, nullptr, [&] { k_batch_greedy_begin<<<1, 1, 0, st>>>(a, h_loop, ch); }, &prev));

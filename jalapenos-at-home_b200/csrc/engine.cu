@@ -263,6 +263,44 @@ jl_status host_pass(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int
     return record_pass_ctx(ctx, layers, head_rows > 0);
 }
 
+// Whether `m` runs passes over more than 16 rows as multi-chunk passes.
+bool multi_chunk_model(const jl_model* m) { return m->mx.fused && m->bf_head.a && m->mx.chunks > 1; }
+
+// A pass of 17..16*chunks rows from the host as one multi-chunk pass
+// (recorded directly on m->stream).  Predicted rows: every row (`all`), or
+// the last one; their ids land in out_ids at 16 * chunk + index.
+jl_status host_pass_multi(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool all, bool head) {
+    const int C = (int)((n + SMALL_M - 1) / SMALL_M);
+    StageSlot* sl = nullptr;
+    JL_TRY(stage_begin(m, &sl));
+    const int last = (int)((n - 1) / SMALL_M);
+    for (int k = 0; k < C; ++k) {
+        const int rows = (int)std::min<size_t>(SMALL_M, n - (size_t)k * SMALL_M);
+        PassHdr& h = sl->hdr[k];
+        h.rows = rows;
+        h.head_rows = !head ? 0 : all ? rows : (k == last ? 1 : 0);
+        h.pad0 = h.pad1 = 0;
+        for (int j = 0; j < SMALL_M; ++j) sl->head_row[k * SMALL_M + j] = all ? j : rows - 1;
+    }
+    for (size_t i = 0; i < n; ++i) {
+        sl->row[i].token = ids[i];
+        sl->row[i].seq = 0;
+        sl->row[i].pos = (int32_t)(c->len + i);
+        sl->row[i].pad = 0;
+    }
+    sl->page_table[0] = c->d_pages;
+    cudaStream_t st = m->stream;
+    JL_CUDA(cudaMemcpyAsync(m->pass.hdr, sl->hdr, C * sizeof(PassHdr), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(m->pass.row, sl->row, n * sizeof(RowDesc), cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(m->pass.head_row, sl->head_row, (size_t)C * SMALL_M * sizeof(int32_t),
+                            cudaMemcpyHostToDevice, st));
+    JL_CUDA(cudaMemcpyAsync(m->pass.page_table, sl->page_table, sizeof(int32_t*), cudaMemcpyHostToDevice, st));
+    JL_TRY(stage_end(m, sl, st));
+    PassCtx ctx{m, st, C * SMALL_M, C * SMALL_M, false, att_splits_for(m, c->len + n)};
+    ctx.chunks = C;
+    return record_pass_ctx(ctx, m->layers, head);
+}
+
 }  // namespace
 
 // The decode pass with every MXFP4 projection fused with its neighbours:
@@ -274,6 +312,8 @@ jl_status record_fused_pass(const PassCtx& c, int layers) {
     const jl_model* m = c.m;
     const MxBuffers& B = m->mx;
     const int h = m->hidden, tiles = h / 128;
+    const bool multi = c.chunks > 1;  // chunk strides of the piece images
+    const size_t sx = multi ? B.sx : 0, sattn = multi ? B.sattn : 0, sact = multi ? B.sact : 0;
     JL_TRY(launch_embed(c));
     if (layers > 0) JL_TRY(mx_norm_pieces(c, m->s.x, h, m->lw[0].in_ln, h, B.bx, B.part));
     for (int l = 0; l < layers; ++l) {
@@ -286,6 +326,7 @@ jl_status record_fused_pass(const PassCtx& c, int layers) {
         qkv.layer = l;
         qkv.qn = L.q_norm;
         qkv.kn = L.k_norm;
+        qkv.cs_b = sx;
         JL_TRY(mx_project_fused(c, L.mx_qkv, MXE_QKV, qkv, m->s.qkv, qkv_ld(m)));
         JL_TRY(launch_attention(c, l, true));  // lib.rs:401-441
         MxFuse o;  // lib.rs:444-449 + residual, then post_attention_layernorm
@@ -293,6 +334,8 @@ jl_status record_fused_pass(const PassCtx& c, int layers) {
         o.bout = B.bx;
         o.part_out = B.part;
         o.next_w = L.post_ln;
+        o.cs_b = sattn;
+        o.cs_bout = sx;
         JL_TRY(mx_project_fused(c, L.mx_o, MXE_ADD, o, m->s.x, h));
         MxFuse gu;  // lib.rs:459-463
         gu.b = B.bx;
@@ -300,9 +343,13 @@ jl_status record_fused_pass(const PassCtx& c, int layers) {
         gu.part_tiles = tiles;
         gu.norm_width = h;
         gu.bout = B.bact;
+        gu.cs_b = sx;
+        gu.cs_bout = sact;
         JL_TRY(mx_project_fused(c, L.mx_gateup, MXE_SWIGLU, gu, nullptr, m->inter));
         MxFuse dn;  // lib.rs:464-467 + residual, then the next input_layernorm
         dn.b = B.bact;
+        dn.cs_b = sact;
+        dn.cs_bout = sx;
         if (l + 1 < layers) {
             dn.bout = B.bx;
             dn.part_out = B.part;
@@ -315,11 +362,15 @@ jl_status record_fused_pass(const PassCtx& c, int layers) {
 
 jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head) {
     const jl_model* m = c.m;
-    const bool dec = c.draft && m->dec_ok && c.rows_cap <= 2;
-    if (dec || (m->mx.fused && c.rows_cap <= mx_max_tokens())) {
+    const bool dec = c.draft && m->dec_ok && c.rows_cap <= 2 && c.chunks == 1;
+    if (c.chunks > 1 && !(m->mx.fused && m->bf_head.a)) {
+        set_error("multi-chunk passes need the fused tensor-core pass and output table");
+        return JL_ERR_INVALID_ARG;
+    }
+    if (dec || (m->mx.fused && (c.rows_cap <= mx_max_tokens() || c.chunks > 1))) {
         if (dec) JL_TRY(record_dec_pass(c, layers));
         else JL_TRY(record_fused_pass(c, layers));
-        if (with_head && m->bf_head.a && c.head_cap <= mx_max_tokens())  // model.rs:220-239
+        if (with_head && m->bf_head.a && (c.head_cap <= mx_max_tokens() || c.chunks > 1))  // model.rs:220-239
             return mx_head_fused(c, m->bf_head, m->final_norm, m->s.logits, m->vocab);
         if (with_head) {
             JL_TRY(launch_rmsnorm(c, m->s.x, m->final_norm, m->s.xh, true));  // model.rs:228
@@ -364,7 +415,12 @@ jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool 
     // long-prompt kernels at every prompt length (B200, Qwen3-8B MXFP4: 2048
     // tokens 0.86 s against 1.13 s), so every prompt takes it; otherwise
     // prompts over 256 tokens use the long-prompt kernels.
-    const size_t chunk = n <= 256 || m->mx.fused
+    // A model with multi-chunk passes takes up to 16 * chunks rows at a time:
+    // every kernel then runs all chunks in one launch, so the weights stream
+    // from HBM about once per pass instead of once per 16 rows.
+    const bool multi = multi_chunk_model(m);
+    const size_t chunk = multi ? (size_t)SMALL_M * m->mx.chunks
+                         : n <= 256 || m->mx.fused
                              ? (size_t)SMALL_M
                              : (all ? std::min<size_t>(m->max_rows, HEAD_CAP) : (size_t)m->max_rows);
     size_t done = 0;
@@ -372,13 +428,20 @@ jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool 
         const size_t take = std::min(chunk, n - done);
         const bool last = done + take == n;
         const int head_rows = all ? (int)take : (last ? 1 : 0);
-        JL_TRY(host_pass(m, c, ids + done, take, head_rows, all, m->layers, draft_step));
+        // where the predicted rows' ids and logits land
+        size_t out_at = 0;
+        if (multi && take > (size_t)SMALL_M) {
+            JL_TRY(host_pass_multi(m, c, ids + done, take, all, head_rows > 0));
+            if (!all) out_at = (take - 1) / SMALL_M * SMALL_M;
+        } else {
+            JL_TRY(host_pass(m, c, ids + done, take, head_rows, all, m->layers, draft_step));
+        }
         if (head_rows) {
             const size_t first = all ? done : 0;
-            JL_CUDA(cudaMemcpyAsync(m->host_out, m->pass.out_ids, head_rows * sizeof(uint32_t),
+            JL_CUDA(cudaMemcpyAsync(m->host_out, m->pass.out_ids + out_at, head_rows * sizeof(uint32_t),
                                     cudaMemcpyDeviceToHost, m->stream));
             if (out_logits)
-                JL_CUDA(cudaMemcpyAsync(out_logits + first * m->vocab, m->s.logits,
+                JL_CUDA(cudaMemcpyAsync(out_logits + first * m->vocab, m->s.logits + out_at * m->vocab,
                                         (size_t)head_rows * m->vocab * sizeof(float),
                                         cudaMemcpyDeviceToHost, m->stream));
             JL_CUDA(cudaStreamSynchronize(m->stream));

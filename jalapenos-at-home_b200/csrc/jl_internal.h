@@ -35,6 +35,7 @@ constexpr int SMALL_M = 16;      // passes up to this many rows use the decode k
 constexpr int ATT_WIN = 2;       // KV pages per decode-attention window (one CTA per window over long contexts)
 constexpr int ATT_PART = 4 + HEAD;  // floats of one window's partial: max, sum, 2 pad, 128 outputs
 constexpr int MAX_SEQS = 64;     // sequences one pass may touch
+constexpr int MAX_CHUNKS = 32;   // 16-row chunks of one multi-chunk pass (fused decode kernels)
 constexpr int MAX_GAMMA = 16;    // largest draft length of the device-resident loop
 
 // ---- errors --------------------------------------------------------------
@@ -129,6 +130,11 @@ struct MxBuffers {
     uint8_t* bhead = nullptr;  // [hidden / 64][64 * 128]
     float* amax_v = nullptr;   // [T][MX_PART_STRIDE]
     int* amax_i = nullptr;
+    // Multi-chunk passes: `chunks` copies of every buffer above from bx on,
+    // chunk c's at c * (its stride): bytes for the piece images, elements for
+    // part, amax_v and amax_i.
+    int chunks = 1;
+    size_t sx = 0, sattn = 0, sact = 0, spart = 0, shead = 0, samax = 0;
 };
 
 struct LayerW {
@@ -313,8 +319,14 @@ struct PassCtx {
     int head_cap;   // predicted rows the pass may hold
     bool draft = false;  // a speculative loop's draft step (may take the CUDA-core path)
     int att_splits = 1;  // decode attention: window CTAs per row in the launch grid (att_splits_for)
+    // A multi-chunk pass (fused decode kernels only): `chunks` > 1 chunks of
+    // 16 rows, rows_cap = head_cap = 16 * chunks.  Chunk c has its own header
+    // (hdr[c]); its rows are row[16c ..], its predicted rows are listed in
+    // head_row[16c ..] as indices within the chunk and predicted into
+    // out_ids[16c ..].  Each kernel runs every chunk in one launch.
+    int chunks = 1;
     // The rows this pass reads: by default the model's own pass buffer; a
-    // batched loop points each 16-row chunk pass at its slice of a larger one.
+    // batched loop points each pass at its own buffers.
     PassBuf view{};
     const PassBuf& pass() const { return view.hdr ? view : m->pass; }
 };
@@ -355,6 +367,7 @@ struct MxFuse {
     int layer = 0;                     // q|k|v: cache layer and QK-norm weights
     const uint16_t* qn = nullptr;
     const uint16_t* kn = nullptr;
+    size_t cs_b = 0, cs_bout = 0;      // multi-chunk passes: chunk strides of b and bout (bytes)
 };
 jl_status mx_configure();
 int mx_max_tokens();

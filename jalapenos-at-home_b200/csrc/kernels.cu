@@ -340,12 +340,12 @@ __global__ void __launch_bounds__(256) k_gemm(const PassHdr* __restrict__ hdr, i
 
 // ---------------------------------------------------------------------------
 
-__global__ void k_embed(PassBuf pb, Mat e, float* __restrict__ x, int hidden) {
+__global__ void k_embed(PassBuf pb, Mat e, float* __restrict__ x, int hidden, int chunked) {
     // lib.rs:213-235, model.rs:167-170
     ptx::grid_dependency_wait();  // PDL: the previous kernel's writes are visible past here
     ptx::launch_dependents();
     const int row = blockIdx.x;
-    if (row >= pb.hdr->rows) return;
+    if (chunked ? row % SMALL_M >= pb.hdr[row / SMALL_M].rows : row >= pb.hdr->rows) return;
     uint32_t tok = pb.row[row].token;
     if (tok >= (uint32_t)e.rows) tok = 0;  // ids are validated on the host
     float* out = x + (size_t)row * hidden;
@@ -598,6 +598,10 @@ __device__ __forceinline__ NormRope norm_rope_args(const uint16_t* gw, const flo
 struct AttnSplit {
     float* ws;
     int* cnt;
+    // a multi-chunk pass: row r is row r % 16 of chunk r / 16, whose header
+    // is hdr[r / 16] and whose attention pieces start at bout + chunk * cs_bout
+    int chunked;
+    size_t cs_bout;
 };
 
 // QK-RMSNorm and RoPE of one head held as dims (l, l+32, l+64, l+96) by lane
@@ -652,8 +656,10 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
     // and the cache rows before this row's position by earlier passes: the
     // first window of pages is copied before waiting for the q|k|v kernel,
     // which writes only this row's own K/V (fetched again after the wait).
-    const int rows = pb.hdr->rows;
-    bool valid = row < rows;
+    const int crow = sp.chunked ? row % SMALL_M : row;  // row within its chunk
+    const int rows = pb.hdr[sp.chunked ? row / SMALL_M : 0].rows;
+    if (bout && sp.chunked) bout += (row / SMALL_M) * sp.cs_bout;
+    bool valid = crow < rows;
     RowDesc rd = {};
     if (valid) {
         rd = pb.row[row];
@@ -713,22 +719,42 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
             if (warp == row && kgood && zs == nsplit - 1) kpage = pt[rj.pos / PAGE];
         }
     }
-    // Not RAW: the page of the position this warp re-fetches after the wait
-    // (position pos - row + warp: this pass's rows of the sequence)
+    // Not RAW: this pass wrote the K/V of the sequence's rows just before
+    // this one (`back` of them, at consecutive positions) and of this row;
+    // the page of the position this warp re-fetches after the wait
+    // (position pos - back + warp).
+    int back = 0;
+    if (!RAW && valid) {
+        for (int base = 0; base < row; base += 32) {
+            const int r = row - 1 - base - lane;
+            bool same = false;
+            if (r >= 0) {
+                const RowDesc q = pb.row[r];
+                same = q.seq == rd.seq && q.pos == rd.pos - (row - r);
+            }
+            const unsigned stop = __ballot_sync(0xffffffffu, !same);
+            if (stop) {
+                back = base + __ffs(stop) - 1;
+                break;
+            }
+            back = base + 32;
+        }
+        back = min(back, row);
+    }
     int own_p = -1, own_pg = -1;
-    if (!RAW && valid && warp <= row && rd.pos - row + warp >= 0) {
-        own_p = rd.pos - row + warp;
+    if (!RAW && valid && warp <= back && rd.pos - back + warp >= 0) {
+        own_p = rd.pos - back + warp;
         own_pg = pt[own_p / PAGE];
     }
     __syncthreads();  // the barrier is initialised before anyone waits on it
     ptx::grid_dependency_wait();
     ptx::launch_dependents();
-    if (row < rows && !valid && sub == 0) {  // uniform over the CTA
+    if (crow < rows && !valid && sub == 0) {  // uniform over the CTA
         if (threadIdx.x == 0) atomicOr(kv.err, 2);
         *(float4*)(out + (size_t)row * out_ld + h * HEAD + 4 * lane) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (!valid) {
-        if (bout && sub == 0) mx::emit_pieces_smem(qw, HEAD, 4, row, 0, 1, lane, 32, h * HEAD, bN, bout);
+        if (bout && sub == 0) mx::emit_pieces_smem(qw, HEAD, 4, crow, 0, 1, lane, 32, h * HEAD, bN, bout);
         return;
     }
     if (RAW) {
@@ -801,10 +827,10 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
             }
         } else {
         // The q|k|v kernel of this pass wrote this row's K/V and those of the
-        // pass's earlier rows of the sequence (at most `row` positions back):
-        // fetch them again over the early copy.
+        // pass's earlier rows of the sequence (`back` positions back): fetch
+        // them again over the early copy.
             constexpr int RB = HEAD * (F32 ? 4 : 2);  // bytes of one row: 256 or 512
-            const int lo = max(rd.pos - row, w0 * PAGE), hi = min(rd.pos, (w0 + wn) * PAGE - 1);
+            const int lo = max(rd.pos - back, w0 * PAGE), hi = min(rd.pos, (w0 + wn) * PAGE - 1);
             for (int p = lo + warp; p <= hi; p += nw) {
                 const int pg = p == own_p ? own_pg : pt[p / PAGE];
                 if ((unsigned)pg >= (unsigned)kv.pages) continue;  // flagged when the window was copied
@@ -969,7 +995,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
         __syncwarp();  // every lane has finished reading q
         *(float4*)(qw + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
         __syncwarp();
-        mx::emit_pieces_smem(qw, HEAD, 4, row, 1, 1, lane, 32, h * HEAD, bN, bout);
+        mx::emit_pieces_smem(qw, HEAD, 4, crow, 1, 1, lane, 32, h * HEAD, bN, bout);
     }
 }
 
@@ -1182,7 +1208,7 @@ jl_status configure_kernels() {
 
 jl_status launch_embed(const PassCtx& c) {
     return launch_pdl(k_embed, dim3(c.rows_cap), dim3(256), 0, c.stream, c.pass(), c.m->embed, c.m->s.x,
-                      c.m->hidden);
+                      c.m->hidden, c.chunks > 1 ? 1 : 0);
 }
 
 jl_status launch_rmsnorm(const PassCtx& c, const float* x, const uint16_t* w, float* out,
@@ -1214,13 +1240,19 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     dim3 grid(c.m->q_heads, c.rows_cap);
     const int group = c.m->q_heads / c.m->kv_heads;
     uint8_t* bout = pieces ? c.m->mx.battn : nullptr;
-    const int bN = 8 * c.rows_cap;
-    if (c.rows_cap <= SMALL_M && group <= 8) {  // decode passes: a warp per query head
+    const bool chunked = c.chunks > 1;
+    const int bN = 8 * (chunked ? SMALL_M : c.rows_cap);
+    if ((c.rows_cap <= SMALL_M || chunked) && group <= 8) {  // decode passes: a warp per query head
         const int split = att_split(group);
-        const dim3 g2(c.m->kv_heads, c.rows_cap, att_grid_splits(c)), blk(32 * group * split);
+        // the split workspace holds SMALL_M rows x att_smax windows: a pass
+        // over more rows takes fewer window CTAs per row (a row whose context
+        // spans more windows than the grid has is done by one CTA)
+        int z = att_grid_splits(c);
+        while (z > 1 && (size_t)c.rows_cap * z > (size_t)SMALL_M * c.m->att_smax) z >>= 1;
+        const dim3 g2(c.m->kv_heads, c.rows_cap, z), blk(32 * group * split);
         const int qw = c.m->q_heads * HEAD;
         const AttnRaw none{};
-        const AttnSplit sp{c.m->att_ws, c.m->att_cnt};
+        const AttnSplit sp{c.m->att_ws, c.m->att_cnt, chunked ? 1 : 0, chunked ? c.m->mx.sattn : 0};
         if (c.m->kv.dtype == JL_KV_F32)
             return launch_pdl(k_attn_decode<1, 0>, g2, blk, att_smem(1), c.stream, c.pass(),
                               (const float*)c.m->s.qkv, qkv_ld(c.m), group, split, kv_view(c.m, layer),
@@ -1280,7 +1312,7 @@ jl_status launch_attention_raw(const PassCtx& c, int layer, const uint16_t* qn, 
     const int split = att_split(group);
     const dim3 g2(m->kv_heads, c.rows_cap, att_grid_splits(c)), blk(32 * group * split);
     const int qw = m->q_heads * HEAD;
-    const AttnSplit sp{m->att_ws, m->att_cnt};
+    const AttnSplit sp{m->att_ws, m->att_cnt, 0, 0};
     AttnRaw raw;
     raw.qn = qn;
     raw.kn = kn;

@@ -98,17 +98,19 @@ jl_status finish_model(jl_model* m, const jl_model_options& o) {
     for (size_t i = 0; i < m->kv.pages; ++i) m->kv.free_list[i] = (int32_t)(m->kv.pages - 1 - i);
     // decode attention over long contexts: a window CTA's partial sums for
     // every window a sequence of the pool can span
-    m->att_smax = (int)std::max<size_t>(1, (m->kv.pages + ATT_WIN - 1) / ATT_WIN);
+    // (no more than the context limit needs)
+    const size_t seq_pages = std::min(m->kv.pages, ((size_t)m->max_positions + 2 * MAX_GAMMA + PAGE - 1) / PAGE);
+    m->att_smax = (int)std::max<size_t>(1, (seq_pages + ATT_WIN - 1) / ATT_WIN);
     {
         const size_t group = (size_t)m->q_heads / m->kv_heads;
         const size_t floats = (size_t)m->kv_heads * SMALL_M * m->att_smax * group * ATT_PART;
         if (cudaMalloc(&m->att_ws, floats * sizeof(float)) != cudaSuccess ||
-            cudaMalloc(&m->att_cnt, (size_t)m->kv_heads * SMALL_M * sizeof(int)) != cudaSuccess) {
+            cudaMalloc(&m->att_cnt, (size_t)m->kv_heads * SMALL_M * MAX_CHUNKS * sizeof(int)) != cudaSuccess) {
             cudaGetLastError();
             set_error("cannot allocate the attention split workspace");
             return JL_ERR_OOM;
         }
-        JL_CUDA(cudaMemset(m->att_cnt, 0, (size_t)m->kv_heads * SMALL_M * sizeof(int)));
+        JL_CUDA(cudaMemset(m->att_cnt, 0, (size_t)m->kv_heads * SMALL_M * MAX_CHUNKS * sizeof(int)));
     }
     // scratch
     const int R = m->max_rows = o.max_pass_rows ? (int)o.max_pass_rows : 4096;
@@ -121,7 +123,7 @@ jl_status finish_model(jl_model* m, const jl_model_options& o) {
     const size_t off_act = sp.take((size_t)R * m->inter * 4);
     const size_t off_xh = sp.take((size_t)R * H * 4);
     const size_t off_logits = sp.take((size_t)R * m->vocab * 4);
-    const size_t off_hdr = sp.take(sizeof(PassHdr));
+    const size_t off_hdr = sp.take(MAX_CHUNKS * sizeof(PassHdr));
     const size_t off_row = sp.take((size_t)R * sizeof(RowDesc));
     const size_t off_head = sp.take((size_t)R * sizeof(int32_t));
     const size_t off_pt = sp.take((size_t)MAX_SEQS * sizeof(int32_t*));
@@ -149,7 +151,7 @@ jl_status finish_model(jl_model* m, const jl_model_options& o) {
     m->counters = (int*)(b + off_cnt);
     // pinned staging for host-driven passes
     for (StageSlot& sl : m->stage) {
-        JL_CUDA(cudaMallocHost(&sl.hdr, sizeof(PassHdr)));
+        JL_CUDA(cudaMallocHost(&sl.hdr, MAX_CHUNKS * sizeof(PassHdr)));
         JL_CUDA(cudaMallocHost(&sl.row, (size_t)R * sizeof(RowDesc)));
         JL_CUDA(cudaMallocHost(&sl.head_row, (size_t)R * sizeof(int32_t)));
         JL_CUDA(cudaMallocHost(&sl.page_table, (size_t)MAX_SEQS * sizeof(int32_t*)));
@@ -254,18 +256,28 @@ jl_status build_mx(jl_model* m) {
     const size_t off_b = sp.take((size_t)maxS * img_stage);
     const size_t off_ws = sp.take(ws_floats * sizeof(float));
     const size_t off_t = sp.take((size_t)maxT * sizeof(int));
+    // fused-pass buffers: one copy per chunk a multi-chunk pass may hold
+    const int C = fused ? std::max(1, std::min(MAX_CHUNKS, m->max_rows / SMALL_M)) : 1;
+    MxBuffers& X = m->mx;
+    X.chunks = C;
+    X.sx = (size_t)(m->hidden / 256) * img_stage;
+    X.sattn = (size_t)(QW / 256) * img_stage;
+    X.sact = (size_t)(m->inter / 256) * img_stage;
+    X.spart = (size_t)(m->hidden / 128) * MX_PART_STRIDE;
+    X.shead = (size_t)(m->hidden / 64) * (4 * mx_max_tokens()) * 128;
+    X.samax = head_bf ? (size_t)m->bf_head.T * MX_PART_STRIDE : 0;
     size_t off_fx = 0, off_fa = 0, off_ff = 0, off_fp = 0;
     if (fused) {
-        off_fx = sp.take((size_t)(m->hidden / 256) * img_stage);
-        off_fa = sp.take((size_t)(QW / 256) * img_stage);
-        off_ff = sp.take((size_t)(m->inter / 256) * img_stage);
-        off_fp = sp.take((size_t)(m->hidden / 128) * MX_PART_STRIDE * sizeof(float));
+        off_fx = sp.take(C * X.sx);
+        off_fa = sp.take(C * X.sattn);
+        off_ff = sp.take(C * X.sact);
+        off_fp = sp.take(C * X.spart * sizeof(float));
     }
     size_t off_bh = 0, off_av = 0, off_ai = 0;
     if (head_bf) {
-        off_bh = sp.take((size_t)(m->hidden / 64) * (4 * mx_max_tokens()) * 128);
-        off_av = sp.take((size_t)m->bf_head.T * MX_PART_STRIDE * sizeof(float));
-        off_ai = sp.take((size_t)m->bf_head.T * MX_PART_STRIDE * sizeof(int));
+        off_bh = sp.take(C * X.shead);
+        off_av = sp.take(C * X.samax * sizeof(float));
+        off_ai = sp.take(C * X.samax * sizeof(int));
     }
     if (cudaMalloc(&m->mx.scratch, sp.bytes) != cudaSuccess) {
         cudaGetLastError();

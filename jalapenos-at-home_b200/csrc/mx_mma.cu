@@ -81,11 +81,16 @@ __global__ void __launch_bounds__(256) k_mx_pieces(const PassHdr* __restrict__ h
 __global__ void __launch_bounds__(128) k_norm_pieces(const PassHdr* __restrict__ hdr, int mcap,
                                                      const float* __restrict__ x, int ldx,
                                                      const uint16_t* __restrict__ w, int width, int N,
-                                                     uint8_t* __restrict__ bout, float* __restrict__ part) {
+                                                     uint8_t* __restrict__ bout, float* __restrict__ part,
+                                                     size_t cs_bout, size_t cs_part) {
     __shared__ float red[4];
     ptx::grid_dependency_wait();
     ptx::launch_dependents();
-    const int t = blockIdx.x, m = blockIdx.y;
+    const int t = blockIdx.x, m = blockIdx.y, c = blockIdx.z;  // chunk c of a multi-chunk pass
+    hdr += c;
+    x += (size_t)c * SMALL_M * ldx;
+    bout += c * cs_bout;
+    part += c * cs_part;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int M = min(hdr->rows, mcap);
     const int k = t * 128 + threadIdx.x;
@@ -107,11 +112,15 @@ __global__ void __launch_bounds__(128) k_norm_pieces(const PassHdr* __restrict__
 // rows past the predicted ones are zero.
 __global__ void __launch_bounds__(256) k_head_pieces(PassBuf pb, int head_cap, const float* __restrict__ x,
                                                      int hidden, const uint16_t* __restrict__ w, int N,
-                                                     uint8_t* __restrict__ bimg) {
+                                                     uint8_t* __restrict__ bimg, size_t cs_img) {
     __shared__ float red[32];
     ptx::grid_dependency_wait();
     ptx::launch_dependents();
-    const int r = blockIdx.x;
+    const int r = blockIdx.x, c = blockIdx.y;  // chunk c of a multi-chunk pass
+    pb.hdr += c;
+    pb.head_row += c * SMALL_M;
+    x += (size_t)c * SMALL_M * hidden;
+    bimg += c * cs_img;
     const bool live = r < min(pb.hdr->head_rows, head_cap);
     const float* xr = live ? x + (size_t)pb.head_row[r] * hidden : x;
     float size = 1.f;
@@ -143,12 +152,16 @@ __global__ void __launch_bounds__(256) k_head_pieces(PassBuf pb, int head_cap, c
 // First maximum of each predicted row over the head tiles' partial maxima,
 // in tile order (ties to the lower index, model.rs:288-296).
 __global__ void __launch_bounds__(256) k_argmax_tiles(PassBuf pb, int T, const float* __restrict__ amax_v,
-                                                      const int* __restrict__ amax_i) {
+                                                      const int* __restrict__ amax_i, size_t cs_amax) {
     __shared__ float bv_s[8];
     __shared__ int bi_s[8];
     ptx::grid_dependency_wait();
     ptx::launch_dependents();
-    const int r = blockIdx.x;
+    const int r = blockIdx.x, c = blockIdx.y;  // chunk c of a multi-chunk pass
+    pb.hdr += c;
+    pb.out_ids += c * SMALL_M;
+    amax_v += c * cs_amax;
+    amax_i += c * cs_amax;
     if (r >= pb.hdr->head_rows) return;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
@@ -244,6 +257,10 @@ struct MxArgs {
     // head: each tile's first maximum per row ([T][MX_PART_STRIDE])
     float* amax_v;
     int* amax_i;
+    // Multi-chunk launches (grid y = chunk of MX_MAXTOK rows): chunk c reads
+    // b + c*cs_b and writes bout + c*cs_bout (bytes), part_in/part_out/amax
+    // + c*cs_* (elements); hdr, rows and y advance by one chunk.
+    size_t cs_b, cs_bout, cs_part_in, cs_part_out, cs_amax;
 };
 
 enum : int { MX_STORE = 0, MX_ADD = 1, MX_SWIGLU = 2, MX_QKV = 3, MX_HEAD = 4 };
@@ -320,8 +337,28 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 // or on the row count) and runs the epilogue.  When the cluster has another
 // tile, each leader warp frees the buffer with a 4-byte st.async onto every
 // peer's slot_free barrier.  No thread waits on a remote acknowledgement.
+// The arguments of chunk c of a multi-chunk launch.
+__device__ __forceinline__ MxArgs chunk_args(const MxArgs& a0, int c) {
+    MxArgs a = a0;
+    if (c) {
+        a.b += c * a.cs_b;
+        a.hdr += c;
+        if (a.y) a.y += (size_t)c * MX_MAXTOK * a.ldy;
+        if (a.bout) a.bout += c * a.cs_bout;
+        if (a.part_in) a.part_in += c * a.cs_part_in;
+        if (a.part_out) a.part_out += c * a.cs_part_out;
+        if (a.rows) a.rows += c * MX_MAXTOK;
+        if (a.amax_v) {
+            a.amax_v += c * a.cs_amax;
+            a.amax_i += c * a.cs_amax;
+        }
+    }
+    return a;
+}
+
 template <int EPI, int KIND>
-__global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(MxArgs a) {
+__global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
+    const MxArgs a = chunk_args(a0, blockIdx.y);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     __shared__ uint64_t full[MX_MAXSTAGES], empty[MX_MAXSTAGES], tfull[2], tempty[2];
@@ -922,10 +959,10 @@ jl_status configure_mx() {
 }
 
 template <int EPI, int KIND>
-jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream) {
+jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream, int chunks) {
     const int nc = std::min(a.T, a.ksplit > 1 ? mx_clusters(a.ksplit) : sms);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(nc * a.ksplit);
+    cfg.gridDim = dim3(nc * a.ksplit, chunks);
     cfg.blockDim = dim3(MX_THREADS);
     cfg.dynamicSmemBytes = mx_smem(a.N, KIND, a.mcap, a.ksplit);
     cfg.stream = stream;
@@ -946,17 +983,17 @@ jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream) {
     return JL_OK;
 }
 
-jl_status launch_gemv(int epi, const MxArgs& a, int sms, cudaStream_t stream) {
+jl_status launch_gemv(int epi, const MxArgs& a, int sms, cudaStream_t stream, int chunks = 1) {
     if (a.ksplit < 1 || a.ksplit > MX_MAXCLUSTER) {
         set_error("tensor-core projection: split-K %d outside 1..%d", a.ksplit, MX_MAXCLUSTER);
         return JL_ERR_INVALID_ARG;
     }
     switch (epi) {
-        case MX_ADD: return launch_gemv_t<MX_ADD, KIND_MX>(a, sms, stream);
-        case MX_SWIGLU: return launch_gemv_t<MX_SWIGLU, KIND_MX>(a, sms, stream);
-        case MX_QKV: return launch_gemv_t<MX_QKV, KIND_MX>(a, sms, stream);
-        case MX_HEAD: return launch_gemv_t<MX_HEAD, KIND_BF>(a, sms, stream);
-        default: return launch_gemv_t<MX_STORE, KIND_MX>(a, sms, stream);
+        case MX_ADD: return launch_gemv_t<MX_ADD, KIND_MX>(a, sms, stream, chunks);
+        case MX_SWIGLU: return launch_gemv_t<MX_SWIGLU, KIND_MX>(a, sms, stream, chunks);
+        case MX_QKV: return launch_gemv_t<MX_QKV, KIND_MX>(a, sms, stream, chunks);
+        case MX_HEAD: return launch_gemv_t<MX_HEAD, KIND_BF>(a, sms, stream, chunks);
+        default: return launch_gemv_t<MX_STORE, KIND_MX>(a, sms, stream, chunks);
     }
 }
 
@@ -1068,23 +1105,33 @@ jl_status mx_project(const PassCtx& c, const MxProj& p, int epi, int use_head, c
     return launch_gemv(epi, a, m->sms, c.stream);
 }
 
+// Rows per chunk of a pass on the fused kernels, or 0 when it has none.
+int chunk_rows(const PassCtx& c) {
+    if (c.chunks > 1)
+        return c.chunks <= c.m->mx.chunks && c.rows_cap == c.chunks * MX_MAXTOK ? MX_MAXTOK : 0;
+    return c.rows_cap >= 1 && c.rows_cap <= MX_MAXTOK ? c.rows_cap : 0;
+}
+
 jl_status mx_norm_pieces(const PassCtx& c, const float* x, int ldx, const uint16_t* w, int width,
                          uint8_t* bout, float* part) {
-    const int mcap = c.rows_cap;
-    if (mcap < 1 || mcap > MX_MAXTOK || width % STAGE_K) {
-        set_error("norm pieces take 1..%d rows and a width that is a multiple of %d", MX_MAXTOK, STAGE_K);
+    const int mcap = chunk_rows(c);
+    if (!mcap || width % STAGE_K) {
+        set_error("norm pieces take 1..%d rows (or %d chunks of %d) and a width that is a multiple of %d",
+                  MX_MAXTOK, c.m->mx.chunks, MX_MAXTOK, STAGE_K);
         return JL_ERR_INVALID_ARG;
     }
-    return launch_pdl(k_norm_pieces, dim3(width / 128, mcap), dim3(128), 0, c.stream,
-                      (const PassHdr*)c.pass().hdr, mcap, x, ldx, w, width, PIECES * mcap, bout, part);
+    return launch_pdl(k_norm_pieces, dim3(width / 128, mcap, c.chunks), dim3(128), 0, c.stream,
+                      (const PassHdr*)c.pass().hdr, mcap, x, ldx, w, width, PIECES * mcap, bout, part,
+                      c.m->mx.sx, c.m->mx.spart);
 }
 
 jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxFuse& f, float* y,
                            int ldy) {
     const jl_model* m = c.m;
-    const int mcap = c.rows_cap;
-    if (mcap < 1 || mcap > MX_MAXTOK) {
-        set_error("tensor-core projection takes 1..%d rows per pass, got %d", MX_MAXTOK, mcap);
+    const int mcap = chunk_rows(c);
+    if (!mcap) {
+        set_error("tensor-core projection takes 1..%d rows per pass (or %d chunks of %d), got %d", MX_MAXTOK,
+                  m->mx.chunks, MX_MAXTOK, c.rows_cap);
         return JL_ERR_INVALID_ARG;
     }
     const int N = PIECES * mcap;
@@ -1122,7 +1169,11 @@ jl_status mx_project_fused(const PassCtx& c, const MxProj& p, int epi, const MxF
         a.page_table = c.pass().page_table;
         a.kv = kv_view(m, f.layer);
     }
-    return launch_gemv(epi, a, m->sms, c.stream);
+    a.cs_b = f.cs_b;
+    a.cs_bout = f.cs_bout;
+    a.cs_part_in = m->mx.spart;
+    a.cs_part_out = m->mx.spart;
+    return launch_gemv(epi, a, m->sms, c.stream, c.chunks);
 }
 
 MxScratchPlan mx_scratch_plan(const MxProj& p, int mcap) {
@@ -1198,14 +1249,15 @@ jl_status mx_build_bf16(const Mat& w, uint8_t* dst, MxProj* out, cudaStream_t st
 jl_status mx_head_fused(const PassCtx& c, const MxProj& p, const uint16_t* norm, float* logits,
                         int ldy) {
     const jl_model* m = c.m;
-    const int mcap = c.head_cap;
+    const int mcap = c.chunks > 1 ? chunk_rows(c) : c.head_cap;
     if (mcap < 1 || mcap > MX_MAXTOK || !m->mx.bhead) {
-        set_error("tensor-core output table takes 1..%d rows per pass", MX_MAXTOK);
+        set_error("tensor-core output table takes 1..%d rows per pass (or %d chunks of %d)", MX_MAXTOK,
+                  m->mx.chunks, MX_MAXTOK);
         return JL_ERR_INVALID_ARG;
     }
     const int N = ((4 * mcap + 7) / 8) * 8;  // four pieces per row, a multiple of 8 columns
-    JL_TRY(launch_pdl(k_head_pieces, dim3(N / 4), dim3(256), 0, c.stream, c.pass(), mcap,
-                      (const float*)m->s.x, m->hidden, norm, N, m->mx.bhead));
+    JL_TRY(launch_pdl(k_head_pieces, dim3(N / 4, c.chunks), dim3(256), 0, c.stream, c.pass(), mcap,
+                      (const float*)m->s.x, m->hidden, norm, N, m->mx.bhead, m->mx.shead));
     MxArgs a = {};
     a.a = p.a;
     a.b = m->mx.bhead;
@@ -1223,9 +1275,11 @@ jl_status mx_head_fused(const PassCtx& c, const MxProj& p, const uint16_t* norm,
     a.err = m->counters;
     a.amax_v = m->mx.amax_v;
     a.amax_i = m->mx.amax_i;
-    JL_TRY(launch_gemv(MX_HEAD, a, m->sms, c.stream));
-    return launch_pdl(k_argmax_tiles, dim3(mcap), dim3(256), 0, c.stream, c.pass(), p.T,
-                      (const float*)m->mx.amax_v, (const int*)m->mx.amax_i);
+    a.cs_b = m->mx.shead;
+    a.cs_amax = m->mx.samax;
+    JL_TRY(launch_gemv(MX_HEAD, a, m->sms, c.stream, c.chunks));
+    return launch_pdl(k_argmax_tiles, dim3(mcap, c.chunks), dim3(256), 0, c.stream, c.pass(), p.T,
+                      (const float*)m->mx.amax_v, (const int*)m->mx.amax_i, m->mx.samax);
 }
 
 }  // namespace jl
