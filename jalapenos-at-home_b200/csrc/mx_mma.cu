@@ -261,6 +261,10 @@ struct MxArgs {
     // b + c*cs_b and writes bout + c*cs_bout (bytes), part_in/part_out/amax
     // + c*cs_* (elements); hdr, rows and y advance by one chunk.
     size_t cs_b, cs_bout, cs_part_in, cs_part_out, cs_amax;
+    // TMEM columns between the two accumulator buffers: 64 (0 reads as 64)
+    // in a 256-column allocation, or 256 in a 512-column one (two
+    // accumulators of 128 columns; the launch then keeps one CTA per SM)
+    int acc_step;
 };
 
 enum : int { MX_STORE = 0, MX_ADD = 1, MX_SWIGLU = 2, MX_QKV = 3, MX_HEAD = 4 };
@@ -402,8 +406,10 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
         ptx::mbar_init(&slot_free, 1);  // a peer's expect_tx, then the leader warps' bytes
         ptx::fence_barrier_init();
     }
+    const int acc_step = a.acc_step > 64 ? 256 : 64;
+    const uint32_t tcols = acc_step > 64 ? 512u : (uint32_t)TMEM_COLS;
     if (warp == 1) {
-        ptx::tmem_alloc(&tmem_base_s, TMEM_COLS);
+        ptx::tmem_alloc(&tmem_base_s, tcols);
         ptx::tmem_relinquish();
     }
     ptx::tc_fence_before();
@@ -467,7 +473,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
                     break;
                 }
                 ptx::tc_fence_after();
-                const uint32_t d_tmem = tmem + ACC_COL + buf * 64;
+                const uint32_t d_tmem = tmem + ACC_COL + buf * acc_step;
                 for (int s = s0; s < s1; s += G, ++g) {
                     const int slot = g % ST;
                     if (!ptx::mbar_wait(&full[slot], (g / ST) & 1, WAIT_LIMIT)) {
@@ -570,7 +576,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
             if (!ptx::mbar_wait(&tfull[buf], use & 1, WAIT_LIMIT)) ok = false;
             ptx::tc_fence_after();
             float val[MX_MAXTOK];
-            const uint32_t lanebase = tmem + ((uint32_t)(quarter * 32) << 16) + ACC_COL + buf * 64;
+            const uint32_t lanebase = tmem + ((uint32_t)(quarter * 32) << 16) + ACC_COL + buf * acc_step;
             constexpr int CPR = cols_per_row(KIND), RPL = 32 / CPR;  // rows per 32-column load
 #pragma unroll
             for (int m0 = 0; m0 < MX_MAXTOK; m0 += RPL) {
@@ -820,7 +826,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
         ptx::cluster_arrive();
         ptx::cluster_wait();
     }
-    if (warp == 1) ptx::tmem_dealloc(tmem, TMEM_COLS);
+    if (warp == 1) ptx::tmem_dealloc(tmem, tcols);
     if (!ok && lane == 0) atomicOr(a.err, 4);  // a bounded wait gave up
 }
 }  // namespace
@@ -947,6 +953,10 @@ size_t mx_smem(int N, int kind, int mcap, int ks) {
 }
 
 constexpr int MX_PROBE_SMEM = 120 * 1024;  // more than half an SM: one CTA per SM
+// Dynamic shared memory of a launch whose CTAs allocate all 512 TMEM
+// columns: more than half an SM, so no two CTAs (of one cluster above all,
+// which wait for each other) ever share an SM and its TMEM.
+constexpr size_t MX_ONE_PER_SM = 116 * 1024;
 
 template <int EPI, int KIND>
 jl_status configure_mx() {
@@ -960,11 +970,22 @@ jl_status configure_mx() {
 
 template <int EPI, int KIND>
 jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream, int chunks) {
-    const int nc = std::min(a.T, a.ksplit > 1 ? mx_clusters(a.ksplit) : sms);
+    // One wave of CTAs (one per SM at these shapes): a multi-chunk launch
+    // gives each chunk its share, so a CTA runs several tiles through its
+    // ring instead of each chunk waiting for a wave of its own.
+    const int nc = std::max(1, std::min(a.T, a.ksplit > 1 ? mx_clusters(a.ksplit) : sms) / chunks);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(nc * a.ksplit, chunks);
     cfg.blockDim = dim3(MX_THREADS);
     cfg.dynamicSmemBytes = mx_smem(a.N, KIND, a.mcap, a.ksplit);
+    MxArgs b = a;
+    if (chunks > 1 && a.N > 64) {
+        // several tiles per CTA: two 128-column accumulators, so a tile's
+        // epilogue overlaps the next tile's MMAs
+        b.nbuf = 2;
+        b.acc_step = 256;
+        cfg.dynamicSmemBytes = std::max(cfg.dynamicSmemBytes, MX_ONE_PER_SM);
+    }
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -979,7 +1000,7 @@ jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream, int chunk
     }
     cfg.attrs = attr;
     cfg.numAttrs = n;
-    JL_CUDA(cudaLaunchKernelEx(&cfg, k_mx_gemv<EPI, KIND>, a));
+    JL_CUDA(cudaLaunchKernelEx(&cfg, k_mx_gemv<EPI, KIND>, b));
     return JL_OK;
 }
 
