@@ -60,6 +60,10 @@ def parse():
     ap.add_argument("--profile", action="store_true",
                     help="small run for ncu: one k+1-row target pass and one draft pass "
                          "(Model::time_pass), no timing loop")
+    ap.add_argument("--config5", action="store_true",
+                    help="BASELINE.json configs[4]: per-GPU batches of independent sequences with 4096-token "
+                         "contexts and 256 new tokens (one JSON line per batch size)")
+    ap.add_argument("--batches", default="1,8,32", help="--config5 batch sizes")
     ap.add_argument("--small", action="store_true",
                     help="with --profile: two layers of each model at full width and an 8192-entry "
                          "vocabulary (under 0.5 GB on the device), for multi-pass ncu captures")
@@ -302,6 +306,67 @@ def aggregate(dist, new_tokens: int, decode_ms: float, e2e_s: float):
     return all_tokens / (max_decode_ms / 1000.0), all_tokens / max_e2e_s, all_tokens, max_decode_ms
 
 
+def run_config5(args, dist):
+    """each GPU decodes a batch of B independent
+    sequences (random 4096-token contexts, seeds 3 + index, 256 new tokens,
+    k = 4, oracle draft p) in lockstep rounds through
+    jl_generate_speculative_batch; replicas on N GPUs.  `value` = all ranks'
+    new tokens over the slowest rank's decode time; HBM GB/s per GPU from the
+    algorithmic bytes (weights per lockstep pass, each sequence's KV per pass
+    it takes part in); the roofline is that of the path's formula: bytes per
+    round W_t + k W_d + B KV_t(ctx) + B k KV_d(ctx) at the measured copy
+    bandwidth."""
+    import jalapeno as J
+    import oracle as O
+
+    peak, peak_kind = measured_peaks()
+    ctx, new, k = 4096, 256, args.gamma
+    batches = [int(x) for x in args.batches.split(",")]
+    t, d = PRESETS["qwen3-8b"], PRESETS["qwen3-0.6b"]
+    opts = dict(kv_pool_tokens=max(batches) * (ctx + new + 128) + 1024, max_pass_rows=256, device=dist.local)
+    target = J.Model.synthesize(**t, seed=0, mxfp4=True, name="Qwen3-8B-MXFP4", **opts)
+    draft = J.Model.synthesize(**d, seed=1, mxfp4=True, name="Qwen3-0.6B-MXFP4", **opts)
+    ti, di = target.info, draft.info
+    w_t, w_d = ti.pass_bytes, di.pass_bytes
+    kv_t, kv_d = ti.kv_bytes_per_token, di.kv_bytes_per_token
+    for B in batches:
+        prompts = [O.prompt_ids(ctx, ti.vocab, 3 + i + 1000 * dist.rank) for i in range(B)]
+        g = J.generate_batch(target, prompts, new + 2 * k)
+        streams = [s.tokens for s in g.results]
+        t0 = time.perf_counter()
+        r = J.generate_speculative_batch(target, draft, prompts, new, J.DraftSchedule.fixed(k),
+                                         oracle_streams=streams, oracle_p=args.p,
+                                         oracle_seeds=[5 + i for i in range(B)])
+        wall = time.perf_counter() - t0
+        assert all(s.tokens == st[: ctx + new] for s, st in zip(r.results, streams)), \
+            "speculative output differs from greedy"
+        tokens = sum(len(s.tokens) - ctx for s in r.results)
+        value, e2e, all_tokens, max_ms = aggregate(dist, tokens, r.decode_ms, wall)
+        greedy_value, _, _, _ = aggregate(dist, B * (new + 2 * k - 1), g.decode_ms, 1.0)
+        # algorithmic bytes: weights once per lockstep pass, KV once per sequence per pass
+        draft_sets = max(s.draft.passes for s in r.results)
+        kv = sum(s.verify.passes * kv_t + s.draft.passes * kv_d for s in r.results) * (ctx + new / 2)
+        moved = r.rounds * w_t + draft_sets * w_d + kv
+        round_bytes = w_t + k * w_d + B * (ctx + new / 2) * (kv_t + k * kv_d)
+        roof = peak * 1e9 * (tokens / max(r.rounds, 1)) / round_bytes
+        line = {"metric": "configs[4] aggregate spec-decode tok/s (k=4, per-GPU batch, 4096-token contexts)",
+                "value": value, "unit": "tok/s", "n_gpus": dist.world, "batch_per_gpu": B,
+                "higher_is_better": True, "scaling": "weak", "dtype": "mxfp4 weights, f32 activations",
+                "data": "synthetic: seeded N(0, 0.02) weights, uniform random contexts",
+                "ms_decode": max_ms, "tokens": all_tokens, "rounds": r.rounds,
+                "acceptance": sum(s.accepted for s in r.results) / max(1, sum(s.drafted for s in r.results)),
+                "hbm_gbs_per_gpu": moved / (r.decode_ms / 1000.0) / 1e9,
+                "roofline": {"tok_s": roof * dist.world, "frac": value / (roof * dist.world), "peak_gbs": peak,
+                             "peak": peak_kind},
+                "greedy_batch_tok_s": greedy_value, "prefill_s": r.prefill_ms / 1000.0,
+                "e2e": {"value": e2e, "unit": "tok/s (wall, prefill included)"},
+                "config": {"workload": "Qwen3-8B MXFP4 + Qwen3-0.6B MXFP4, batched speculative decode",
+                           "batch_per_gpu": B, "context_tokens": ctx, "new_tokens": new, "k": k,
+                           "draft_mode": f"oracle p={args.p}", "parallelism": f"replicas x{dist.world}"}}
+        if dist.rank == 0:
+            print(json.dumps(line), flush=True)
+
+
 def workload_config(args):
     return {"workload": "Qwen3-8B MXFP4 target + Qwen3-0.6B MXFP4 draft, greedy speculative decode",
             "k": args.gamma, "batch_per_gpu": 1, "prompt_tokens": args.prompt,
@@ -320,6 +385,10 @@ def main():
         return
     if args.profile:
         run_profile(args, dist)
+        dist.close()
+        return
+    if args.config5:
+        run_config5(args, dist)
         dist.close()
         return
     import jalapeno as J

@@ -36,7 +36,9 @@ jl_status add_conditional(cudaGraph_t graph, cudaGraphNode_t* deps, size_t ndeps
 
 int att_splits_for(const jl_model* m, size_t max_ctx) {
     const size_t pages = (max_ctx + PAGE - 1) / PAGE;
-    const int need = (int)std::max<size_t>(1, (pages + ATT_WIN - 1) / ATT_WIN);
+    const int nwin = (int)std::max<size_t>(1, (pages + ATT_WIN - 1) / ATT_WIN);
+    const int wpc = (nwin + ATT_ZMAX - 1) / ATT_ZMAX;  // as the attention kernel splits a row
+    const int need = (nwin + wpc - 1) / wpc;
     int s = 1;
     while (s < need) s <<= 1;
     return std::min(s, std::max(1, m->att_smax));
@@ -298,6 +300,7 @@ jl_status host_pass_multi(jl_model* m, jl_cache* c, const uint32_t* ids, size_t 
     JL_TRY(stage_end(m, sl, st));
     PassCtx ctx{m, st, C * SMALL_M, C * SMALL_M, false, att_splits_for(m, c->len + n)};
     ctx.chunks = C;
+    ctx.prefill = true;
     return record_pass_ctx(ctx, m->layers, head);
 }
 

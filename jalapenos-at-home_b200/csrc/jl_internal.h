@@ -34,6 +34,7 @@ constexpr int PAGE = 64;         // tokens per KV page
 constexpr int SMALL_M = 16;      // passes up to this many rows use the decode kernels (tensor-core MXFP4)
 constexpr int ATT_WIN = 2;       // KV pages per decode-attention window (one CTA per window over long contexts)
 constexpr int ATT_PART = 4 + HEAD;  // floats of one window's partial: max, sum, 2 pad, 128 outputs
+constexpr int ATT_ZMAX = 64;     // window CTAs per row at most: past 64 windows each CTA takes several
 constexpr int MAX_SEQS = 64;     // sequences one pass may touch
 constexpr int MAX_CHUNKS = 32;   // 16-row chunks of one multi-chunk pass (fused decode kernels)
 constexpr int MAX_GAMMA = 16;    // largest draft length of the device-resident loop
@@ -229,10 +230,12 @@ struct jl_model {
     // they have run, so a pass never reads a later pass's descriptors.
     jl::StageSlot stage[jl::STAGE_SLOTS];
     int stage_next = 0;
-    // decode attention over long contexts: one CTA per window of pages, a
-    // partial-sum workspace [kv_heads][16 rows][att_smax][group][4 + 128] f32
-    // and per (kv head, row) arrival counters (zero between launches)
+    // decode attention over long contexts: one CTA per window of pages (up
+    // to att_smax per row), a partial-sum workspace of att_rows rows
+    // [kv_heads][rows][att_smax][group][4 + 128] f32 and per (kv head, row)
+    // arrival counters (zero between launches)
     int att_smax = 1;
+    int att_rows = 16;
     float* att_ws = nullptr;
     int* att_cnt = nullptr;
     int small_graph_splits[5] = {};       // att_splits each small_graph was captured with
@@ -325,6 +328,9 @@ struct PassCtx {
     // head_row[16c ..] as indices within the chunk and predicted into
     // out_ids[16c ..].  Each kernel runs every chunk in one launch.
     int chunks = 1;
+    // A multi-chunk pass over one sequence's prompt at consecutive positions
+    // (predict): attention shares each K/V page among 8 rows.
+    bool prefill = false;
     // The rows this pass reads: by default the model's own pass buffer; a
     // batched loop points each pass at its own buffers.
     PassBuf view{};

@@ -675,11 +675,13 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
     // pass's longest row (a grid too small for a row, which no launch here
     // makes, falls back to CTA z = 0 doing every window).
     const int nwin = max(1, (npages + ATT_WIN - 1) / ATT_WIN);
-    const int nsplit = nwin <= (int)gridDim.z ? nwin : 1;
+    const int wpc = (nwin + ATT_ZMAX - 1) / ATT_ZMAX;  // consecutive windows per CTA (1 up to 64 windows)
+    const int need = (nwin + wpc - 1) / wpc;
+    const int nsplit = need <= (int)gridDim.z ? need : 1;
     const int zs = blockIdx.z;
     if (zs >= (valid ? nsplit : 1)) return;  // uniform over the CTA
-    const int w_lo = nsplit > 1 ? zs * ATT_WIN : 0;
-    const int w_hi = nsplit > 1 ? min(npages, w_lo + ATT_WIN) : npages;
+    const int w_lo = nsplit > 1 ? zs * wpc * ATT_WIN : 0;
+    const int w_hi = nsplit > 1 ? min(npages, w_lo + wpc * ATT_WIN) : npages;
     const int32_t* pt = valid ? pb.page_table[rd.seq] : nullptr;
     if (valid && threadIdx.x == 0) {
         ptx::mbar_init(&bar, 1);
@@ -999,6 +1001,197 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
     }
 }
 
+// Prefill attention (lib.rs:401-441) for a multi-chunk pass whose rows are
+// one sequence at consecutive positions, as predict builds them: a CTA per
+// (KV head, PF_ROWS rows) streams the sequence's K/V pages once through
+// shared memory (two page buffers) for all its rows x `group` query heads.
+// Each (row, head) pair belongs to one warp, which keeps its running max and
+// sum over the pages in order: lanes score positions lane and lane + 32 of a
+// page (causal per row), then own 4 of the 128 output dimensions; a warp
+// keeps NP = group / 2 pairs (group <= 8).  The output goes out as in
+// k_attn_decode: f32 rows and the o projection's pieces.
+constexpr int PF_ROWS = 8;
+constexpr int PF_WARPS = 16;
+__host__ __device__ constexpr size_t pf_smem(int f32, int group) {
+    return 4 * (size_t)att_page_bytes(f32) + (size_t)PF_ROWS * group * HEAD * 4 + PF_WARPS * HEAD * 4;
+}
+
+template <int F32, int NP>
+__global__ void __launch_bounds__(PF_WARPS * 32) k_attn_prefill(PassBuf pb, const float* __restrict__ qkv, int ld,
+                                                               int group, KvView kv, float* __restrict__ out,
+                                                               int out_ld, uint8_t* __restrict__ bout, int bN,
+                                                               size_t cs_bout) {
+    constexpr int PB = att_page_bytes(F32);
+    extern __shared__ __align__(128) uint8_t pf[];  // [2 buffers][K|V][PB], q [pairs][HEAD], o [warps][HEAD]
+    float* qs = (float*)(pf + 4 * PB);
+    float* os = qs + PF_ROWS * group * HEAD;
+    __shared__ uint64_t bar[2];
+    __shared__ int page_s[2];
+    const int g = blockIdx.x, r0 = blockIdx.y * PF_ROWS;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int chunk = r0 / SMALL_M, lr0 = r0 % SMALL_M;
+    if (bout) bout += chunk * cs_bout;
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&bar[0], 1);
+        ptx::mbar_init(&bar[1], 1);
+        ptx::fence_barrier_init();
+    }
+    __syncthreads();
+    ptx::grid_dependency_wait();  // q and this pass's K/V come from the q|k|v kernel
+    ptx::launch_dependents();
+    const int rows = pb.hdr[chunk].rows;
+    const RowDesc first = pb.row[r0];
+    const bool seq_ok = lr0 < rows && (unsigned)first.seq < (unsigned)MAX_SEQS;
+    const int32_t* pt = seq_ok ? pb.page_table[first.seq] : nullptr;
+    // live rows of this CTA: the same sequence at consecutive positions
+    int nlive = 0, last_pos = -1;
+    for (int i = 0; i < PF_ROWS && lr0 + i < rows; ++i) {
+        const RowDesc rd = pb.row[r0 + i];
+        if (!seq_ok || rd.seq != first.seq || rd.pos != first.pos + i || rd.pos < 0 || rd.pos >= kv.max_pos) {
+            if (threadIdx.x == 0) atomicOr(kv.err, 2);
+            break;
+        }
+        nlive = i + 1;
+        last_pos = rd.pos;
+    }
+    const int pairs = PF_ROWS * group;
+    // q of every live pair (QK-normalised and rotated by the q|k|v kernel)
+    for (int i = threadIdx.x; i < pairs * (HEAD / 4); i += blockDim.x) {
+        const int pr = i / (HEAD / 4), d4 = i % (HEAD / 4);
+        const int r = pr / group, h = g * group + pr % group;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < nlive) v = *(const float4*)(qkv + (size_t)(r0 + r) * ld + h * HEAD + 4 * d4);
+        *(float4*)(qs + (size_t)pr * HEAD + 4 * d4) = v;
+    }
+    const int npages = nlive ? last_pos / PAGE + 1 : 0;
+    __syncthreads();  // every pair's q is in shared memory
+    auto issue = [&](int p) {  // thread 0: K and V of page p into buffer p & 1
+        const int pg = pt[p];
+        const int b = p & 1;
+        page_s[b] = page_ok(kv, pg) ? pg : -1;
+        if (page_s[b] < 0) {
+            ptx::mbar_arrive(&bar[b]);
+            return;
+        }
+        ptx::mbar_arrive_expect_tx(&bar[b], 2 * PB);
+        const size_t off = kv_index(pg, g, 0, kv.kv_heads) * (F32 ? 4 : 2);
+        ptx::bulk_g2s(pf + (2 * b) * PB, (const uint8_t*)kv.k + off, PB, &bar[b]);
+        ptx::bulk_g2s(pf + (2 * b + 1) * PB, (const uint8_t*)kv.v + off, PB, &bar[b]);
+    };
+    if (threadIdx.x == 0 && npages > 0) issue(0);
+    float m[NP], l[NP], acc[NP][4];
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+        m[j] = -INFINITY;
+        l[j] = 0.f;
+        acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    }
+    const float scale = sqrtf(128.0f);
+    bool ok = true;
+    for (int p = 0; p < npages; ++p) {
+        const int b = p & 1;
+        if (threadIdx.x == 0 && p + 1 < npages) issue(p + 1);  // the other buffer was freed below
+        if (!ptx::mbar_wait(&bar[b], (p >> 1) & 1, ATT_WAIT)) ok = false;
+        if (page_s[b] >= 0) {
+            const uint8_t* Ks = pf + (2 * b) * PB;
+            const uint8_t* Vs = pf + (2 * b + 1) * PB;
+#pragma unroll
+            for (int j = 0; j < NP; ++j) {
+                const int pr = warp + j * PF_WARPS;
+                const int r = pr / group;
+                if (pr >= pairs || r >= nlive) continue;  // uniform over the warp
+                const int vis = first.pos + r + 1 - p * PAGE;  // positions of this page the row sees
+                if (vis <= 0) continue;
+                const float* qw = qs + (size_t)pr * HEAD;
+                float sc[2];
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const int t = lane + 32 * half;
+                    float dot = 0.f;
+                    if (F32) {
+                        const float4* kr = (const float4*)(Ks + (size_t)t * HEAD * 4);
+#pragma unroll 8
+                        for (int c = 0; c < 32; ++c) {
+                            const int cc = (c + lane) & 31;
+                            const float4 k4 = kr[cc];
+                            const float4 q4 = *(const float4*)(qw + 4 * cc);
+                            dot = fmaf(q4.x, k4.x, dot);
+                            dot = fmaf(q4.y, k4.y, dot);
+                            dot = fmaf(q4.z, k4.z, dot);
+                            dot = fmaf(q4.w, k4.w, dot);
+                        }
+                    } else {
+                        const uint4* kr = (const uint4*)(Ks + (size_t)t * HEAD * 2);
+#pragma unroll 4
+                        for (int c = 0; c < 16; ++c) {
+                            const int cc = (c + lane) & 15;
+                            const uint4 k8 = kr[cc];
+                            const float4 qa = *(const float4*)(qw + 8 * cc);
+                            const float4 qb = *(const float4*)(qw + 8 * cc + 4);
+                            dot = fmaf(qa.x, __uint_as_float(k8.x << 16), dot);
+                            dot = fmaf(qa.y, __uint_as_float(k8.x & 0xffff0000u), dot);
+                            dot = fmaf(qa.z, __uint_as_float(k8.y << 16), dot);
+                            dot = fmaf(qa.w, __uint_as_float(k8.y & 0xffff0000u), dot);
+                            dot = fmaf(qb.x, __uint_as_float(k8.z << 16), dot);
+                            dot = fmaf(qb.y, __uint_as_float(k8.z & 0xffff0000u), dot);
+                            dot = fmaf(qb.z, __uint_as_float(k8.w << 16), dot);
+                            dot = fmaf(qb.w, __uint_as_float(k8.w & 0xffff0000u), dot);
+                        }
+                    }
+                    sc[half] = t < vis ? __fdiv_rn(dot, scale) : -INFINITY;
+                }
+                const float nm = fmaxf(m[j], warp_max(fmaxf(sc[0], sc[1])));
+                const float corr = m[j] == -INFINITY ? 0.f : expf(m[j] - nm);
+                const float p0 = sc[0] == -INFINITY ? 0.f : expf(sc[0] - nm);
+                const float p1 = sc[1] == -INFINITY ? 0.f : expf(sc[1] - nm);
+                l[j] = fmaf(l[j], corr, warp_sum(p0 + p1));
+#pragma unroll
+                for (int d = 0; d < 4; ++d) acc[j][d] *= corr;
+                m[j] = nm;
+                const int n = min(PAGE, vis);
+                for (int t = 0; t < n; ++t) {
+                    const float pt_ = __shfl_sync(0xffffffffu, t < 32 ? p0 : p1, t & 31);
+                    float v[4];
+                    if (F32) {
+                        const float4 v4 = *(const float4*)(Vs + ((size_t)t * HEAD + 4 * lane) * 4);
+                        v[0] = v4.x; v[1] = v4.y; v[2] = v4.z; v[3] = v4.w;
+                    } else {
+                        const uint2 v2 = *(const uint2*)(Vs + ((size_t)t * HEAD + 4 * lane) * 2);
+                        v[0] = __uint_as_float(v2.x << 16);
+                        v[1] = __uint_as_float(v2.x & 0xffff0000u);
+                        v[2] = __uint_as_float(v2.y << 16);
+                        v[3] = __uint_as_float(v2.y & 0xffff0000u);
+                    }
+#pragma unroll
+                    for (int d = 0; d < 4; ++d) acc[j][d] = fmaf(pt_, v[d], acc[j][d]);
+                }
+            }
+        }
+        __syncthreads();  // buffer b is free for page p + 2
+    }
+    if (!ok && threadIdx.x == 0) atomicOr(kv.err, 4);  // a page copy did not arrive in time
+    // outputs: f32 rows, then the o projection's pieces (zero for dead rows)
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+        const int pr = warp + j * PF_WARPS;
+        if (pr >= pairs) continue;
+        const int r = pr / group, h = g * group + pr % group;
+        if (lr0 + r >= SMALL_M) continue;
+        const bool live = r < nlive && l[j] > 0.f;
+        float o[4];
+#pragma unroll
+        for (int d = 0; d < 4; ++d) o[d] = live ? __fdiv_rn(acc[j][d], l[j]) : 0.f;
+        if (lr0 + r < rows) *(float4*)(out + (size_t)(r0 + r) * out_ld + h * HEAD + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
+        if (bout) {
+            float* ow = os + (size_t)warp * HEAD;
+            __syncwarp();
+            *(float4*)(ow + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
+            __syncwarp();
+            mx::emit_pieces_smem(ow, HEAD, 4, lr0 + r, 1, 1, lane, 32, h * HEAD, bN, bout);
+        }
+    }
+}
+
 // First maximum of each predicted row, ties to the lower index
 // (model.rs:288-296, gpu.metal:176-212).
 __global__ void __launch_bounds__(1024) k_argmax(PassBuf pb, const float* __restrict__ logits,
@@ -1196,6 +1389,12 @@ jl_status configure_kernels() {
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_STORE>()));
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_ADD>()));
     JL_TRY((configure_skinny<MAT_MXFP4, EPI_SWIGLU>()));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_prefill<0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_smem(0, 8)));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_prefill<0, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_smem(0, 8)));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_prefill<0, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_smem(0, 8)));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_prefill<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_smem(1, 8)));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_prefill<1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_smem(1, 8)));
+    JL_CUDA(cudaFuncSetAttribute(k_attn_prefill<1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_smem(1, 8)));
     JL_CUDA(cudaFuncSetAttribute(k_attn_decode<0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(0)));
     JL_CUDA(cudaFuncSetAttribute(k_attn_decode<1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(1)));
     JL_CUDA(cudaFuncSetAttribute(k_attn_decode<0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(0)));
@@ -1242,13 +1441,30 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     uint8_t* bout = pieces ? c.m->mx.battn : nullptr;
     const bool chunked = c.chunks > 1;
     const int bN = 8 * (chunked ? SMALL_M : c.rows_cap);
+    if (chunked && c.prefill && group <= 8) {  // one sequence's prompt: K/V pages shared by 8 rows
+        const dim3 g3(c.m->kv_heads, c.rows_cap / PF_ROWS), blk(PF_WARPS * 32);
+        const int qw = c.m->q_heads * HEAD;
+        const int f32 = c.m->kv.dtype == JL_KV_F32 ? 1 : 0;
+        const int np = group <= 2 ? 1 : group <= 4 ? 2 : 4;  // (row, head) pairs per warp
+        auto go = [&](auto kern) {
+            return launch_pdl(kern, g3, blk, pf_smem(f32, group), c.stream, c.pass(), (const float*)c.m->s.qkv,
+                              qkv_ld(c.m), group, kv_view(c.m, layer), c.m->s.attn, qw, bout, bN, c.m->mx.sattn);
+        };
+        switch (f32 * 3 + (np == 1 ? 0 : np == 2 ? 1 : 2)) {
+            case 0: return go(k_attn_prefill<0, 1>);
+            case 1: return go(k_attn_prefill<0, 2>);
+            case 2: return go(k_attn_prefill<0, 4>);
+            case 3: return go(k_attn_prefill<1, 1>);
+            case 4: return go(k_attn_prefill<1, 2>);
+            default: return go(k_attn_prefill<1, 4>);
+        }
+    }
     if ((c.rows_cap <= SMALL_M || chunked) && group <= 8) {  // decode passes: a warp per query head
         const int split = att_split(group);
-        // the split workspace holds SMALL_M rows x att_smax windows: a pass
-        // over more rows takes fewer window CTAs per row (a row whose context
-        // spans more windows than the grid has is done by one CTA)
+        // the split workspace holds att_rows rows x att_smax windows (a row
+        // whose context needs more CTAs than a grid has is done by one CTA).
         int z = att_grid_splits(c);
-        while (z > 1 && (size_t)c.rows_cap * z > (size_t)SMALL_M * c.m->att_smax) z >>= 1;
+        while (z > 1 && (size_t)c.rows_cap * z > (size_t)c.m->att_rows * c.m->att_smax) z >>= 1;
         const dim3 g2(c.m->kv_heads, c.rows_cap, z), blk(32 * group * split);
         const int qw = c.m->q_heads * HEAD;
         const AttnRaw none{};

@@ -96,14 +96,13 @@ jl_status finish_model(jl_model* m, const jl_model_options& o) {
     }
     m->kv.free_list.resize(m->kv.pages);
     for (size_t i = 0; i < m->kv.pages; ++i) m->kv.free_list[i] = (int32_t)(m->kv.pages - 1 - i);
-    // decode attention over long contexts: a window CTA's partial sums for
-    // every window a sequence of the pool can span
-    // (no more than the context limit needs)
-    const size_t seq_pages = std::min(m->kv.pages, ((size_t)m->max_positions + 2 * MAX_GAMMA + PAGE - 1) / PAGE);
-    m->att_smax = (int)std::max<size_t>(1, (seq_pages + ATT_WIN - 1) / ATT_WIN);
+    // decode attention over long contexts: the partial sums of up to
+    // ATT_ZMAX window CTAs for every row of the largest multi-chunk pass
+    m->att_smax = ATT_ZMAX;
+    m->att_rows = std::max(SMALL_M, std::min(o.max_pass_rows ? (int)o.max_pass_rows : 4096, SMALL_M * MAX_CHUNKS));
     {
         const size_t group = (size_t)m->q_heads / m->kv_heads;
-        const size_t floats = (size_t)m->kv_heads * SMALL_M * m->att_smax * group * ATT_PART;
+        const size_t floats = (size_t)m->kv_heads * m->att_rows * m->att_smax * group * ATT_PART;
         if (cudaMalloc(&m->att_ws, floats * sizeof(float)) != cudaSuccess ||
             cudaMalloc(&m->att_cnt, (size_t)m->kv_heads * SMALL_M * MAX_CHUNKS * sizeof(int)) != cudaSuccess) {
             cudaGetLastError();
