@@ -972,21 +972,46 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
         if (!last_s) return;
         __threadfence();  // the other windows' partials are visible
         if (sub != 0) return;
-        M = -INFINITY;
-        for (int z = 0; z < nsplit; ++z) M = fmaxf(M, __ldcg(part + ((size_t)z * group + hw) * ATT_PART));
+        // Lane z (and z + 32) fetches window z's max and sum, so those loads
+        // go out together; the sums then run in window order through
+        // shuffles, the output loads several windows at a time.
+        static_assert(ATT_ZMAX <= 64, "two windows per lane");
+        float mz_l[2], lz_l[2], f_l[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int z = lane + 32 * i;
+            const float* P = part + ((size_t)z * group + hw) * ATT_PART;
+            mz_l[i] = z < nsplit ? __ldcg(P) : -INFINITY;
+            lz_l[i] = z < nsplit ? __ldcg(P + 1) : 0.f;
+        }
+        M = warp_max(fmaxf(mz_l[0], mz_l[1]));
+#pragma unroll
+        for (int i = 0; i < 2; ++i) f_l[i] = mz_l[i] == -INFINITY ? 0.f : expf(mz_l[i] - M);
         L = 0.f;
         o[0] = o[1] = o[2] = o[3] = 0.f;
-        for (int z = 0; z < nsplit; ++z) {
-            const float* P = part + ((size_t)z * group + hw) * ATT_PART;
-            const float mz = __ldcg(P);
-            if (mz == -INFINITY) continue;  // a window whose pages were all flagged
-            const float f = expf(mz - M);
-            L = fmaf(__ldcg(P + 1), f, L);
-            const float4 a4 = __ldcg((const float4*)(P + 4 + 4 * lane));
-            o[0] = fmaf(a4.x, f, o[0]);
-            o[1] = fmaf(a4.y, f, o[1]);
-            o[2] = fmaf(a4.z, f, o[2]);
-            o[3] = fmaf(a4.w, f, o[3]);
+        constexpr int ZB = F32 && RAW ? 2 : 4;  // windows per batch of loads (registers of the f32 raw variant)
+        for (int z0 = 0; z0 < nsplit; z0 += ZB) {
+            float4 a4[ZB];
+#pragma unroll
+            for (int j = 0; j < ZB; ++j) {
+                const int z = z0 + j;
+                a4[j] = z < nsplit ? __ldcg((const float4*)(part + ((size_t)z * group + hw) * ATT_PART + 4 + 4 * lane))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int j = 0; j < ZB; ++j) {
+                const int z = z0 + j;
+                if (z >= nsplit) break;
+                const float mz = __shfl_sync(0xffffffffu, z < 32 ? mz_l[0] : mz_l[1], z & 31);
+                const float f = __shfl_sync(0xffffffffu, z < 32 ? f_l[0] : f_l[1], z & 31);
+                const float lz = __shfl_sync(0xffffffffu, z < 32 ? lz_l[0] : lz_l[1], z & 31);
+                if (mz == -INFINITY) continue;  // a window whose pages were all flagged
+                L = fmaf(lz, f, L);
+                o[0] = fmaf(a4[j].x, f, o[0]);
+                o[1] = fmaf(a4[j].y, f, o[1]);
+                o[2] = fmaf(a4[j].z, f, o[2]);
+                o[3] = fmaf(a4[j].w, f, o[3]);
+            }
         }
     }
     if (sub != 0) return;
@@ -1107,7 +1132,7 @@ __global__ void __launch_bounds__(PF_WARPS * 32) k_attn_prefill(PassBuf pb, cons
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     const int t = lane + 32 * half;
-                    float dot = 0.f;
+                    float d[4] = {0.f, 0.f, 0.f, 0.f};  // four chains, summed at the end
                     if (F32) {
                         const float4* kr = (const float4*)(Ks + (size_t)t * HEAD * 4);
 #pragma unroll 8
@@ -1115,10 +1140,10 @@ __global__ void __launch_bounds__(PF_WARPS * 32) k_attn_prefill(PassBuf pb, cons
                             const int cc = (c + lane) & 31;
                             const float4 k4 = kr[cc];
                             const float4 q4 = *(const float4*)(qw + 4 * cc);
-                            dot = fmaf(q4.x, k4.x, dot);
-                            dot = fmaf(q4.y, k4.y, dot);
-                            dot = fmaf(q4.z, k4.z, dot);
-                            dot = fmaf(q4.w, k4.w, dot);
+                            d[0] = fmaf(q4.x, k4.x, d[0]);
+                            d[1] = fmaf(q4.y, k4.y, d[1]);
+                            d[2] = fmaf(q4.z, k4.z, d[2]);
+                            d[3] = fmaf(q4.w, k4.w, d[3]);
                         }
                     } else {
                         const uint4* kr = (const uint4*)(Ks + (size_t)t * HEAD * 2);
@@ -1128,16 +1153,17 @@ __global__ void __launch_bounds__(PF_WARPS * 32) k_attn_prefill(PassBuf pb, cons
                             const uint4 k8 = kr[cc];
                             const float4 qa = *(const float4*)(qw + 8 * cc);
                             const float4 qb = *(const float4*)(qw + 8 * cc + 4);
-                            dot = fmaf(qa.x, __uint_as_float(k8.x << 16), dot);
-                            dot = fmaf(qa.y, __uint_as_float(k8.x & 0xffff0000u), dot);
-                            dot = fmaf(qa.z, __uint_as_float(k8.y << 16), dot);
-                            dot = fmaf(qa.w, __uint_as_float(k8.y & 0xffff0000u), dot);
-                            dot = fmaf(qb.x, __uint_as_float(k8.z << 16), dot);
-                            dot = fmaf(qb.y, __uint_as_float(k8.z & 0xffff0000u), dot);
-                            dot = fmaf(qb.z, __uint_as_float(k8.w << 16), dot);
-                            dot = fmaf(qb.w, __uint_as_float(k8.w & 0xffff0000u), dot);
+                            d[0] = fmaf(qa.x, __uint_as_float(k8.x << 16), d[0]);
+                            d[1] = fmaf(qa.y, __uint_as_float(k8.x & 0xffff0000u), d[1]);
+                            d[2] = fmaf(qa.z, __uint_as_float(k8.y << 16), d[2]);
+                            d[3] = fmaf(qa.w, __uint_as_float(k8.y & 0xffff0000u), d[3]);
+                            d[0] = fmaf(qb.x, __uint_as_float(k8.z << 16), d[0]);
+                            d[1] = fmaf(qb.y, __uint_as_float(k8.z & 0xffff0000u), d[1]);
+                            d[2] = fmaf(qb.z, __uint_as_float(k8.w << 16), d[2]);
+                            d[3] = fmaf(qb.w, __uint_as_float(k8.w & 0xffff0000u), d[3]);
                         }
                     }
+                    const float dot = __fadd_rn(__fadd_rn(d[0], d[1]), __fadd_rn(d[2], d[3]));
                     sc[half] = t < vis ? __fdiv_rn(dot, scale) : -INFINITY;
                 }
                 const float nm = fmaxf(m[j], warp_max(fmaxf(sc[0], sc[1])));
@@ -1149,8 +1175,16 @@ __global__ void __launch_bounds__(PF_WARPS * 32) k_attn_prefill(PassBuf pb, cons
                 for (int d = 0; d < 4; ++d) acc[j][d] *= corr;
                 m[j] = nm;
                 const int n = min(PAGE, vis);
+                // the page's weights go through this warp's row of shared
+                // memory: each lane then reads them as broadcasts
+                float* pw = os + (size_t)warp * HEAD;
+                __syncwarp();
+                pw[lane] = p0;
+                pw[lane + 32] = p1;
+                __syncwarp();
+#pragma unroll 8
                 for (int t = 0; t < n; ++t) {
-                    const float pt_ = __shfl_sync(0xffffffffu, t < 32 ? p0 : p1, t & 31);
+                    const float pt_ = pw[t];
                     float v[4];
                     if (F32) {
                         const float4 v4 = *(const float4*)(Vs + ((size_t)t * HEAD + 4 * lane) * 4);
