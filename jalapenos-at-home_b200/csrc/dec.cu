@@ -7,11 +7,12 @@
 // kernels take almost none: each CTA owns a tile of weight rows and copies
 // them (MXFP4 codes and scales, exactly as the checkpoint stores them) into
 // shared memory with bulk copies BEFORE it waits for the previous kernel
-// (weights never depend on it).  After the wait it loads the f32 input rows,
-// normalises them (RMSNorm, lib.rs:268-290), and each warp computes
-// its rows' dot products: lanes take 32-element blocks, decode E2M1 pairs in
-// hardware (cvt.rn.f16x2.e2m1x2), apply the block's E8M0 scale, and the warp
-// sums.  Epilogues: q|k|v (QK-RMSNorm, RoPE, K/V appended to the cache),
+// (weights never depend on it).  After the wait it loads the f32 input rows
+// (times the RMSNorm weight), and each warp computes its rows' dot products:
+// lanes take 32-element blocks, decode E2M1 pairs in hardware
+// (cvt.rn.f16x2.e2m1x2), apply the block's E8M0 scale, and the warp sums; the
+// RMSNorm division (lib.rs:268-290) is applied to those sums, so no
+// block-wide reduction stands between the input load and the dot products.  Epilogues: q|k|v (QK-RMSNorm, RoPE, K/V appended to the cache),
 // residual add, SwiGLU (lib.rs:337-468).
 //
 // The rounding differs from the tensor-core path, so a model runs these
@@ -53,8 +54,10 @@ __device__ __forceinline__ void dec_copy_rows(const DecTile& t, int r0, int n, i
 }
 
 // Loads M input rows (f32, width K) into shared memory in the swizzled chunk
-// layout; with `w` set, as the RMSNorm x / sqrt(mean(x^2) + 1e-6) * w
-// (lib.rs:268-290).  Whole CTA.
+// layout; with `w` set, as x * w, and warp j's share of row m's sum of
+// squares goes to ssq[m * 8 + j].  The RMSNorm division (lib.rs:268-290) is
+// applied to the dot products instead (dec_rms): W (x * w) / rms, so the
+// dot products need not wait for a block-wide sum.  Whole CTA (8 warps).
 // Each thread holds at most DEC_XCHUNKS float4 chunks of a row in registers,
 // so x is read from global memory once.  The thread's norm weights (wv, from
 // dec_norm_weights) are fetched before the dependency wait: they never depend
@@ -72,21 +75,18 @@ __device__ __forceinline__ void dec_norm_weights(const uint16_t* __restrict__ w,
 
 __device__ __forceinline__ void dec_load_x(const float* __restrict__ x, int ldx, int M, int K,
                                            const uint16_t* __restrict__ w, const uint2 (&wv)[DEC_XCHUNKS],
-                                           float4* xs4, float* red) {
+                                           float4* xs4, float* ssq) {
     const int K4 = K / 4;
     for (int m = 0; m < M; ++m) {
         const float* xr = x + (size_t)m * ldx;
         float4 v[DEC_XCHUNKS];
-        float ss = 0.f;
 #pragma unroll
         for (int i = 0; i < DEC_XCHUNKS; ++i) {
             const int c = threadIdx.x + i * blockDim.x;
             v[i] = c < K4 ? reinterpret_cast<const float4*>(xr)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        float size = 1.f;
         if (w) {
-            // each thread sums the squares of its chunks, then the CTA adds
-            // the threads' sums (block_sum)
+            float ss = 0.f;
 #pragma unroll
             for (int i = 0; i < DEC_XCHUNKS; ++i) {
                 ss = fmaf(v[i].x, v[i].x, ss);
@@ -94,22 +94,32 @@ __device__ __forceinline__ void dec_load_x(const float* __restrict__ x, int ldx,
                 ss = fmaf(v[i].z, v[i].z, ss);
                 ss = fmaf(v[i].w, v[i].w, ss);
             }
-            ss = block_sum(ss, red);
-            size = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-6f));
+            ss = warp_sum(ss);
+            if ((threadIdx.x & 31) == 0) ssq[m * 8 + (threadIdx.x >> 5)] = ss;
         }
 #pragma unroll
         for (int i = 0; i < DEC_XCHUNKS; ++i) {
             const int c = threadIdx.x + i * blockDim.x;
             if (c >= K4) continue;
             if (w) {
-                v[i].x = __fmul_rn(__fdiv_rn(v[i].x, size), bf16f(wv[i].x & 0xffffu));
-                v[i].y = __fmul_rn(__fdiv_rn(v[i].y, size), bf16f(wv[i].x >> 16));
-                v[i].z = __fmul_rn(__fdiv_rn(v[i].z, size), bf16f(wv[i].y & 0xffffu));
-                v[i].w = __fmul_rn(__fdiv_rn(v[i].w, size), bf16f(wv[i].y >> 16));
+                v[i].x = __fmul_rn(v[i].x, bf16f(wv[i].x & 0xffffu));
+                v[i].y = __fmul_rn(v[i].y, bf16f(wv[i].x >> 16));
+                v[i].z = __fmul_rn(v[i].z, bf16f(wv[i].y & 0xffffu));
+                v[i].w = __fmul_rn(v[i].w, bf16f(wv[i].y >> 16));
             }
             xs4[m * K4 + dec_swz(c)] = v[i];
         }
     }
+}
+
+// sqrt(mean(x^2) + 1e-6) of row m from the warps' shares (in warp order),
+// after the barrier that publishes them; 1 without a norm.
+__device__ __forceinline__ float dec_rms(const float* ssq, int m, int K, bool norm) {
+    if (!norm) return 1.f;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = __fadd_rn(ss, ssq[m * 8 + j]);
+    return sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-6f));
 }
 
 // Dot products of R weight rows (codes wr[i], scales sr[i], width K) with
@@ -239,6 +249,9 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
     constexpr int RPW = TR / 8;
     static_assert(TR % 8 == 0 && RPW <= 2, "one or two rows per warp of an 8-warp CTA");
     if (warp >= n) return;
+    float rms[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) rms[m] = dec_rms(red, m, K, a.norm != nullptr);
     if (EPI == DEC_SWIGLU) {
         const uint8_t* wr[2 * RPW];
         const uint8_t* sr[2 * RPW];
@@ -259,9 +272,10 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
                 if (r >= n) continue;
 #pragma unroll
                 for (int m = 0; m < M; ++m)  // lib.rs:459-463
-                    if (m < rows)
-                        a.y[(size_t)m * a.ldy + r0 + r] =
-                            __fmul_rn(__fdiv_rn(o[h][m], __fadd_rn(1.0f, expf(-o[h][m]))), o[RPW + h][m]);
+                    if (m < rows) {
+                        const float g = __fdiv_rn(o[h][m], rms[m]), u = __fdiv_rn(o[RPW + h][m], rms[m]);
+                        a.y[(size_t)m * a.ldy + r0 + r] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                    }
             }
     } else {
         const uint8_t* wr[RPW];
@@ -282,7 +296,8 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
                 for (int m = 0; m < M; ++m)
                     if (m < rows) {
                         float* d = a.y + (size_t)m * a.ldy + r0 + r;
-                        *d = EPI == DEC_ADD ? __fadd_rn(*d, o[h][m]) : o[h][m];  // residual (model.rs:178-186)
+                        const float v = __fdiv_rn(o[h][m], rms[m]);
+                        *d = EPI == DEC_ADD ? __fadd_rn(*d, v) : v;  // residual (model.rs:178-186)
                     }
             }
     }

@@ -265,6 +265,9 @@ struct MxArgs {
     // in a 256-column allocation, or 256 in a 512-column one (two
     // accumulators of 128 columns; the launch then keeps one CTA per SM)
     int acc_step;
+    // Ring slots whose weights are requested into L2 ahead of their copy
+    // into shared memory (0: none)
+    int l2_ahead;
 };
 
 enum : int { MX_STORE = 0, MX_ADD = 1, MX_SWIGLU = 2, MX_QKV = 3, MX_HEAD = 4 };
@@ -442,6 +445,22 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
                 pre = g;
             }
             ptx::grid_dependency_wait();
+            // Slot h of this CTA is stage s0 + (h % spt) * G of its
+            // (h / spt)-th tile.  Once the activation copies of the slots
+            // loaded before the wait are out, each slot's copy is followed
+            // by an L2 request for the weights of the slot l2_ahead + ST - 1
+            // further on, so that copy later finds them in L2: more bytes
+            // are on their way from HBM than the ring holds.
+            const int spt = (s1 - s0 + G - 1) / G;
+            int pf = pre;  // next slot whose weights go to L2
+            auto l2_upto = [&](int last) {
+                for (; a.l2_ahead > 0 && spt > 0 && pf <= last; ++pf) {
+                    const int t = cid + (pf / spt) * NC;
+                    if (t >= a.T) break;
+                    const int s = s0 + (pf % spt) * G;
+                    ptx::bulk_prefetch_l2(a.a + ((size_t)t * a.S + s) * WS, (uint32_t)(min(G, s1 - s) * WS));
+                }
+            };
             int g = 0;
             for (int t = cid; t < a.T && ok; t += NC) {
                 for (int s = s0; s < s1; s += G, ++g) {
@@ -456,6 +475,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
                         ptx::bulk_g2s(base, a.a + ((size_t)t * a.S + s) * WS, (uint32_t)(n * WS), &full[slot]);
                     }
                     ptx::bulk_g2s(base + G * WS, a.b + (size_t)s * BS, (uint32_t)(n * BS), &full[slot]);
+                    if (g + 1 >= pre) l2_upto(g + ST + a.l2_ahead - 1);
                 }
             }
             // every load is issued: the next kernel may start prefetching
@@ -952,6 +972,11 @@ size_t mx_smem(int N, int kind, int mcap, int ks) {
     return (size_t)st * mx_slot_bytes(N, kind, gr) + part * ks + 1024;
 }
 
+// Ring slots requested into L2 beyond the ring by k_mx_gemv's loader: on for
+// the output table (measured on B200: the 8B's 1.245 GB table 220 -> 202 us
+// per pass), off for the layer projections (slightly slower with it).
+constexpr int MX_L2_AHEAD = 1;
+
 constexpr int MX_PROBE_SMEM = 120 * 1024;  // more than half an SM: one CTA per SM
 // Dynamic shared memory of a launch whose CTAs allocate all 512 TMEM
 // columns: more than half an SM, so no two CTAs (of one cluster above all,
@@ -979,6 +1004,7 @@ jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream, int chunk
     cfg.blockDim = dim3(MX_THREADS);
     cfg.dynamicSmemBytes = mx_smem(a.N, KIND, a.mcap, a.ksplit);
     MxArgs b = a;
+    b.l2_ahead = EPI == MX_HEAD ? MX_L2_AHEAD : 0;
     if (chunks > 1 && a.N > 64) {
         // several tiles per CTA: two 128-column accumulators, so a tile's
         // epilogue overlaps the next tile's MMAs

@@ -135,6 +135,12 @@ __device__ __forceinline__ void cluster_wait() {
 // ---- bulk copies (global -> shared through the TMA engine) -------------------
 
 // 1-D bulk copy; src, dst 16-byte aligned, bytes a multiple of 16.
+// Asks for `bytes` at `src` to be brought into L2, with no shared-memory
+// destination and no completion to wait for (16-byte aligned address and size).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

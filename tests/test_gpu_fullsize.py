@@ -72,3 +72,19 @@ def test_long_context_draft_and_verify_attention():
     assert r.tokens == greedy
     r = J.generate_speculative(target, draft, prompt, 16, 4)
     assert r.tokens == greedy
+
+
+def test_draft_step_path_proposes_the_models_own_greedy_tokens():
+    """The draft-step kernels (CUDA-core MXFP4 projections, attention on raw
+    q|k|v, the RMSNorm division applied to the dot products) against the
+    tensor-core path the greedy loop takes: with the same Qwen3-0.6B MXFP4
+    weights as target and draft, the real draft's proposals are the target's
+    own greedy tokens except at a near tie of the two paths' roundings, so
+    almost every proposal is accepted."""
+    cfg = O.PRESETS["qwen3-0.6b"]
+    target = J.Model.from_config(cfg, 1, mxfp4=True, kv_pool_tokens=1024)
+    draft = J.Model.from_config(cfg, 1, mxfp4=True, kv_pool_tokens=1024)
+    greedy = target.generate(PROMPT, 40)
+    r = J.generate_speculative(target, draft, PROMPT, 40, 4)
+    assert r.tokens == greedy
+    assert r.drafted > 0 and r.accepted >= 0.9 * r.drafted, (r.accepted, r.drafted)
