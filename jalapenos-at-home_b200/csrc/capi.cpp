@@ -148,9 +148,9 @@ jl_status jl_model_load(const char* dir, const jl_model_options* opts, jl_model*
     JL_GUARD({
         HostConfig cfg;
         JL_TRY(load_config(dir, &cfg));
-        jl_weights w;
-        JL_TRY(load_weights(dir, &w));
-        return model_from_weights(&w, cfg, o, out);
+        WeightIndex w;
+        JL_TRY(scan_weights(dir, &w));
+        return model_from_checkpoint(w, cfg, o, out);
     })
 }
 

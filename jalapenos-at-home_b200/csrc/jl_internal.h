@@ -77,6 +77,28 @@ struct HostConfig {
     int layers = 0, max_positions = 0, eos = 0;
 };
 
+// Where a tensor's bytes lie in a checkpoint file.
+struct FileRange {
+    std::string path;
+    uint64_t offset = 0, bytes = 0;
+};
+
+// A checkpoint's tensors after every header check, with the payloads left in
+// the files: BF16 values (little-endian u16) or MXFP4 packed codes at `data`.
+// MXFP4 scales are read while scanning (a NaN scale is a format error), and
+// are 1/16 of the packed bytes.
+struct IndexTensor {
+    std::string name;
+    jl_dtype dtype = JL_BF16;
+    std::vector<size_t> shape;     // logical shape
+    FileRange data;
+    std::vector<uint8_t> scales;   // JL_MXFP4
+};
+
+struct WeightIndex {
+    std::map<std::string, IndexTensor> tensors;
+};
+
 }  // namespace jl
 
 struct jl_weights {
@@ -86,6 +108,8 @@ struct jl_weights {
 namespace jl {
 
 jl_status load_weights(const std::string& dir, jl_weights* out);
+jl_status scan_weights(const std::string& dir, WeightIndex* out);
+jl_status read_range(const FileRange& r, void* dst, size_t offset, size_t bytes);
 jl_status load_config(const std::string& dir, HostConfig* out);
 
 // ---- device structures -------------------------------------------------------
@@ -274,8 +298,8 @@ struct jl_cache {
 namespace jl {
 
 // ---- model construction (model.cu) --------------------------------------------
-jl_status model_from_weights(jl_weights* w, const HostConfig& cfg, const jl_model_options& o,
-                             jl_model** out);
+jl_status model_from_checkpoint(const WeightIndex& w, const HostConfig& cfg, const jl_model_options& o,
+                                jl_model** out);
 jl_status model_synthesize(const jl_synth_config& c, const jl_model_options& o, jl_model** out);
 void model_free(jl_model* m);
 jl_status cache_create(jl_model* m, jl_cache** out);

@@ -304,18 +304,105 @@ jl_status build_mx(jl_model* m) {
     return JL_OK;
 }
 
-jl_status model_from_weights(jl_weights* w, const HostConfig& cfg, const jl_model_options& o,
-                             jl_model** out) {
-    auto& T = w->tensors;
-    auto find = [&](const std::string& name) -> HostTensor* {
+namespace {
+
+static_assert(__BYTE_ORDER__ == __ORDER_LITTLE_ENDIAN__,
+              "safetensors BF16 payloads (little-endian u16) are copied to the device as they are");
+
+// Streams checkpoint payloads from their files to device memory through two
+// pinned buffers: the read of one chunk overlaps the copy of the other, and
+// the host never holds more than two chunks of the checkpoint.
+class Stager {
+  public:
+    static constexpr size_t CHUNK = 16u << 20;
+
+    ~Stager() {
+        if (stream_) cudaStreamSynchronize(stream_);
+        for (int i = 0; i < 2; ++i) {
+            if (ev_[i]) cudaEventDestroy(ev_[i]);
+            if (buf_[i]) cudaFreeHost(buf_[i]);
+        }
+        if (stream_) cudaStreamDestroy(stream_);
+    }
+
+    jl_status init() {
+        JL_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+        for (int i = 0; i < 2; ++i) {
+            if (cudaHostAlloc(&buf_[i], CHUNK, cudaHostAllocDefault) != cudaSuccess) {
+                cudaGetLastError();
+                buf_[i] = nullptr;
+                set_error("could not allocate %zu bytes of pinned host memory for loading", CHUNK);
+                return JL_ERR_OOM;
+            }
+            JL_CUDA(cudaEventCreateWithFlags(&ev_[i], cudaEventDisableTiming));
+        }
+        return JL_OK;
+    }
+
+    // The bytes of `r` to dst (device memory).
+    jl_status file(const FileRange& r, char* dst) {
+        for (uint64_t off = 0; off < r.bytes; off += CHUNK) {
+            const size_t n = (size_t)std::min<uint64_t>(CHUNK, r.bytes - off);
+            const int i = next_;
+            next_ ^= 1;
+            JL_CUDA(cudaEventSynchronize(ev_[i]));  // the copy out of this buffer is done
+            JL_TRY(read_range(r, buf_[i], (size_t)off, n));
+            JL_CUDA(cudaMemcpyAsync(dst + off, buf_[i], n, cudaMemcpyHostToDevice, stream_));
+            JL_CUDA(cudaEventRecord(ev_[i], stream_));
+        }
+        return JL_OK;
+    }
+
+    // `n` bytes already in host memory (MXFP4 scales) to dst.
+    jl_status host(const void* src, size_t n, char* dst) {
+        JL_CUDA(cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, stream_));
+        return JL_OK;
+    }
+
+    jl_status finish() {
+        JL_CUDA(cudaStreamSynchronize(stream_));
+        return JL_OK;
+    }
+
+  private:
+    cudaStream_t stream_ = nullptr;
+    void* buf_[2] = {nullptr, nullptr};
+    cudaEvent_t ev_[2] = {nullptr, nullptr};
+    int next_ = 0;
+};
+
+// Whether two tensors hold the same bytes: compared chunk by chunk from the
+// files, stopping at the first difference.
+jl_status same_payload(const IndexTensor& a, const IndexTensor& b, bool* same) {
+    *same = false;
+    if (a.dtype != b.dtype || a.shape != b.shape || a.data.bytes != b.data.bytes || a.scales != b.scales)
+        return JL_OK;
+    constexpr size_t CH = 4u << 20;
+    std::vector<uint8_t> x(CH), y(CH);
+    for (uint64_t off = 0; off < a.data.bytes; off += CH) {
+        const size_t n = (size_t)std::min<uint64_t>(CH, a.data.bytes - off);
+        JL_TRY(read_range(a.data, x.data(), (size_t)off, n));
+        JL_TRY(read_range(b.data, y.data(), (size_t)off, n));
+        if (memcmp(x.data(), y.data(), n) != 0) return JL_OK;
+    }
+    *same = true;
+    return JL_OK;
+}
+
+}  // namespace
+
+jl_status model_from_checkpoint(const WeightIndex& w, const HostConfig& cfg, const jl_model_options& o,
+                                jl_model** out) {
+    auto& T = w.tensors;
+    auto find = [&](const std::string& name) -> const IndexTensor* {
         auto it = T.find(name);
         return it == T.end() ? nullptr : &it->second;
     };
     // Shapes (engine/src/gpu.rs:398-406)
-    HostTensor* embed = find("model.embed_tokens.weight");
-    HostTensor* q0 = find("model.layers.0.self_attn.q_proj.weight");
-    HostTensor* k0 = find("model.layers.0.self_attn.k_proj.weight");
-    HostTensor* g0 = find("model.layers.0.mlp.gate_proj.weight");
+    const IndexTensor* embed = find("model.embed_tokens.weight");
+    const IndexTensor* q0 = find("model.layers.0.self_attn.q_proj.weight");
+    const IndexTensor* k0 = find("model.layers.0.self_attn.k_proj.weight");
+    const IndexTensor* g0 = find("model.layers.0.mlp.gate_proj.weight");
     if (!embed || embed->shape.size() != 2) {
         set_error("missing tensor model.embed_tokens.weight");
         return JL_ERR_FORMAT;
@@ -327,12 +414,10 @@ jl_status model_from_weights(jl_weights* w, const HostConfig& cfg, const jl_mode
     const int hidden = (int)embed->shape[1];
     const int q_heads = (int)(q0->shape[0] / HEAD), kv_heads = (int)(k0->shape[0] / HEAD);
     const int inter = (int)g0->shape[0];
-    HostTensor* head = find("lm_head.weight");
+    const IndexTensor* head = find("lm_head.weight");
     // A head identical to the embedding table is stored once (gpu.rs:340-357).
     bool tied = !head;
-    if (head && head->shape == embed->shape && head->dtype == embed->dtype &&
-        head->bf16 == embed->bf16 && head->packed == embed->packed && head->scales == embed->scales)
-        tied = true;
+    if (head) JL_TRY(same_payload(*head, *embed, &tied));
     const int vocab = (int)(tied ? embed->shape[0] : head->shape[0]);
     if (q0->shape[1] != (size_t)hidden || q0->shape[0] % HEAD || k0->shape[0] % HEAD) {
         set_error("unexpected attention shapes");
@@ -383,7 +468,7 @@ jl_status model_from_weights(jl_weights* w, const HostConfig& cfg, const jl_mode
     std::vector<size_t> offs(wants.size()), offs2(wants.size());
     for (size_t i = 0; i < wants.size(); ++i) {
         auto& wt = wants[i];
-        HostTensor* t = find(wt.name);
+        const IndexTensor* t = find(wt.name);
         if (!t) {
             set_error("missing tensor %s", wt.name.c_str());
             return JL_ERR_FORMAT;
@@ -414,11 +499,15 @@ jl_status model_from_weights(jl_weights* w, const HostConfig& cfg, const jl_mode
     }
     m->arena_bytes = plan.bytes;
     char* base = (char*)m->arena;
+    // Payloads go from the files straight to the arena (engine/src/gpu.rs:359-375
+    // uploads each tensor once from host memory).
+    Stager st;
+    JL_TRY(st.init());
     for (size_t i = 0; i < wants.size(); ++i) {
         auto& wt = wants[i];
-        HostTensor* t = find(wt.name);
+        const IndexTensor* t = find(wt.name);
+        JL_TRY(st.file(t->data, base + offs[i]));
         if (wt.cols == 0) {
-            JL_CUDA(cudaMemcpy(base + offs[i], t->bf16.data(), wt.rows * 2, cudaMemcpyHostToDevice));
             *wt.norm = (const uint16_t*)(base + offs[i]);
             m->tensor_index[wt.name] = {base + offs[i], wt.rows * 2};
             continue;
@@ -426,19 +515,17 @@ jl_status model_from_weights(jl_weights* w, const HostConfig& cfg, const jl_mode
         Mat& mat = *wt.mat;
         mat.rows = (int)wt.rows;
         mat.cols = (int)wt.cols;
+        mat.data = base + offs[i];
         if (t->dtype == JL_MXFP4) {
             mat.kind = MAT_MXFP4;
-            JL_CUDA(cudaMemcpy(base + offs[i], t->packed.data(), t->packed.size(), cudaMemcpyHostToDevice));
-            JL_CUDA(cudaMemcpy(base + offs2[i], t->scales.data(), t->scales.size(), cudaMemcpyHostToDevice));
-            mat.data = base + offs[i];
+            JL_TRY(st.host(t->scales.data(), t->scales.size(), base + offs2[i]));
             mat.scales = (const uint8_t*)(base + offs2[i]);
         } else {
             mat.kind = MAT_BF16;
-            JL_CUDA(cudaMemcpy(base + offs[i], t->bf16.data(), t->bf16.size() * 2, cudaMemcpyHostToDevice));
-            mat.data = base + offs[i];
         }
         m->tensor_index[wt.name] = {mat.data, mat.bytes()};
     }
+    JL_TRY(st.finish());
     if (tied) m->head = m->embed;
     JL_TRY(finish_model(m, o));
     JL_TRY(build_mx(m));

@@ -245,7 +245,7 @@ jl_status load_config(const std::string& dir, HostConfig* out) {
     return JL_OK;
 }
 
-jl_status load_weights(const std::string& dir, jl_weights* out) {
+jl_status scan_weights(const std::string& dir, WeightIndex* out) {
     // engine/src/lib.rs:89-100: every *.safetensors file, sorted by path.
     DIR* d = opendir(dir.c_str());
     if (!d) {
@@ -265,7 +265,8 @@ jl_status load_weights(const std::string& dir, jl_weights* out) {
     }
     struct Raw {
         std::vector<size_t> shape;
-        std::vector<uint8_t> bytes;
+        FileRange at;
+        std::vector<uint8_t> bytes;  // scales only
     };
     std::map<std::string, Raw> packed, scales;
     auto& tensors = out->tensors;
@@ -348,12 +349,7 @@ jl_status load_weights(const std::string& dir, jl_weights* out) {
             // lib.rs:129-133
             if (e.start > e.end || e.end > file_len - base)
                 return fmt_error("invalid tensor offsets", e.name);
-            std::vector<uint8_t> bytes(e.end - e.start);
-            if (fseeko(f, (off_t)(base + e.start), SEEK_SET) != 0 ||
-                (bytes.size() && fread(bytes.data(), 1, bytes.size(), f) != bytes.size())) {
-                set_error("short read of %s in %s", e.name.c_str(), path.c_str());
-                return JL_ERR_IO;
-            }
+            const FileRange at{path, base + e.start, e.end - e.start};
             // lib.rs:137-141
             size_t elements = 1;
             for (size_t dim : e.shape) {
@@ -362,31 +358,35 @@ jl_status load_weights(const std::string& dir, jl_weights* out) {
             }
             if (quantized && e.dtype == "U8") {
                 // lib.rs:142-162
-                if (elements != bytes.size()) return fmt_error("invalid packed tensor size", e.name);
+                if (elements != at.bytes) return fmt_error("invalid packed tensor size", e.name);
                 if (ends_with(e.name, ".mxfp4_packed")) {
                     std::string n = e.name.substr(0, e.name.size() - strlen(".mxfp4_packed"));
                     if (packed.count(n)) return fmt_error("duplicate packed tensor");
-                    packed[n] = Raw{e.shape, std::move(bytes)};
+                    packed[n] = Raw{e.shape, at, {}};
                 } else if (ends_with(e.name, ".mxfp4_scales")) {
                     std::string n = e.name.substr(0, e.name.size() - strlen(".mxfp4_scales"));
                     if (scales.count(n)) return fmt_error("duplicate scale tensor");
-                    scales[n] = Raw{e.shape, std::move(bytes)};
+                    Raw r{e.shape, at, std::vector<uint8_t>(at.bytes)};
+                    if (fseeko(f, (off_t)at.offset, SEEK_SET) != 0 ||
+                        (at.bytes && fread(r.bytes.data(), 1, at.bytes, f) != at.bytes)) {
+                        set_error("short read of %s in %s", e.name.c_str(), path.c_str());
+                        return JL_ERR_IO;
+                    }
+                    scales[n] = std::move(r);
                 } else {
                     return fmt_error("unexpected U8 tensor", e.name);
                 }
             } else {
                 // lib.rs:163-181
                 bool dtype_ok = e.dtype == "BF16" || (quantized && e.dtype == "U16");
-                if (!dtype_ok || elements > SIZE_MAX / 2 || elements * 2 != bytes.size())
+                if (!dtype_ok || elements > SIZE_MAX / 2 || elements * 2 != at.bytes)
                     return fmt_error("expected BF16 tensor", e.name);
                 if (tensors.count(e.name)) return fmt_error("duplicate tensor");
-                HostTensor t;
+                IndexTensor t;
                 t.name = e.name;
                 t.dtype = JL_BF16;
                 t.shape = e.shape;
-                t.bf16.resize(elements);
-                for (size_t i = 0; i < elements; ++i)
-                    t.bf16[i] = (uint16_t)(bytes[2 * i] | (bytes[2 * i + 1] << 8));
+                t.data = at;
                 tensors.emplace(e.name, std::move(t));
             }
         }
@@ -403,21 +403,65 @@ jl_status load_weights(const std::string& dir, jl_weights* out) {
         // Tensor::quantized -> Mxfp4::validate (engine/src/mxfp4.rs:11-25)
         if (rows == 0 || cols == 0 || cols % 32)
             return fmt_error("MXFP4 requires nonempty rows with a width divisible by 32");
-        if (kv.second.bytes.size() != rows * cols / 2 || sc->second.bytes.size() != rows * cols / 32)
+        if (kv.second.at.bytes != rows * cols / 2 || sc->second.bytes.size() != rows * cols / 32)
             return fmt_error("MXFP4 data length does not match shape");
         if (std::find(sc->second.bytes.begin(), sc->second.bytes.end(), 255) != sc->second.bytes.end())
             return fmt_error("MXFP4 checkpoint contains a NaN scale");
         if (tensors.count(kv.first)) return fmt_error("duplicate tensor");
-        HostTensor t;
+        IndexTensor t;
         t.name = kv.first;
         t.dtype = JL_MXFP4;
         t.shape = {rows, cols};
-        t.packed = std::move(kv.second.bytes);
+        t.data = kv.second.at;
         t.scales = std::move(sc->second.bytes);
         tensors.emplace(kv.first, std::move(t));
         scales.erase(sc);
     }
     if (!scales.empty()) return fmt_error("MXFP4 scales have no matching packed weights");
+    return JL_OK;
+}
+
+jl_status read_range(const FileRange& r, void* dst, size_t offset, size_t bytes) {
+    if (offset > r.bytes || bytes > r.bytes - offset) {
+        set_error("read past the end of a tensor in %s", r.path.c_str());
+        return JL_ERR_INVALID_ARG;
+    }
+    FILE* f = fopen(r.path.c_str(), "rb");
+    if (!f) {
+        set_error("cannot open %s", r.path.c_str());
+        return JL_ERR_IO;
+    }
+    std::unique_ptr<FILE, int (*)(FILE*)> guard(f, fclose);
+    if (fseeko(f, (off_t)(r.offset + offset), SEEK_SET) != 0 ||
+        (bytes && fread(dst, 1, bytes, f) != bytes)) {
+        set_error("short read in %s", r.path.c_str());
+        return JL_ERR_IO;
+    }
+    return JL_OK;
+}
+
+jl_status load_weights(const std::string& dir, jl_weights* out) {
+    // engine/src/lib.rs:85-202: the whole checkpoint in host memory.
+    WeightIndex idx;
+    JL_TRY(scan_weights(dir, &idx));
+    for (auto& kv : idx.tensors) {
+        IndexTensor& it = kv.second;
+        HostTensor t;
+        t.name = it.name;
+        t.dtype = it.dtype;
+        t.shape = it.shape;
+        std::vector<uint8_t> bytes(it.data.bytes);
+        JL_TRY(read_range(it.data, bytes.data(), 0, bytes.size()));
+        if (it.dtype == JL_MXFP4) {
+            t.packed = std::move(bytes);
+            t.scales = std::move(it.scales);
+        } else {
+            t.bf16.resize(bytes.size() / 2);
+            for (size_t i = 0; i < t.bf16.size(); ++i)
+                t.bf16[i] = (uint16_t)(bytes[2 * i] | (bytes[2 * i + 1] << 8));
+        }
+        out->tensors.emplace(kv.first, std::move(t));
+    }
     return JL_OK;
 }
 
