@@ -237,6 +237,17 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
     ptx::grid_dependency_wait();
     ptx::launch_dependents();
     const int rows = min(a.hdr->rows, a.mcap);
+    // residual add: the x values lane 0 of this warp adds to, read now so the
+    // load overlaps the input load and the dot products (only this CTA
+    // writes these rows of x)
+    float xold[TR / 8][M];
+#pragma unroll
+    for (int h = 0; h < TR / 8; ++h)
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+            xold[h][m] = EPI == DEC_ADD && lane == 0 && warp + 8 * h < n && m < rows
+                             ? a.y[(size_t)m * a.ldy + r0 + warp + 8 * h]
+                             : 0.f;
     dec_load_x(a.x, K, M, K, a.norm, wv, xs4, red);
     const bool ok = ptx::mbar_wait(&bar, 0, DEC_WAIT);
     __syncthreads();
@@ -297,7 +308,7 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
                     if (m < rows) {
                         float* d = a.y + (size_t)m * a.ldy + r0 + r;
                         const float v = __fdiv_rn(o[h][m], rms[m]);
-                        *d = EPI == DEC_ADD ? __fadd_rn(*d, v) : v;  // residual (model.rs:178-186)
+                        *d = EPI == DEC_ADD ? __fadd_rn(xold[h][m], v) : v;  // residual (model.rs:178-186)
                     }
             }
     }
