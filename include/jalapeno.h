@@ -99,7 +99,11 @@ void jl_model_options_default(jl_model_options* o);
 /* Loads config.json (num_hidden_layers, max_position_embeddings,
  * eos_token_id) and every .safetensors file of `dir`, uploads to the GPU.  bf16 and MXFP4
  * tensors may be mixed; a tied lm_head (absent or equal to the embedding
- * table) is stored once.  opts may be NULL. */
+ * table) is stored once.  Every header is checked before any payload is
+ * read (the checks and messages of jl_weights_load); payloads then go from
+ * the files to the device through two 16 MB pinned buffers, so host memory
+ * never holds the checkpoint.  opts may be NULL.
+ * Replaces Model::load (engine/src/model.rs:55-57). */
 jl_status jl_model_load(const char* dir, const jl_model_options* opts, jl_model** out);
 
 /* Architecture of a seeded synthetic model (no file I/O): the same tensors a
