@@ -54,6 +54,15 @@ def expect_error(tmp_path, match, status=J.JL_ERR_FORMAT):
         J.load(tmp_path)
     assert e.value.status == status, e.value
     assert match in e.value.message, e.value.message
+    # Model::load checks every header before it reads a payload or touches a
+    # GPU: the same status and message, here without a device
+    cfg = tmp_path / "config.json"
+    if not cfg.exists():
+        cfg.write_text(json.dumps({"num_hidden_layers": 1, "max_position_embeddings": 64,
+                                   "eos_token_id": 0}))
+    with pytest.raises(J.JlError) as m:
+        J.Model.load(tmp_path)
+    assert (m.value.status, m.value.message) == (e.value.status, e.value.message)
 
 
 def entry(dtype, shape, start, end):
