@@ -921,7 +921,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
                 }
             }
         }
-        __syncthreads();  // the window is free for the next copy
+        if (w0 + ATT_WIN < w_hi) __syncthreads();  // the window is free for the next copy (uniform)
     }
     if (!ok && threadIdx.x == 0) atomicOr(kv.err, 4);  // a page copy did not arrive in time
     // merge the head's warps in warp order
