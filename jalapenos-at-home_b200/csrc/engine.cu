@@ -403,8 +403,17 @@ jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head) {
 }
 
 
-jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool all,
-                  uint32_t* out_ids, float* out_logits, bool draft_step) {
+// predict(), except that the last pass's predicted ids (and logits) are left
+// in flight on m->stream: predict_finish() waits for them.  Two models'
+// prompts started this way run on their own streams at the same time.
+struct PendingIds {
+    uint32_t* dst = nullptr;
+    size_t count = 0;
+};
+
+jl_status predict_start(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool all,
+                        uint32_t* out_ids, float* out_logits, bool draft_step, PendingIds* pend) {
+    *pend = PendingIds{};
     if (n == 0 || c->len + n > (size_t)m->max_positions) {  // model.rs:212
         set_error("predict needs 1..%zu tokens, got %zu", (size_t)m->max_positions - c->len, n);
         return JL_ERR_INVALID_ARG;
@@ -447,14 +456,32 @@ jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool 
                 JL_CUDA(cudaMemcpyAsync(out_logits + first * m->vocab, m->s.logits + out_at * m->vocab,
                                         (size_t)head_rows * m->vocab * sizeof(float),
                                         cudaMemcpyDeviceToHost, m->stream));
-            JL_CUDA(cudaStreamSynchronize(m->stream));
-            memcpy(out_ids + first, m->host_out, head_rows * sizeof(uint32_t));
+            if (last) {
+                pend->dst = out_ids + first;
+                pend->count = (size_t)head_rows;
+            } else {
+                JL_CUDA(cudaStreamSynchronize(m->stream));
+                memcpy(out_ids + first, m->host_out, head_rows * sizeof(uint32_t));
+            }
         }
         c->len += take;
         done += take;
     }
+    return JL_OK;
+}
+
+jl_status predict_finish(jl_model* m, const PendingIds& p) {
+    JL_CUDA(cudaSetDevice(m->device));
     JL_CUDA(cudaStreamSynchronize(m->stream));
+    if (p.count) memcpy(p.dst, m->host_out, p.count * sizeof(uint32_t));
     return check_device_flag(m);
+}
+
+jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool all,
+                  uint32_t* out_ids, float* out_logits, bool draft_step) {
+    PendingIds p;
+    JL_TRY(predict_start(m, c, ids, n, all, out_ids, out_logits, draft_step, &p));
+    return predict_finish(m, p);
 }
 
 jl_status time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t rows, size_t reps,
@@ -1037,12 +1064,18 @@ jl_status generate_speculative(jl_model* T, jl_model* D, const uint32_t* prompt,
     JL_TRY(cache_create(D, &dc));
     std::unique_ptr<jl_cache, void (*)(jl_cache*)> g2(dc, cache_free);
     cudaStream_t st = T->stream;
-    // prefill both models (speculative.rs:69-75)
+    // prefill both models (speculative.rs:69-75), each on its own stream, at
+    // the same time; the target's stream then waits for the draft's
     JL_CUDA(cudaEventRecord(T->ev0, st));
     uint32_t first = 0, dnext = 0;
-    JL_TRY(predict(T, tc, prompt, n, false, &first, nullptr));
-    JL_TRY(predict(D, dc, prompt, n, false, &dnext, nullptr));
+    PendingIds pt, pd;
+    JL_TRY(predict_start(T, tc, prompt, n, false, &first, nullptr, false, &pt));
+    JL_TRY(predict_start(D, dc, prompt, n, false, &dnext, nullptr, false, &pd));
+    JL_CUDA(cudaEventRecord(D->ev0, D->stream));
+    JL_CUDA(cudaStreamWaitEvent(st, D->ev0, 0));
     JL_CUDA(cudaEventRecord(T->ev1, st));
+    JL_TRY(predict_finish(T, pt));
+    JL_TRY(predict_finish(D, pd));
     JL_CUDA(cudaEventSynchronize(T->ev1));
     r->prefill_ms = elapsed_ms(T->ev0, T->ev1);
     r->prefill_passes = 2;
