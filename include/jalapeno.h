@@ -4,8 +4,7 @@
  * This ABI replaces the reference engine crate's public Rust API
  * (fawwaz46/jalapenos-at-home, engine/src/lib.rs:16-21) and its native GPU
  * bridge (engine/src/gpu.rs:19-42 -> engine/src/gpu.m:21-128).  Each entry
- * point names the reference item it stands in for.  A Rust binding a
- * maintainer would add is shown in INTEGRATION.md.
+ * point names the reference item it stands in for.
  *
  * Conventions
  *  - Every call returns jl_status; JL_OK is 0.  On failure,
@@ -249,7 +248,9 @@ jl_status jl_project(jl_model* m, int layer, jl_projection which, const float* x
  * comes from one fixed 4 MiB device array per device (no allocation of any
  * kind); a projection whose scratch would exceed it is rejected with
  * JL_ERR_INVALID_ARG.  Calls share that array, so calls that overlap on
- * the GPU race.  The first call on a device looks up the array's address.
+ * the GPU race.  Creating or loading a model on a device sets the array up
+ * (module load, address lookup, a pinned flag word), so no call loads or
+ * allocates anything.
  * Returns after the projection has finished (the stream is synchronised). */
 jl_status jl_project_noalloc(jl_model* m, int layer, jl_projection which, const float* x,
                              size_t rows, float* y, void* stream);

@@ -435,6 +435,9 @@ jl_status mx_project_with(const MxProj& p, int epi, const PassHdr* hdr, int mcap
                           cudaStream_t stream);
 jl_status project_noalloc(jl_model* m, int layer, int which, const float* x, size_t rows, float* y,
                           cudaStream_t stream);
+// Loads project_noalloc's module, array and kernels on the current device
+// and pins its host flag word, so that no call of it loads or allocates.
+jl_status noalloc_prepare(int device);
 // Builds the tensor-core copies of every MXFP4 projection of `m` (model.cu).
 jl_status build_mx(jl_model* m);
 jl_status launch_fill_u16(uint16_t* out, size_t n, uint16_t value, cudaStream_t stream);

@@ -1052,6 +1052,8 @@ jl_status mx_configure() {
     JL_TRY((configure_mx<MX_SWIGLU, KIND_MX>()));
     JL_TRY((configure_mx<MX_QKV, KIND_MX>()));
     JL_TRY((configure_mx<MX_HEAD, KIND_BF>()));
+    cudaFuncAttributes fa;  // loads the piece encoder now rather than at its first launch
+    JL_CUDA(cudaFuncGetAttributes(&fa, k_mx_pieces));
     int dev = 0, sms = 0;
     JL_CUDA(cudaGetDevice(&dev));
     JL_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

@@ -16,6 +16,12 @@
 // the error flag (the only parts read before they are written) at the start
 // of every call.  Calls whose work overlaps on the GPU (different streams,
 // different host threads) race on the array.
+//
+// CUDA loads a module, with its __device__ arrays, and each kernel lazily,
+// at first use (CUDA_MODULE_LOADING=LAZY, the default since 12.2).  So the
+// array's address, this file's kernels and the pinned host word the error
+// flag is read into are all set up by noalloc_prepare, which model creation
+// runs once per device: a call itself loads and allocates nothing.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -38,6 +44,7 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES
 struct DeviceScratch {
     std::once_flag once;
     uint8_t* ptr = nullptr;
+    int* host_flag = nullptr;  // pinned word the error flag is copied into
     cudaError_t err = cudaSuccess;
 };
 DeviceScratch g_devices[MAX_DEVICES];
@@ -53,9 +60,11 @@ __global__ void k_noalloc_begin(PassHdr* hdr, int rows, int* err, int* tickets, 
     if (i < n_tickets) tickets[i] = 0;
 }
 
-// The device address of g_noalloc_scratch on `device` (which is current),
-// looked up once per device.
-jl_status scratch_for(int device, uint8_t** out) {
+// The device address of g_noalloc_scratch on `device` (which is current)
+// and the pinned word its error flag is read into, set up once per device:
+// the address lookup loads this file's module (and with it the array), and
+// the attribute query loads the setup kernel.
+jl_status scratch_for(int device, uint8_t** out, int** host_flag) {
     if (device < 0 || device >= MAX_DEVICES) {
         set_error("project_noalloc: device %d out of range", device);
         return JL_ERR_INVALID_ARG;
@@ -65,13 +74,17 @@ jl_status scratch_for(int device, uint8_t** out) {
         void* p = nullptr;
         d.err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         d.ptr = (uint8_t*)p;
+        cudaFuncAttributes fa;
+        if (d.err == cudaSuccess) d.err = cudaFuncGetAttributes(&fa, k_noalloc_begin);
+        if (d.err == cudaSuccess) d.err = cudaMallocHost(&d.host_flag, sizeof(int));
+        if (d.err != cudaSuccess) cudaGetLastError();
     });
-    if (d.err != cudaSuccess || !d.ptr) {
-        set_error("project_noalloc: cudaGetSymbolAddress failed on device %d: %s", device,
-                  cudaGetErrorString(d.err));
+    if (d.err != cudaSuccess || !d.ptr || !d.host_flag) {
+        set_error("project_noalloc: set-up failed on device %d: %s", device, cudaGetErrorString(d.err));
         return JL_ERR_CUDA;
     }
     *out = d.ptr;
+    if (host_flag) *host_flag = d.host_flag;
     return JL_OK;
 }
 
@@ -83,6 +96,11 @@ struct DeviceRestore {
 };
 
 }  // namespace
+
+jl_status noalloc_prepare(int device) {
+    uint8_t* p = nullptr;
+    return scratch_for(device, &p, nullptr);
+}
 
 jl_status project_noalloc(jl_model* m, int layer, int which, const float* x, size_t rows, float* y,
                           cudaStream_t stream) {
@@ -120,7 +138,8 @@ jl_status project_noalloc(jl_model* m, int layer, int which, const float* x, siz
     JL_CUDA(cudaGetDevice(&restore.prev));
     JL_CUDA(cudaSetDevice(m->device));
     uint8_t* base = nullptr;
-    JL_TRY(scratch_for(m->device, &base));
+    int* host_flag = nullptr;
+    JL_TRY(scratch_for(m->device, &base, &host_flag));
     PassHdr* hdr = (PassHdr*)base;
     int* err = (int*)(base + 64);
     uint8_t* scratch = base + NOALLOC_HEADER_BYTES;
@@ -128,9 +147,11 @@ jl_status project_noalloc(jl_model* m, int layer, int which, const float* x, siz
     k_noalloc_begin<<<(p->T + 255) / 256, 256, 0, st>>>(hdr, (int)rows, err, (int*)scratch, p->T);
     JL_CUDA(cudaGetLastError());
     JL_TRY(mx_project_with(*p, epi, hdr, (int)rows, x, win, y, wout, scratch, err, m->sms, st));
+    // the flag comes back on the caller's stream into the pinned word: no
+    // copy on the legacy default stream, which would wait for other streams
+    JL_CUDA(cudaMemcpyAsync(host_flag, err, sizeof(int), cudaMemcpyDeviceToHost, st));
     JL_CUDA(cudaStreamSynchronize(st));
-    int flag = 0;
-    JL_CUDA(cudaMemcpy(&flag, err, sizeof flag, cudaMemcpyDeviceToHost));
+    const int flag = *host_flag;
     if (flag) {
         set_error("project_noalloc: a device-side wait timed out (flag %d)", flag);
         return JL_ERR_TIMEOUT;

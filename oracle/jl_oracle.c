@@ -314,43 +314,97 @@ static int cache_reserve(jlo_cache* c, size_t tokens) {
 
 /* ---- building blocks ----------------------------------------------- */
 
+/* Signed E2M1 level of each nibble of a byte: [byte][0] the low nibble (the
+ * even element), [byte][1] the high one. */
+static float g_pair_levels[256][2];
+static int g_pair_ready = 0;
+
+static void pair_levels_init(void) {
+    if (g_pair_ready) return;
+#pragma omp critical(jlo_pair_levels)
+    if (!g_pair_ready) {
+        for (int b = 0; b < 256; ++b)
+            for (int h = 0; h < 2; ++h) {
+                unsigned code = (unsigned)(b >> (4 * h)) & 15u;
+                g_pair_levels[b][h] = (code & 8) ? -LEVELS[code & 7] : LEVELS[code & 7];
+            }
+        g_pair_ready = 1;
+    }
+}
+
+static void decode_row(const matrix_t* w, int r, float* wrow) {
+    /* mxfp4.rs:35-49 for one row.  A level times a power-of-two scale is the
+     * same number whichever sign is applied first (round to nearest even is
+     * symmetric), so the signed table gives Mxfp4::values' exact values. */
+    const int K = w->cols;
+    if (w->kind == JLO_MXFP4) {
+        const uint8_t* p = w->packed + (size_t)r * (K / 2);
+        const uint8_t* sc = w->scales + (size_t)r * (K / 32);
+        for (int b = 0; b < K / 32; ++b) {
+            const float scale = ldexpf(1.0f, (int)sc[b] - 127);
+            for (int j = 0; j < 16; ++j) {
+                const uint8_t byte = p[b * 16 + j];
+                wrow[b * 32 + 2 * j] = g_pair_levels[byte][0] * scale;
+                wrow[b * 32 + 2 * j + 1] = g_pair_levels[byte][1] * scale;
+            }
+        }
+    } else {
+        const uint16_t* src = w->bf16 + (size_t)r * K;
+        for (int i = 0; i < K; ++i) {
+            uint32_t u = (uint32_t)src[i] << 16;
+            memcpy(&wrow[i], &u, 4);
+        }
+    }
+}
+
 static void matmul_rows(const matrix_t* w, const float* x, size_t rows, float* y) {
     /* lib.rs:240-266: each sum starts at 0.0 and adds x*w in order of i.
-     * The weight row is decoded once (Mxfp4::values gives the same exact
-     * values as Mxfp4::value) and up to 8 token rows are summed side by side;
-     * every sum still accumulates in index order, so results are identical
+     * A weight row is decoded once (Mxfp4::values gives the same exact
+     * values as Mxfp4::value).  One token row: four weight rows are summed
+     * side by side; several token rows: up to 8 token rows side by side.
+     * Every sum still accumulates in index order, so results are identical
      * to the one-row-at-a-time loop. */
     const int K = w->cols, O = w->rows;
+    pair_levels_init();
 #pragma omp parallel
     {
-        float* wrow = (float*)malloc((size_t)K * sizeof(float));
+        float* wrow = (float*)malloc((size_t)4 * K * sizeof(float));
+        if (rows == 1) {
 #pragma omp for schedule(static)
-        for (int r = 0; r < O; ++r) {
-            if (w->kind == JLO_MXFP4) {
-                jlo_mxfp4_values(w->packed, w->scales, (size_t)r * K, (size_t)r * K + K, wrow);
-            } else {
-                const uint16_t* src = w->bf16 + (size_t)r * K;
+            for (int r0 = 0; r0 < O; r0 += 4) {
+                const int nr = O - r0 < 4 ? O - r0 : 4;
+                for (int j = 0; j < nr; ++j) decode_row(w, r0 + j, wrow + (size_t)j * K);
+                for (int j = nr; j < 4; ++j) memcpy(wrow + (size_t)j * K, wrow, (size_t)K * sizeof(float));
+                const float* w0 = wrow;
+                const float* w1 = wrow + K;
+                const float* w2 = wrow + 2 * (size_t)K;
+                const float* w3 = wrow + 3 * (size_t)K;
+                float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
                 for (int i = 0; i < K; ++i) {
-                    uint32_t u = (uint32_t)src[i] << 16;
-                    memcpy(&wrow[i], &u, 4);
+                    const float xi = x[i];
+                    s0 += xi * w0[i];
+                    s1 += xi * w1[i];
+                    s2 += xi * w2[i];
+                    s3 += xi * w3[i];
                 }
+                const float s[4] = {s0, s1, s2, s3};
+                for (int j = 0; j < nr; ++j) y[r0 + j] = s[j];
             }
-            if (rows == 1) {
-                float sum = 0.0f;
-                for (int i = 0; i < K; ++i) sum += x[i] * wrow[i];
-                y[r] = sum;
-                continue;
-            }
-            for (size_t t0 = 0; t0 < rows; t0 += 8) {
-                const size_t nt = rows - t0 < 8 ? rows - t0 : 8;
-                float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                const float* xt[8];
-                for (size_t j = 0; j < 8; ++j) xt[j] = x + (t0 + (j < nt ? j : 0)) * (size_t)K;
-                for (int i = 0; i < K; ++i) {
-                    const float wi = wrow[i];
-                    for (size_t j = 0; j < 8; ++j) sum[j] += xt[j][i] * wi;
+        } else {
+#pragma omp for schedule(static)
+            for (int r = 0; r < O; ++r) {
+                decode_row(w, r, wrow);
+                for (size_t t0 = 0; t0 < rows; t0 += 8) {
+                    const size_t nt = rows - t0 < 8 ? rows - t0 : 8;
+                    float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    const float* xt[8];
+                    for (size_t j = 0; j < 8; ++j) xt[j] = x + (t0 + (j < nt ? j : 0)) * (size_t)K;
+                    for (int i = 0; i < K; ++i) {
+                        const float wi = wrow[i];
+                        for (size_t j = 0; j < 8; ++j) sum[j] += xt[j][i] * wi;
+                    }
+                    for (size_t j = 0; j < nt; ++j) y[(t0 + j) * (size_t)O + r] = sum[j];
                 }
-                for (size_t j = 0; j < nt; ++j) y[(t0 + j) * (size_t)O + r] = sum[j];
             }
         }
         free(wrow);
@@ -435,9 +489,8 @@ static int attention(const jlo_model* m, jlo_cache* cache, int l, const float* x
     float* k = (float*)malloc(rows * kv_len * sizeof(float));
     float* v = (float*)malloc(rows * kv_len * sizeof(float));
     float* mixed = (float*)calloc(rows * q_len, sizeof(float));
-    float* scores = (float*)malloc((offset + rows) * sizeof(float));
-    if (!q || !k || !v || !mixed || !scores) {
-        free(q); free(k); free(v); free(mixed); free(scores);
+    if (!q || !k || !v || !mixed) {
+        free(q); free(k); free(v); free(mixed);
         return -2;
     }
     matmul_rows(&L->proj[JLO_Q], x, rows, q); /* :353-355 */
@@ -457,8 +510,22 @@ static int attention(const jlo_model* m, jlo_cache* cache, int l, const float* x
     }
     const int group = m->q_heads / m->kv_heads;           /* :397 */
     const float scale = sqrtf((float)HEAD_DIM);           /* :398 */
-    for (size_t t = 0; t < rows; ++t) {
-        for (int h = 0; h < m->q_heads; ++h) {
+    /* every (row, head) pair is independent: threads take whole pairs, each
+     * computed in the reference's order */
+    const long pairs = (long)rows * m->q_heads;
+    int fail = 0;
+#pragma omp parallel
+    {
+        float* sc = (float*)malloc((offset + rows) * sizeof(float));
+        if (!sc) {
+#pragma omp atomic write
+            fail = 1;
+        }
+#pragma omp for schedule(dynamic, 1)
+        for (long p = 0; p < pairs; ++p) {
+            if (!sc) continue;
+            const size_t t = (size_t)(p / m->q_heads);
+            const int h = (int)(p % m->q_heads);
             int kv_h = h / group;
             const float* qh = q + t * q_len + (size_t)h * HEAD_DIM;
             size_t visible = offset + t + 1;
@@ -466,26 +533,31 @@ static int attention(const jlo_model* m, jlo_cache* cache, int l, const float* x
                 const float* kh = K + s * kv_len + (size_t)kv_h * HEAD_DIM;
                 float dot = 0.0f;
                 for (int i = 0; i < HEAD_DIM; ++i) dot += qh[i] * kh[i];
-                scores[s] = dot / scale;
+                sc[s] = dot / scale;
             }
             float max = -INFINITY;                          /* :420-425 */
             for (size_t s = 0; s < visible; ++s)
-                if (scores[s] > max) max = scores[s];
+                if (sc[s] > max) max = sc[s];
             float total = 0.0f;                             /* :426-430 */
             for (size_t s = 0; s < visible; ++s) {
-                scores[s] = expf(scores[s] - max);
-                total += scores[s];
+                sc[s] = expf(sc[s] - max);
+                total += sc[s];
             }
             float* o = mixed + t * q_len + (size_t)h * HEAD_DIM;
             for (size_t s = 0; s < visible; ++s) {          /* :433-439 */
-                float share = scores[s] / total;
+                float share = sc[s] / total;
                 const float* vh = V + s * kv_len + (size_t)kv_h * HEAD_DIM;
                 for (int i = 0; i < HEAD_DIM; ++i) o[i] += share * vh[i];
             }
         }
+        free(sc);
+    }
+    if (fail) {
+        free(q); free(k); free(v); free(mixed);
+        return -2;
     }
     matmul_rows(&L->proj[JLO_O], mixed, rows, out); /* :444-449 */
-    free(q); free(k); free(v); free(mixed); free(scores);
+    free(q); free(k); free(v); free(mixed);
     return 0;
 }
 

@@ -91,3 +91,40 @@ def test_rejects_bf16_projection(torch_cuda):
     y = torch.zeros(1, cfg.hidden, device="cuda:0")
     with pytest.raises(J.JlError, match="not MXFP4"):
         m.project_noalloc(0, J.PROJ_O, x.data_ptr(), 1, y.data_ptr())
+
+
+FIRST_CALL = r"""
+import sys
+sys.path[:0] = {paths!r}
+import numpy as np
+import torch
+import jalapeno as J
+import oracle as O
+cfg = O.PRESETS["tiny-untied"]
+m = J.Model.synthesize(cfg.layers, cfg.hidden, cfg.q_heads, cfg.kv_heads, cfg.inter, cfg.vocab,
+                       cfg.tied, seed=3, mxfp4=True, mxfp4_embed=True,
+                       max_positions=cfg.max_positions, eos=cfg.eos)
+x = torch.randn(2, cfg.hidden, device="cuda:0")
+y = torch.empty(2, cfg.inter, device="cuda:0")
+torch.cuda.synchronize()
+before = torch.cuda.mem_get_info(0)[0]
+m.project_noalloc(0, J.PROJ_GATE_UP, x.data_ptr(), 2, y.data_ptr())
+after = torch.cuda.mem_get_info(0)[0]
+print("free bytes", before, after)
+assert after == before, f"the first call changed free device memory by {{before - after}} bytes"
+"""
+
+
+def test_first_call_allocates_no_device_memory(torch_cuda):
+    """The library sets the fixed array up when a model is created, not on
+    the first call: in a fresh process, the device's free memory is the same
+    before and after the first call."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parents[1]
+    paths = [str(repo / "jalapenos-at-home_b200"), str(repo / "oracle")]
+    r = subprocess.run([sys.executable, "-c", FIRST_CALL.format(paths=paths)], capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
