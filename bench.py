@@ -56,7 +56,6 @@ def parse():
     ap.add_argument("--p", type=float, default=0.25, help="oracle-draft replacement probability")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--profile", action="store_true",
                     help="small run for ncu: one k+1-row target pass and one draft pass "
                          "(Model::time_pass), no timing loop")
@@ -108,11 +107,11 @@ class Dist:
     The process group is NCCL over the GPUs, or gloo on host cores when
     JL_DIST_BACKEND=gloo (the multi-process tests, which have no GPU)."""
 
-    def __init__(self):
+    def __init__(self, backend: str | None = None, timeout_s: int = 300):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
-        self.backend = os.environ.get("JL_DIST_BACKEND", "nccl")
+        self.backend = backend or os.environ.get("JL_DIST_BACKEND", "nccl")
         self.pg = None
         if self.world > 1:
             import datetime
@@ -120,7 +119,7 @@ class Dist:
             import torch
             import torch.distributed as dist
 
-            timeout = datetime.timedelta(seconds=300)
+            timeout = datetime.timedelta(seconds=timeout_s)
             if self.backend == "nccl":
                 torch.cuda.set_device(self.local)
                 dist.init_process_group("nccl", timeout=timeout, device_id=torch.device("cuda", self.local))
@@ -224,75 +223,138 @@ def make_models(J, device: int):
     return target, draft
 
 
-def cpu_baseline(J, O, target, draft, prompt, greedy, args, budget_s):
-    """The reference's CPU path (the oracle's restatement of engine/src/lib.rs
-    and speculative.rs) on this host's cores, same models and workload, timed
-    on a bounded number of decode rounds after prefill."""
+def oracle_from_device(O, gpu_model, preset, mxfp4):
+    """An oracle model holding the GPU model's own weights (read back from the
+    device; a few seconds instead of synthesizing on the host)."""
     import numpy as np
 
-    def oracle_model(gpu_model, preset, mxfp4):
-        cfg = O.Config(preset, **PRESETS[preset], max_positions=40960, eos=151645)
-        tensors = {}
+    cfg = O.Config(preset, **PRESETS[preset], max_positions=40960, eos=151645)
+    tensors = {}
 
-        def mat(name, rows, cols, q):
-            if q:
-                raw = gpu_model.read_tensor(name, rows * cols // 2 + rows * cols // 32)
-                return O.Matrix(rows, cols, packed=raw[: rows * cols // 2].copy(),
-                                scales=raw[rows * cols // 2:].copy())
-            raw = gpu_model.read_tensor(name, rows * cols * 2)
-            return O.Matrix(rows, cols, bf16=raw.view(np.uint16).copy())
+    def mat(name, rows, cols, q):
+        if q:
+            raw = gpu_model.read_tensor(name, rows * cols // 2 + rows * cols // 32)
+            return O.Matrix(rows, cols, packed=raw[: rows * cols // 2].copy(),
+                            scales=raw[rows * cols // 2:].copy())
+        raw = gpu_model.read_tensor(name, rows * cols * 2)
+        return O.Matrix(rows, cols, bf16=raw.view(np.uint16).copy())
 
-        tensors["embed"] = mat("model.embed_tokens.weight", cfg.vocab, cfg.hidden, False)
-        tensors["lm_head"] = None if cfg.tied else mat("lm_head.weight", cfg.vocab, cfg.hidden, False)
-        tensors["norm"] = np.full(cfg.hidden, O.ONE_BF16, np.uint16)
-        for layer in range(cfg.layers):
-            for p in O.PROJECTIONS:
-                shape = O.shape_of(cfg, p)
-                tensors[f"{layer}.{p}"] = mat(f"model.layers.{layer}.{O.HF_NAMES[p]}", shape[0],
-                                              shape[1], mxfp4)
-            for n in O.NORM_CODE:
-                tensors[f"{layer}.{n}"] = np.full(O.shape_of(cfg, n)[0], O.ONE_BF16, np.uint16)
-        return O.Model(cfg, tensors)
+    tensors["embed"] = mat("model.embed_tokens.weight", cfg.vocab, cfg.hidden, False)
+    tensors["lm_head"] = None if cfg.tied else mat("lm_head.weight", cfg.vocab, cfg.hidden, False)
+    tensors["norm"] = np.full(cfg.hidden, O.ONE_BF16, np.uint16)
+    for layer in range(cfg.layers):
+        for p in O.PROJECTIONS:
+            shape = O.shape_of(cfg, p)
+            tensors[f"{layer}.{p}"] = mat(f"model.layers.{layer}.{O.HF_NAMES[p]}", shape[0], shape[1],
+                                          mxfp4)
+        for n in O.NORM_CODE:
+            tensors[f"{layer}.{n}"] = np.full(O.shape_of(cfg, n)[0], O.ONE_BF16, np.uint16)
+    return O.Model(cfg, tensors)
 
-    t_ref = oracle_model(target, "qwen3-8b", True)
-    d_ref = oracle_model(draft, "qwen3-0.6b", True)
-    res = O.generate_scheduled(t_ref, d_ref, prompt, args.new, O.DraftSchedule.fixed(args.gamma),
-                               round_bf16=True, oracle_stream=greedy, oracle_p=args.p,
-                               oracle_seed=5, max_seconds=budget_s)
-    new = len(res.tokens) - len(prompt)
-    return {"value": new / (res.decode_s if res.decode_s > 0 else float("nan")), "unit": "tok/s",
-            "cores": O.threads(), "kind": "port",
-            "sample": (f"oracle spec decode of the same workload (8B MXFP4 + 0.6B MXFP4, k={args.gamma}, "
-                       f"p={args.p}) on {O.threads()} threads: {res.rounds} rounds, {new} tokens in "
-                       f"{res.decode_s:.1f} s after an untimed prefill")}
+
+class OracleSample:
+    """The oracle's restatement of the reference's CPU path
+    (engine/src/lib.rs, model.rs, speculative.rs) on the host cores, for the
+    benchmark workload: both models prefilled once (untimed), then each
+    sample decodes `rounds` speculative rounds from that state (the caches
+    rolled back to the prompt), timed on the host clock.  The bf16-rounding
+    KV cache matches the GPU's bf16 cache."""
+
+    def __init__(self, O, t_ref, d_ref, prompt, stream, args, rounds=3):
+        self.O, self.t_ref, self.d_ref, self.prompt, self.stream = O, t_ref, d_ref, prompt, stream
+        self.args, self.rounds = args, rounds
+        self.tc, self.dc = t_ref.cache(True), d_ref.cache(True)
+        self.t_first = t_ref.predict(prompt, self.tc)[0]
+        self.d_first = d_ref.predict(prompt, self.dc)[0]
+
+    def run(self):
+        self.tc.truncate(len(self.prompt))
+        self.dc.truncate(len(self.prompt))
+        res = self.O.generate_scheduled(
+            self.t_ref, self.d_ref, self.prompt, self.args.new, self.O.DraftSchedule.fixed(self.args.gamma),
+            round_bf16=True, oracle_stream=self.stream, oracle_p=self.args.p, oracle_seed=5,
+            max_rounds=self.rounds, prefilled=(self.tc, self.dc, self.t_first, self.d_first))
+        new = len(res.tokens) - len(self.prompt)
+        return res, new / res.decode_s
+
+    def describe(self, res, threads):
+        new = len(res.tokens) - len(self.prompt)
+        return (f"oracle spec decode of the same workload (8B MXFP4 + 0.6B MXFP4, k={self.args.gamma}, "
+                f"p={self.args.p}, bf16-rounded KV) on {threads} threads: {res.rounds} rounds, {new} "
+                f"tokens in {res.decode_s:.2f} s after an untimed prefill")
+
+
+def cpu_baseline(O, target, draft, prompt, greedy, args):
+    """cpu_baseline of the main line: the oracle port on this host's cores,
+    on the GPU models' own weights, timed on three speculative rounds after
+    an untimed prefill.  Its tokens are compared with the GPU stream."""
+    O.set_threads(physical_cores())
+    t_ref = oracle_from_device(O, target, "qwen3-8b", True)
+    d_ref = oracle_from_device(O, draft, "qwen3-0.6b", True)
+    sample = OracleSample(O, t_ref, d_ref, prompt, greedy, args)
+    res, value = sample.run()
+    match = res.tokens == greedy[: len(res.tokens)]
+    return {"value": value, "unit": "tok/s", "cores": O.threads(), "kind": "port",
+            "sample": sample.describe(res, O.threads()), "tokens_equal_gpu_stream": match}
+
+
+def physical_cores() -> int:
+    try:
+        import psutil
+
+        n = psutil.cpu_count(logical=False)
+        if n:
+            return int(n)
+    except ImportError:
+        pass
+    return os.cpu_count() or 1
 
 
 def run_reference(args, dist):
-    """--impl reference: the reference's CPU implementation of this path (its
-    Rust engine does not build here; the oracle restates it), on host cores."""
-    if dist.rank != 0:
-        return
-    import jalapeno as J
+    """--impl reference: the reference's CPU implementation of this path on
+    the host cores.  Its Rust engine does not build here (no cargo; its GPU
+    path is Metal), so the oracle's restatement of it runs: weights
+    synthesized on the host (the same seeded tensors the GPU synthesizes),
+    the oracle-draft stream from the oracle's own greedy decode, every
+    physical core.  Nothing of this repository's GPU engine is loaded.
+    One speculative generation of the workload (64 new tokens) after an
+    untimed prefill: its first min(W, 3) rounds are the warm-up, the next up
+    to K rounds (at least 3) are timed.  Rank 0 measures; other ranks wait at
+    a host barrier."""
     import oracle as O
 
-    target, draft = make_models(J, dist.local)
-    prompt = O.prompt_ids(args.prompt, 151936, 2)
-    greedy = target.generate(prompt, args.new)
-    samples = []
-    for step in range(args.warmup + args.steps):
-        budget = max(args.cpu_seconds / max(args.steps + args.warmup, 1), 5.0)
-        cb = cpu_baseline(J, O, target, draft, prompt, greedy, args, budget)
-        if step >= args.warmup:
-            samples.append(cb)
-    value = statistics.median(s["value"] for s in samples)
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": workload_config(args),
-            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": samples[0]["cores"],
-                             "kind": "port", "sample": samples[0]["sample"]},
-            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    if dist.rank == 0:
+        threads = physical_cores()
+        O.set_threads(threads)
+        t_ref = O.Model.synthetic("qwen3-8b", 0, mxfp4=True)
+        d_ref = O.Model.synthetic("qwen3-0.6b", 1, mxfp4=True)
+        prompt = O.prompt_ids(args.prompt, 151936, 2)
+        stream = t_ref.generate(prompt, args.new, round_bf16=True)
+        warm = min(args.warmup, 3)
+        tc, dc = t_ref.cache(True), d_ref.cache(True)
+        first = (t_ref.predict(prompt, tc)[0], d_ref.predict(prompt, dc)[0])
+        res = O.generate_scheduled(t_ref, d_ref, prompt, args.new, O.DraftSchedule.fixed(args.gamma),
+                                   round_bf16=True, oracle_stream=stream, oracle_p=args.p, oracle_seed=5,
+                                   max_rounds=warm + args.steps, prefilled=(tc, dc, *first))
+        marks = [(0.0, len(prompt))] + res.round_marks
+        warm = min(warm, max(0, len(marks) - 4))  # at least 3 timed rounds
+        (ta, na), (tb, nb) = marks[warm], marks[-1]
+        timed_rounds = len(marks) - 1 - warm
+        value = (nb - na) / (tb - ta)
+        sample = (f"oracle spec decode of the workload (8B MXFP4 + 0.6B MXFP4, k={args.gamma}, p={args.p}, "
+                  f"bf16-rounded KV) on {O.threads()} threads, one generation after an untimed prefill: "
+                  f"{warm} warm-up rounds, then {timed_rounds} timed rounds, {nb - na} tokens in {tb - ta:.2f} s; "
+                  f"oracle tokens equal to the oracle's own greedy stream: {res.tokens == stream[: len(res.tokens)]}")
+        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32 activations, MXFP4 weights", "data": "synthetic (seeded, synthesized on the host)",
+                "config": workload_config(args),
+                "cpu_baseline": {"value": value, "unit": "tok/s", "cores": O.threads(), "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+    dist.barrier()
 
 
 def aggregate(dist, new_tokens: int, decode_ms: float, e2e_s: float):
@@ -378,11 +440,13 @@ def workload_config(args):
 
 def main():
     args = parse()
-    dist = Dist()
     if args.impl == "reference":
+        # host-only: a gloo barrier (other ranks wait while rank 0 measures)
+        dist = Dist(backend="gloo", timeout_s=3600)
         run_reference(args, dist)
         dist.close()
         return
+    dist = Dist()
     if args.profile:
         run_profile(args, dist)
         dist.close()
@@ -525,7 +589,7 @@ def main():
                 "drafted": r.drafted}
         line["sweep"] = sweep
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(J, O, target, draft, prompt, greedy, args, args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(O, target, draft, prompt, greedy, args)
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
     dist.close()

@@ -159,6 +159,15 @@ jl_status jl_cache_truncate(jl_cache* c, size_t len);
  * [rows_predicted, vocab] f32 logits. */
 jl_status jl_predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int all,
                      uint32_t* out_ids, float* out_logits);
+/* jl_predict for a speculative loop's draft step: n = 1 or 2 tokens,
+ * predicting after the last, through the kernels the loop's draft passes
+ * run (on a model whose layer projections are all MXFP4, CUDA-core
+ * projections with rounding of their own; otherwise the same pass as
+ * jl_predict).  Stands in for the draft's proposal passes of
+ * generate_scheduled (engine/src/speculative.rs:84-92, 136-138, which call
+ * Model::predict); it lets callers check those kernels' logits. */
+jl_status jl_predict_draft(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n,
+                           uint32_t* out_id, float* out_logits);
 /* Model::next_token (model.rs:203-205): predict after a fresh prompt. */
 jl_status jl_next_token(jl_model* m, const uint32_t* ids, size_t n, uint32_t* out_id);
 /* Model::hidden (model.rs:143-154): residual stream after `layers` layers

@@ -256,6 +256,14 @@ jl_status jl_predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, in
     JL_GUARD({ return predict(m, c, ids, n, all != 0, out_ids, out_logits); })
 }
 
+jl_status jl_predict_draft(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, uint32_t* out_id,
+                           float* out_logits) {
+    JL_NEED(m && c && ids && out_id, "model, cache, ids and out_id must be non-null");
+    JL_NEED(c->m == m, "this cache belongs to another model");
+    JL_NEED(n == 1 || n == 2, "a draft step takes 1 or 2 tokens");
+    JL_GUARD({ return predict(m, c, ids, n, false, out_id, out_logits, true); })
+}
+
 jl_status jl_next_token(jl_model* m, const uint32_t* ids, size_t n, uint32_t* out_id) {
     JL_NEED(m && ids && out_id, "model, ids and out_id must be non-null");
     JL_GUARD({

@@ -69,16 +69,23 @@ double elapsed_ms(cudaEvent_t a, cudaEvent_t b) {
 }
 
 // Kernels record impossible states (a page id outside the pool, a position
-// outside the RoPE table) in a device flag instead of touching memory out of
-// range; surface it once the stream is idle.
+// outside the RoPE table) and bounded waits that gave up in a device flag
+// instead of touching memory out of range or spinning forever; surface it
+// once the stream is idle.  Bits: 1 page id, 2 position, 4 a projection's
+// copy or split-K wait, 8 a fused draft step's wait.
 jl_status check_device_flag(jl_model* m) {
     int flag = 0;
     JL_CUDA(cudaMemcpy(&flag, m->counters, sizeof(int), cudaMemcpyDeviceToHost));
     if (flag) {
         JL_CUDA(cudaMemset(m->counters, 0, sizeof(int)));
-        set_error("kernel guard tripped (flags 0x%x): %s", flag,
-                  (flag & 1) ? "KV page id outside the pool" : "position outside the context");
-        return JL_ERR_CUDA;
+        if (flag & 3) {
+            set_error("kernel guard tripped (flags 0x%x): %s", flag,
+                      (flag & 1) ? "KV page id outside the pool" : "position outside the context");
+            return JL_ERR_CUDA;
+        }
+        set_error("a bounded device wait gave up (flags 0x%x): %s", flag,
+                  (flag & 8) ? "fused draft step" : "projection copy or split-K reduction");
+        return JL_ERR_TIMEOUT;
     }
     return JL_OK;
 }
@@ -634,8 +641,11 @@ jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters
 
 size_t pass_kernels(const jl_model* m, size_t rows, bool draft_step) {
     const size_t L = (size_t)m->layers;
-    if (draft_step && m->dec_ok && rows <= 2)  // embed, 5 per layer, head pieces + table + argmax
-        return 1 + 5 * L + (m->bf_head.a ? 3 : (m->mx_head.a ? 4 : 3));
+    const size_t head = m->bf_head.a ? 3 : (m->mx_head.a ? 4 : 3);  // head pieces + table + argmax
+    if (draft_step && m->dm_ok && rows <= 2)  // the fused draft step, then the head
+        return 1 + head;
+    if (draft_step && m->dec_ok && rows <= 2)  // embed, 5 per layer, head
+        return 1 + 5 * L + head;
     if (m->mx.fused && rows <= (size_t)mx_max_tokens())  // embed + norm pieces, 5 per layer, head
         return 2 + 5 * L + (m->bf_head.a ? 3 : (m->mx_head.a ? 4 : 3));
     // embed, 8 per layer (norm, q|k|v, rope, attention, o, norm, gate/up, down) with

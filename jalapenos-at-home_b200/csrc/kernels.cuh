@@ -116,4 +116,40 @@ inline KvView kv_view(const jl_model* m, int layer) {
 
 inline int qkv_ld(const jl_model* m) { return (m->q_heads + 2 * m->kv_heads) * HEAD; }
 
+// What the QK-RMSNorm and RoPE of one head need besides the head itself:
+// lane l's norm weights for dims (l, l+32, l+64, l+96) and rotation factors
+// for dims l and l+32 at position pos.  None of it depends on the previous
+// kernel, so it is fetched before the dependency wait.
+struct NormRope {
+    float w[4];
+    float2 c0, c1;
+};
+__device__ __forceinline__ NormRope norm_rope_args(const uint16_t* gw, const float2* rope, int pos, int lane) {
+    NormRope r;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r.w[i] = bf16f(gw[lane + 32 * i]);
+    r.c0 = rope[(size_t)pos * HALF + lane];
+    r.c1 = rope[(size_t)pos * HALF + lane + 32];
+    return r;
+}
+
+// QK-RMSNorm and RoPE of one head held as dims (l, l+32, l+64, l+96) by lane
+// l (lib.rs:306-313, 372-388; the arithmetic of k_qk_rope_kv).
+__device__ __forceinline__ void norm_rope4(float& a0, float& a1, float& a2, float& a3, const NormRope& nr) {
+    float ss = fmaf(a0, a0, fmaf(a1, a1, fmaf(a2, a2, a3 * a3)));
+    ss = warp_sum(ss);
+    const float size = sqrtf(__fadd_rn(__fdiv_rn(ss, 128.0f), 1e-6f));
+    const float2 c0 = nr.c0, c1 = nr.c1;
+    a0 = __fmul_rn(__fdiv_rn(a0, size), nr.w[0]);
+    a1 = __fmul_rn(__fdiv_rn(a1, size), nr.w[1]);
+    a2 = __fmul_rn(__fdiv_rn(a2, size), nr.w[2]);
+    a3 = __fmul_rn(__fdiv_rn(a3, size), nr.w[3]);
+    const float b0 = __fsub_rn(__fmul_rn(a0, c0.x), __fmul_rn(a2, c0.y));
+    const float b2 = __fadd_rn(__fmul_rn(a2, c0.x), __fmul_rn(a0, c0.y));
+    const float b1 = __fsub_rn(__fmul_rn(a1, c1.x), __fmul_rn(a3, c1.y));
+    const float b3 = __fadd_rn(__fmul_rn(a3, c1.x), __fmul_rn(a1, c1.y));
+    a0 = b0; a1 = b1; a2 = b2; a3 = b3;
+}
+
+
 }  // namespace jl

@@ -248,6 +248,7 @@ jl_status build_mx(jl_model* m) {
     }
     if (head_bf) JL_TRY(mx_build_bf16(m->head, base + bfh_off, &m->bf_head, 0));
     m->dec_ok = dec_supported(m);
+    JL_TRY(dm_prepare(m));
     Plan sp;
     // piece images: per 256-element stage, up to 16 rows x 8 pieces x 128
     // bytes of codes, then 1 KB of scale atoms
@@ -683,6 +684,8 @@ void model_free(jl_model* m) {
     cudaFree(m->mx.scratch);
     cudaFree(m->att_ws);
     cudaFree(m->att_cnt);
+    cudaFree(m->dm_layers);
+    cudaFree(m->dm_cnt);
     for (StageSlot& sl : m->stage) {
         if (sl.done) cudaEventDestroy(sl.done);
         cudaFreeHost(sl.hdr);

@@ -33,7 +33,7 @@ EXPORTS = (
     "jl_weights_count", "jl_weights_at", "jl_weights_get", "jl_model_options_default",
     "jl_model_load", "jl_model_synthesize", "jl_model_free", "jl_model_info_get",
     "jl_model_read_tensor", "jl_cache_create", "jl_cache_free", "jl_cache_len",
-    "jl_cache_truncate", "jl_predict", "jl_next_token", "jl_hidden", "jl_generate",
+    "jl_cache_truncate", "jl_predict", "jl_predict_draft", "jl_next_token", "jl_hidden", "jl_generate",
     "jl_schedule_fixed", "jl_schedule_adaptive", "jl_spec_options_default",
     "jl_generate_speculative", "jl_time_pass", "jl_time_projection", "jl_project",
     "jl_project_noalloc", "jl_pass_kernels", "jl_time_pass_draft", "jl_generate_batch",
@@ -135,6 +135,7 @@ def _load():
         "jl_cache_len": ([vp], sz),
         "jl_cache_truncate": ([vp, sz], ctypes.c_int),
         "jl_predict": ([vp, vp, u32p, sz, ctypes.c_int, u32p, f32p], ctypes.c_int),
+        "jl_predict_draft": ([vp, vp, u32p, sz, u32p, f32p], ctypes.c_int),
         "jl_next_token": ([vp, u32p, sz, u32p], ctypes.c_int),
         "jl_hidden": ([vp, u32p, sz, sz, f32p], ctypes.c_int),
         "jl_generate": ([vp, u32p, sz, sz, u32p, sz, ctypes.POINTER(sz)], ctypes.c_int),
@@ -315,6 +316,24 @@ class Model:
                              _p(ids, ctypes.c_uint32), None if lg is None else _p(lg, ctypes.c_float)))
         out = [int(i) for i in ids]
         return (out, lg) if logits else out
+
+    def predict_draft(self, tokens, cache: "Cache", logits: bool = False):
+        """One draft step (1 or 2 tokens, predicting after the last) through
+        the kernels a speculative loop's draft passes run: the proposal
+        passes of ``generate_scheduled`` (speculative.rs:84-92, 136-138)."""
+        t = u32(tokens)
+        out = np.zeros(1, np.uint32)
+        lg = np.empty((1, self.vocab), np.float32) if logits else None
+        check(lib.jl_predict_draft(self._h, cache._h, _p(t, ctypes.c_uint32), len(t),
+                                   _p(out, ctypes.c_uint32),
+                                   None if lg is None else _p(lg, ctypes.c_float)))
+        return ([int(out[0])], lg) if logits else [int(out[0])]
+
+    @property
+    def has_draft_path(self) -> bool:
+        """Whether draft steps take kernels of their own (CUDA-core MXFP4
+        projections) rather than the tensor-core pass every other pass takes."""
+        return self.pass_kernels(1, draft_step=True) != self.pass_kernels(1)
 
     def next_token(self, tokens) -> int:
         """``Model::next_token`` (model.rs:203-205)."""

@@ -361,54 +361,62 @@ static void matmul_rows(const matrix_t* w, const float* x, size_t rows, float* y
     /* lib.rs:240-266: each sum starts at 0.0 and adds x*w in order of i.
      * A weight row is decoded once (Mxfp4::values gives the same exact
      * values as Mxfp4::value).  One token row: four weight rows are summed
-     * side by side; several token rows: up to 8 token rows side by side.
-     * Every sum still accumulates in index order, so results are identical
-     * to the one-row-at-a-time loop. */
+     * side by side (their decoded values interleaved, so the four sums are
+     * one vector operation).  Several token rows: eight token rows side by
+     * side, from a transposed copy of x.  Every sum still accumulates in
+     * index order with separately rounded products, so results are
+     * identical to the one-row-at-a-time loop. */
     const int K = w->cols, O = w->rows;
     pair_levels_init();
+    float* xt = NULL;
+    const size_t groups = (rows + 7) / 8;
+    if (rows > 1) {
+        /* xt[g][i][j] = x[8g + j][i] (zero past the last row) */
+        xt = (float*)calloc(groups * (size_t)K * 8, sizeof(float));
+        if (!xt) abort();
+        for (size_t t = 0; t < rows; ++t)
+            for (int i = 0; i < K; ++i) xt[((t / 8) * (size_t)K + i) * 8 + t % 8] = x[t * (size_t)K + i];
+    }
 #pragma omp parallel
     {
         float* wrow = (float*)malloc((size_t)4 * K * sizeof(float));
+        float* w4 = (float*)malloc((size_t)4 * K * sizeof(float));
+        if (!wrow || !w4) abort();
         if (rows == 1) {
 #pragma omp for schedule(static)
             for (int r0 = 0; r0 < O; r0 += 4) {
                 const int nr = O - r0 < 4 ? O - r0 : 4;
-                for (int j = 0; j < nr; ++j) decode_row(w, r0 + j, wrow + (size_t)j * K);
-                for (int j = nr; j < 4; ++j) memcpy(wrow + (size_t)j * K, wrow, (size_t)K * sizeof(float));
-                const float* w0 = wrow;
-                const float* w1 = wrow + K;
-                const float* w2 = wrow + 2 * (size_t)K;
-                const float* w3 = wrow + 3 * (size_t)K;
-                float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+                for (int j = 0; j < 4; ++j) decode_row(w, r0 + (j < nr ? j : 0), wrow + (size_t)j * K);
+                for (int i = 0; i < K; ++i)
+                    for (int j = 0; j < 4; ++j) w4[(size_t)i * 4 + j] = wrow[(size_t)j * K + i];
+                float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 for (int i = 0; i < K; ++i) {
                     const float xi = x[i];
-                    s0 += xi * w0[i];
-                    s1 += xi * w1[i];
-                    s2 += xi * w2[i];
-                    s3 += xi * w3[i];
+                    for (int j = 0; j < 4; ++j) s[j] += xi * w4[(size_t)i * 4 + j];
                 }
-                const float s[4] = {s0, s1, s2, s3};
                 for (int j = 0; j < nr; ++j) y[r0 + j] = s[j];
             }
         } else {
 #pragma omp for schedule(static)
             for (int r = 0; r < O; ++r) {
                 decode_row(w, r, wrow);
-                for (size_t t0 = 0; t0 < rows; t0 += 8) {
+                for (size_t g = 0; g < groups; ++g) {
+                    const size_t t0 = g * 8;
                     const size_t nt = rows - t0 < 8 ? rows - t0 : 8;
+                    const float* xg = xt + g * (size_t)K * 8;
                     float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                    const float* xt[8];
-                    for (size_t j = 0; j < 8; ++j) xt[j] = x + (t0 + (j < nt ? j : 0)) * (size_t)K;
                     for (int i = 0; i < K; ++i) {
                         const float wi = wrow[i];
-                        for (size_t j = 0; j < 8; ++j) sum[j] += xt[j][i] * wi;
+                        for (int j = 0; j < 8; ++j) sum[j] += xg[(size_t)i * 8 + j] * wi;
                     }
                     for (size_t j = 0; j < nt; ++j) y[(t0 + j) * (size_t)O + r] = sum[j];
                 }
             }
         }
         free(wrow);
+        free(w4);
     }
+    free(xt);
 }
 
 int jlo_matmul(const jlo_model* m, int which, int layer, const float* x, size_t rows, float* y) {
@@ -463,6 +471,14 @@ uint32_t jlo_argmax(const float* values, size_t n) {
     for (size_t i = 1; i < n; ++i)
         if (values[i] > values[best]) best = i;
     return (uint32_t)best;
+}
+
+void jlo_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
 }
 
 int jlo_threads(void) {

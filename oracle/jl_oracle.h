@@ -115,6 +115,8 @@ uint32_t jlo_argmax(const float* values, size_t n);
 
 /* Number of OpenMP threads the oracle uses (for reporting). */
 int jlo_threads(void);
+/* Sets the OpenMP thread count of later calls (n > 0). */
+void jlo_set_threads(int n);
 
 #ifdef __cplusplus
 }

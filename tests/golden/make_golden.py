@@ -1,8 +1,8 @@
 """Generates the golden fixtures in tests/golden/ from the reference itself.
 
-Run in a container where the reference project is mounted (its path is the
-first argument, default /root/reference); the fixtures it writes are
-committed, so tests never need the reference at run time.
+Run where a checkout of the reference project is available; its path is the
+required first argument.  The fixtures it writes are committed, so tests
+never need the reference at run time.
 
 * mxfp4_quantize.npz -- inputs and outputs of the reference's own
   ``quantize`` / ``dequantize`` (python/quantize_mxfp4.py:18-49) on seeded
@@ -15,7 +15,7 @@ committed, so tests never need the reference at run time.
 * synth.npz -- first values and checksums of the seeded weight stream, so the
   generator definition cannot drift.
 
-Usage: python tests/golden/make_golden.py [/root/reference]
+Usage: python tests/golden/make_golden.py <path to the reference checkout>
 """
 from __future__ import annotations
 
@@ -175,7 +175,9 @@ def make_synth() -> None:
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path to the reference checkout>")
+    ref = Path(sys.argv[1])
     make_quantize(ref)
     make_synth()
     make_forward("tiny", "tiny", 0, False, 12, 16, True)

@@ -1,17 +1,20 @@
 """Full-size BASELINE.json architectures on the GPU.
 
 The CPU oracle checks the first decoder layer of every architecture (its
-tensors are the same whatever the layer count) and the whole 0.6B model;
-the 8B model is checked through size-independent properties: speculative
-output equals greedy output, oracle-draft p=0 accepts every proposal,
-logits are finite.
+tensors are the same whatever the layer count), the whole 0.6B model, the
+64-token greedy streams of Qwen3-1.7B bf16 and MXFP4 (configs 1 and 2, the
+reference's own acceptance test: engine/tests/generation.rs:6-28), and the
+8B model at full depth (last-row logits and the first greedy tokens).  The
+8B speculative loop is also checked through size-independent properties:
+speculative output equals greedy output, oracle-draft p=0 accepts every
+proposal.
 """
 import numpy as np
 import pytest
 
 import jalapeno as J
 import oracle as O
-from gpu_util import HIDDEN_REL_L2, first_layers, logits_close, rel_l2
+from gpu_util import HIDDEN_REL_L2, assert_stream_matches, first_layers, logits_close, rel_l2
 
 pytestmark = [pytest.mark.gpu, pytest.mark.slow]
 
@@ -42,6 +45,32 @@ def test_qwen3_0_6b_mxfp4_logits_match_oracle():
     assert logits_close(lg, rlg)
     assert rel_l2(lg, rlg) < 1e-4
     assert ids == rids
+
+
+@pytest.mark.parametrize("mxfp4", [False, True])
+def test_qwen3_1_7b_greedy_stream_matches_oracle_full_depth(mxfp4):
+    """BASELINE configs 1 and 2: 32-token prompt, 64 greedy tokens, every one
+    equal to the oracle's (f32 KV, the reference's precision)."""
+    cfg = O.PRESETS["qwen3-1.7b"]
+    ref = O.Model.synthetic(cfg, 0, mxfp4=mxfp4)
+    m = J.Model.from_config(cfg, 0, mxfp4=mxfp4, kv_dtype=J.KV_F32, kv_pool_tokens=1024)
+    ids, lg = m.predict(PROMPT, m.cache(), logits=True)
+    rids, rlg = ref.predict(PROMPT, ref.cache(), logits=True)
+    assert logits_close(lg, rlg) and rel_l2(lg, rlg) < 1e-4 and ids == rids
+    assert_stream_matches(m.generate(PROMPT, 64), ref, PROMPT, 64)
+
+
+def test_qwen3_8b_full_depth_matches_oracle():
+    """The headline target at full depth: last-row logits of the 32-token
+    prompt and the first 8 greedy tokens against the oracle."""
+    cfg = O.PRESETS["qwen3-8b"]
+    ref = O.Model.synthetic(cfg, 0, mxfp4=True)
+    m = J.Model.from_config(cfg, 0, mxfp4=True, kv_dtype=J.KV_F32, kv_pool_tokens=1024)
+    ids, lg = m.predict(PROMPT, m.cache(), logits=True)
+    rids, rlg = ref.predict(PROMPT, ref.cache(), logits=True)
+    assert logits_close(lg, rlg), "logits outside 2e-2 abs/rel"
+    assert rel_l2(lg, rlg) < 1e-4 and ids == rids
+    assert_stream_matches(m.generate(PROMPT, 8), ref, PROMPT, 8)
 
 
 def test_qwen3_8b_speculative_properties():

@@ -4,8 +4,9 @@ Tolerances: hidden-state relative L2 < 1e-5 with an f32 KV cache (the
 reference's own MXFP4 tolerance, engine/tests/mxfp4.rs:84); logits within
 2e-2 abs/rel of the oracle (north star) -- in practice far tighter, so the
 tests also bound the relative L2 of the logits; greedy tokens equal
-token-for-token (a near-tie escape is allowed only where the oracle's top-2
-margin is below 1e-3, see gpu_util.compare_streams).
+token-for-token over the whole generated stream (a near-tie escape is
+allowed only where the oracle's top-2 margin is below 1e-3, and is reported;
+see gpu_util.compare_streams).
 """
 import dataclasses
 
@@ -15,8 +16,8 @@ import pytest
 import checkpoint as CK
 import jalapeno as J
 import oracle as O
-from gpu_util import (HIDDEN_REL_L2, LOGIT_TOL, compare_streams, first_layers, logits_close,
-                      rel_l2)
+from gpu_util import (HIDDEN_REL_L2, LOGIT_TOL, assert_stream_matches, compare_streams,
+                      first_layers, logits_close, rel_l2)
 
 pytestmark = pytest.mark.gpu
 
@@ -129,7 +130,7 @@ def test_long_context_attention_windows_match_oracle(oracles, key, n):
     ids, lg = m.predict(prompt, m.cache(), all=False, logits=True)
     rids, rlg = ref.predict(prompt, ref.cache(), all=False, logits=True)
     assert rel_l2(lg, rlg) < 1e-5 and ids == rids
-    assert compare_streams(m.generate(prompt, 12), ref, prompt, 12) >= 6
+    assert_stream_matches(m.generate(prompt, 12), ref, prompt, 12)
 
 
 def test_long_context_speculative_equals_greedy():
@@ -162,14 +163,14 @@ def test_greedy_matches_oracle_token_for_token(oracles, key):
     m = gpu_model(O.PRESETS[key[0]], 0, key[1], kv_dtype=J.KV_F32)
     tokens = m.generate(PROMPT, 24)
     assert tokens[:20] == PROMPT
-    assert compare_streams(tokens, ref, PROMPT, 24) >= 8
+    assert_stream_matches(tokens, ref, PROMPT, 24)
 
 
 def test_greedy_with_bf16_kv_matches_rounded_oracle(oracles):
     ref = oracles[("tiny", True)]
     m = gpu_model(TINY, 0, True, kv_dtype=J.KV_BF16)
     tokens = m.generate(PROMPT, 24)
-    assert compare_streams(tokens, ref, PROMPT, 24, round_bf16=True) >= 8
+    assert_stream_matches(tokens, ref, PROMPT, 24, round_bf16=True)
 
 
 def test_rows_are_batch_invariant():
@@ -269,8 +270,8 @@ def test_speculative_control_flow_matches_oracle_loop(oracles):
     target = gpu_model(TINY, 0, False, kv_dtype=J.KV_F32)
     draft = gpu_model(DRAFT, 1, False, kv_dtype=J.KV_F32)
     greedy = target.generate(PROMPT, 30)
-    n = compare_streams(greedy, t_ref, PROMPT, 30)
-    assert n == 30, "streams diverged at a near tie; control-flow comparison needs equal streams"
+    chk = assert_stream_matches(greedy, t_ref, PROMPT, 30)
+    assert not chk.escapes, "streams diverged at a near tie; control-flow comparison needs equal streams"
     stream = greedy
     for p in (0.0, 0.25, 0.5):
         g = J.generate_scheduled(target, draft, PROMPT, 30, J.DraftSchedule.adaptive(4, 8),
