@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--p", type=float, default=0.25, help="oracle-draft replacement probability")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-pytorch", action="store_true",
+                    help="--impl reference: skip the transformers float32 baseline")
     ap.add_argument("--profile", action="store_true",
                     help="small run for ncu: one k+1-row target pass and one draft pass "
                          "(Model::time_pass), no timing loop")
@@ -310,6 +312,39 @@ def physical_cores() -> int:
     return os.cpu_count() or 1
 
 
+def pytorch_baseline(O, t_ref, d_ref, prompt, stream, args, threads):
+    """The reference's Python path (transformers Qwen3ForCausalLM, float32,
+    eager attention; python/speculative_decoding.py with both KV caches kept,
+    python/check_mxfp4.py's dequantized MXFP4 weights) on the same workload
+    and host cores: one generation after an untimed prefill, warm-up rounds,
+    then timed rounds."""
+    import torch
+    import transformers
+
+    import torch_baseline as TB
+
+    torch.set_num_threads(threads)
+    t0 = time.perf_counter()
+    ht, hd = TB.hf_model(t_ref.cfg, t_ref), TB.hf_model(d_ref.cfg, d_ref)
+    build_s = time.perf_counter() - t0
+    warm = min(args.warmup, 3)
+    toks, acc, drafted, rounds, marks = TB.speculative(
+        ht, hd, prompt, args.new, args.gamma, t_ref.eos, t_ref.cfg.vocab, stream, args.p, 5,
+        max_rounds=warm + args.steps)
+    marks = [(0.0, len(prompt))] + marks
+    warm = min(warm, max(0, len(marks) - 4))
+    (ta, na), (tb, nb) = marks[warm], marks[-1]
+    value = (nb - na) / (tb - ta)
+    del ht, hd
+    return {"value": value, "unit": "tok/s", "cores": threads, "kind": "pytorch",
+            "sample": (f"transformers {transformers.__version__} Qwen3ForCausalLM float32 eager on torch "
+                       f"{torch.__version__}, {threads} threads, 8B + 0.6B with MXFP4 projections dequantized, "
+                       f"k={args.gamma}, oracle draft p={args.p}, KV caches kept between rounds: {warm} warm-up "
+                       f"rounds, then {len(marks) - 1 - warm} timed rounds, {nb - na} tokens in {tb - ta:.2f} s "
+                       f"(models built in {build_s:.0f} s); tokens equal to the oracle's: "
+                       f"{toks == stream[: len(toks)]}")}
+
+
 def run_reference(args, dist):
     """--impl reference: the reference's CPU implementation of this path on
     the host cores.  Its Rust engine does not build here (no cargo; its GPU
@@ -353,6 +388,8 @@ def run_reference(args, dist):
                 "cpu_baseline": {"value": value, "unit": "tok/s", "cores": O.threads(), "kind": "port",
                                  "sample": sample},
                 "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        if not args.no_pytorch:
+            line["pytorch_baseline"] = pytorch_baseline(O, t_ref, d_ref, prompt, stream, args, threads)
         print(json.dumps(line), flush=True)
     dist.barrier()
 

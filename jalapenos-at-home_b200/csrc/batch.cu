@@ -213,6 +213,8 @@ jl_status dev_alloc(BatchGraph* g, T** out, size_t count) {
     JL_CUDA(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T)));
     g->dev.push_back(p);
     JL_CUDA(cudaMemset(p, 0, std::max<size_t>(count, 1) * sizeof(T)));
+    // the memset runs on the legacy stream, which the model's stream does not wait for
+    JL_CUDA(cudaDeviceSynchronize());
     *out = (T*)p;
     return JL_OK;
 }

@@ -77,7 +77,8 @@ jl_status check_device_flag(jl_model* m) {
     int flag = 0;
     JL_CUDA(cudaMemcpy(&flag, m->counters, sizeof(int), cudaMemcpyDeviceToHost));
     if (flag) {
-        JL_CUDA(cudaMemset(m->counters, 0, sizeof(int)));
+        JL_CUDA(cudaMemsetAsync(m->counters, 0, sizeof(int), m->stream));
+        JL_CUDA(cudaStreamSynchronize(m->stream));
         if (flag & 3) {
             set_error("kernel guard tripped (flags 0x%x): %s", flag,
                       (flag & 1) ? "KV page id outside the pool" : "position outside the context");
@@ -642,8 +643,6 @@ jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters
 size_t pass_kernels(const jl_model* m, size_t rows, bool draft_step) {
     const size_t L = (size_t)m->layers;
     const size_t head = m->bf_head.a ? 3 : (m->mx_head.a ? 4 : 3);  // head pieces + table + argmax
-    if (draft_step && m->dm_ok && rows <= 2)  // the fused draft step, then the head
-        return 1 + head;
     if (draft_step && m->dec_ok && rows <= 2)  // embed, 5 per layer, head
         return 1 + 5 * L + head;
     if (m->mx.fused && rows <= (size_t)mx_max_tokens())  // embed + norm pieces, 5 per layer, head

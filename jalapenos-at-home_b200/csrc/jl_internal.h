@@ -239,11 +239,6 @@ struct jl_model {
     jl::MxProj mx_head;                   // tensor-core copy of an MXFP4 output table
     jl::MxProj bf_head;                   // tensor-core copy of a bf16 output table (fused pass)
     bool dec_ok = false;                  // draft steps may run on the CUDA-core kernels
-    bool dm_ok = false;                   // ... as the one persistent kernel k_draft_fused
-    int dm_slot = 0, dm_nslots = 0;       // its weight ring: slot bytes and slots
-    size_t dm_smem = 0;                   // its dynamic shared memory
-    void* dm_layers = nullptr;            // its per-layer weight descriptors (device)
-    int* dm_cnt = nullptr;                // its phase counters (device, zero between launches)
     jl::MxBuffers mx;
     const uint16_t* final_norm = nullptr;
     std::vector<jl::LayerW> lw;
@@ -433,13 +428,6 @@ jl_status mx_head_fused(const PassCtx& c, const MxProj& p, const uint16_t* norm,
 bool dec_supported(const jl_model* m);
 jl_status dec_configure();
 jl_status record_dec_pass(const PassCtx& c, int layers);
-// The whole draft step (every layer) as one persistent kernel (dec.cu):
-// whether a model takes it, with its ring slot bytes, slot count and
-// dynamic shared memory; set-up at model creation; one pass's launch.
-bool dm_supported(const jl_model* m, int* slot_bytes, int* nslots, size_t* smem);
-jl_status dm_configure();
-jl_status dm_prepare(jl_model* m);
-jl_status record_dm_pass(const PassCtx& c);
 // mx_project over caller-owned memory: `hdr` (rows read on the device),
 // `scratch` laid out as mx_scratch_plan says, `err` the device error flag.
 jl_status mx_project_with(const MxProj& p, int epi, const PassHdr* hdr, int mcap, const float* x,

@@ -1400,7 +1400,6 @@ jl_status configure_kernels() {
     JL_CUDA(cudaFuncSetAttribute(k_attn_decode<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(1)));
     JL_TRY(mx_configure());
     JL_TRY(dec_configure());
-    JL_TRY(dm_configure());
     JL_TRY(noalloc_prepare(dev));
     if (dev < 64) done[dev] = true;
     return JL_OK;

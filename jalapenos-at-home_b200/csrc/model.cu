@@ -160,6 +160,16 @@ jl_status finish_model(jl_model* m, const jl_model_options& o) {
     return JL_OK;
 }
 
+// Set-up work (weight synthesis and tiling, memsets of the scratch and
+// counters) runs on the legacy default stream, which the model's
+// non-blocking stream does not wait for: without this, a first pass can
+// start while a memset is still clearing its pass descriptors.
+jl_status creation_done(jl_model* m) {
+    JL_CUDA(cudaSetDevice(m->device));
+    JL_CUDA(cudaDeviceSynchronize());
+    return JL_OK;
+}
+
 jl_status begin_model(const jl_model_options& o, jl_model** out) {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
@@ -248,7 +258,6 @@ jl_status build_mx(jl_model* m) {
     }
     if (head_bf) JL_TRY(mx_build_bf16(m->head, base + bfh_off, &m->bf_head, 0));
     m->dec_ok = dec_supported(m);
-    JL_TRY(dm_prepare(m));
     Plan sp;
     // piece images: per 256-element stage, up to 16 rows x 8 pieces x 128
     // bytes of codes, then 1 KB of scale atoms
@@ -530,6 +539,7 @@ jl_status model_from_checkpoint(const WeightIndex& w, const HostConfig& cfg, con
     if (tied) m->head = m->embed;
     JL_TRY(finish_model(m, o));
     JL_TRY(build_mx(m));
+    JL_TRY(creation_done(m));
     *out = guard.release();
     return JL_OK;
 }
@@ -656,6 +666,7 @@ jl_status model_synthesize(const jl_synth_config& c, const jl_model_options& o, 
     if (c.tied) m->head = m->embed;
     JL_TRY(finish_model(m, o));
     JL_TRY(build_mx(m));
+    JL_TRY(creation_done(m));
     *out = guard.release();
     return JL_OK;
 }
@@ -684,8 +695,6 @@ void model_free(jl_model* m) {
     cudaFree(m->mx.scratch);
     cudaFree(m->att_ws);
     cudaFree(m->att_cnt);
-    cudaFree(m->dm_layers);
-    cudaFree(m->dm_cnt);
     for (StageSlot& sl : m->stage) {
         if (sl.done) cudaEventDestroy(sl.done);
         cudaFreeHost(sl.hdr);

@@ -161,3 +161,4 @@ def test_real_draft_loop_matches_oracle_loop(dec_oracle, target_seed):
         assert g.draft.passes == o.draft.passes and g.verify.passes == o.verify.passes
         if target_seed == 1:
             assert g.accepted >= 0.9 * g.drafted
+
