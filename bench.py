@@ -341,7 +341,7 @@ def pytorch_baseline(O, t_ref, d_ref, prompt, stream, args, threads):
                        f"{torch.__version__}, {threads} threads, 8B + 0.6B with MXFP4 projections dequantized, "
                        f"k={args.gamma}, oracle draft p={args.p}, KV caches kept between rounds: {warm} warm-up "
                        f"rounds, then {len(marks) - 1 - warm} timed rounds, {nb - na} tokens in {tb - ta:.2f} s "
-                       f"(models built in {build_s:.0f} s); tokens equal to the oracle's: "
+                       f"(models built in {build_s:.0f} s); tokens equal to the oracle's (f32 cache): "
                        f"{toks == stream[: len(toks)]}")}
 
 
@@ -389,7 +389,10 @@ def run_reference(args, dist):
                                  "sample": sample},
                 "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         if not args.no_pytorch:
-            line["pytorch_baseline"] = pytorch_baseline(O, t_ref, d_ref, prompt, stream, args, threads)
+            # transformers keeps K/V in f32: its oracle-draft stream is the
+            # oracle's greedy stream with an f32 cache
+            stream32 = t_ref.generate(prompt, args.new)
+            line["pytorch_baseline"] = pytorch_baseline(O, t_ref, d_ref, prompt, stream32, args, threads)
         print(json.dumps(line), flush=True)
     dist.barrier()
 
@@ -415,12 +418,19 @@ def run_config5(args, dist):
     it takes part in); the roofline is that of the path's formula: bytes per
     round W_t + k W_d + B KV_t(ctx) + B k KV_d(ctx) at the measured copy
     bandwidth."""
+    for line in config5_lines(args, dist, [int(x) for x in args.batches.split(",")]):
+        if dist.rank == 0:
+            print(json.dumps(line), flush=True)
+
+
+def config5_lines(args, dist, batches):
+    """The configs[4] measurements for each per-GPU batch size (one dict each)."""
     import jalapeno as J
     import oracle as O
 
     peak, peak_kind = measured_peaks()
     ctx, new, k = 4096, 256, args.gamma
-    batches = [int(x) for x in args.batches.split(",")]
+    lines = []
     t, d = PRESETS["qwen3-8b"], PRESETS["qwen3-0.6b"]
     opts = dict(kv_pool_tokens=max(batches) * (ctx + new + 128) + 1024, max_pass_rows=256, device=dist.local)
     target = J.Model.synthesize(**t, seed=0, mxfp4=True, name="Qwen3-8B-MXFP4", **opts)
@@ -462,8 +472,49 @@ def run_config5(args, dist):
                 "config": {"workload": "Qwen3-8B MXFP4 + Qwen3-0.6B MXFP4, batched speculative decode",
                            "batch_per_gpu": B, "context_tokens": ctx, "new_tokens": new, "k": k,
                            "draft_mode": f"oracle p={args.p}", "parallelism": f"replicas x{dist.world}"}}
-        if dist.rank == 0:
-            print(json.dumps(line), flush=True)
+        lines.append(line)
+    del target, draft
+    return lines
+
+
+def other_configs(J, O, draft, args, peak):
+    """BASELINE.json configs[0..2] and a compact configs[4], each with its
+    path roofline at the measured copy bandwidth.  Decode time is device time
+    of the generation loop (CUDA events), prefill excluded.
+      Qwen3-1.7B bf16 greedy, 32-token prompt, 64 tokens.
+      the same with MXFP4 projections.
+      Qwen3-1.7B MXFP4 target + Qwen3-0.6B MXFP4 draft, k = 4,
+                  oracle draft p in {0, 0.25, 0.5}, and the real draft.
+      8B + 0.6B, k = 4, batch 8 of 4096-token contexts, 256 new
+                  tokens per sequence (bench.py --config5 runs batches 1/8/32)."""
+    out = {}
+    c17 = dict(PRESETS["qwen3-1.7b"])
+    prompt = O.prompt_ids(args.prompt, c17["vocab"], 2)
+    for mx in (False, True):
+        m = J.Model.synthesize(**c17, seed=0, mxfp4=mx, kv_pool_tokens=1024, max_pass_rows=256)
+        J.generate_batch(m, [prompt], args.new)  # warm: graphs
+        r = J.generate_batch(m, [prompt], args.new)
+        new = len(r.results[0].tokens) - len(prompt)
+        tps = new / (r.decode_ms / 1000.0)
+        roof = peak * 1e9 / m.info.pass_bytes
+        out[f"1.7B {'MXFP4' if mx else 'bf16'} greedy"] = {
+            "tok_s": tps, "roofline_tok_s": roof, "frac": tps / roof, "pass_bytes": m.info.pass_bytes}
+        if mx:
+            greedy = m.generate(prompt, args.new)
+            w_t, w_d = m.info.pass_bytes, draft.info.pass_bytes
+            for p, stream in ((0.0, True), (0.25, True), (0.5, True), (0.0, False)):
+                kw = dict(oracle_stream=greedy, oracle_p=p, oracle_seed=5) if stream else {}
+                J.generate_speculative(m, draft, prompt, args.new, args.gamma, **kw)  # warm
+                rs = J.generate_speculative(m, draft, prompt, args.new, args.gamma, **kw)
+                assert rs.tokens == greedy, "speculative output differs from greedy"
+                n = len(rs.tokens) - len(prompt)
+                tps = n / (rs.decode_ms / 1000.0)
+                roof = peak * 1e9 * (n / max(rs.rounds, 1)) / (w_t + args.gamma * w_d)
+                out[f"1.7B MXFP4 + 0.6B, k={args.gamma}, " + (f"oracle p={p}" if stream else "real draft")] = {
+                    "tok_s": tps, "accepted": rs.accepted, "drafted": rs.drafted, "roofline_tok_s": roof,
+                    "frac": tps / roof}
+        del m
+    return out
 
 
 def workload_config(args):
@@ -625,6 +676,11 @@ def main():
                 "tok_s": (len(r.tokens) - len(lp)) / (r.decode_ms / 1000.0), "accepted": r.accepted,
                 "drafted": r.drafted}
         line["sweep"] = sweep
+        line["configs"] = other_configs(J, O, draft, args, peak)
+        c5 = config5_lines(args, dist, [8])[0]
+        line["configs"]["configs[4] batch 8, 4096-token contexts, 256 new tokens"] = {
+            key: c5[key] for key in ("value", "acceptance", "hbm_gbs_per_gpu", "roofline", "greedy_batch_tok_s",
+                                     "ms_decode")}
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(O, target, draft, prompt, greedy, args)
     if dist.rank == 0:
