@@ -76,7 +76,6 @@ def run_profile(args, dist):
     k+1-row verify pass of the target and a one-row draft pass, each through
     the captured pass graph the decode loop replays."""
     import jalapeno as J
-    import oracle as O
 
     if args.small:
         opts = dict(kv_pool_tokens=1024, max_pass_rows=64, device=dist.local)
@@ -89,7 +88,7 @@ def run_profile(args, dist):
     else:
         target, draft = make_models(J, dist.local)
         vocab = 151936
-    prompt = O.prompt_ids(args.prompt, vocab, 2)
+    prompt = J.prompt_ids(args.prompt, vocab, 2)
     tw, tg = target.time_pass(prompt, args.gamma + 1, reps=1)
     dw, dg = draft.time_pass_draft(prompt, reps=1)
     print(json.dumps({"profile": True, "target_pass_ms": tg, "draft_pass_ms": dg,
@@ -426,7 +425,6 @@ def run_config5(args, dist):
 def config5_lines(args, dist, batches):
     """The configs[4] measurements for each per-GPU batch size (one dict each)."""
     import jalapeno as J
-    import oracle as O
 
     peak, peak_kind = measured_peaks()
     ctx, new, k = 4096, 256, args.gamma
@@ -439,7 +437,7 @@ def config5_lines(args, dist, batches):
     w_t, w_d = ti.pass_bytes, di.pass_bytes
     kv_t, kv_d = ti.kv_bytes_per_token, di.kv_bytes_per_token
     for B in batches:
-        prompts = [O.prompt_ids(ctx, ti.vocab, 3 + i + 1000 * dist.rank) for i in range(B)]
+        prompts = [J.prompt_ids(ctx, ti.vocab, 3 + i + 1000 * dist.rank) for i in range(B)]
         g = J.generate_batch(target, prompts, new + 2 * k)
         streams = [s.tokens for s in g.results]
         t0 = time.perf_counter()
@@ -477,7 +475,7 @@ def config5_lines(args, dist, batches):
     return lines
 
 
-def other_configs(J, O, draft, args, peak):
+def other_configs(J, draft, args, peak):
     """BASELINE.json configs[0..2] and a compact configs[4], each with its
     path roofline at the measured copy bandwidth.  Decode time is device time
     of the generation loop (CUDA events), prefill excluded.
@@ -489,7 +487,7 @@ def other_configs(J, O, draft, args, peak):
                   tokens per sequence (bench.py --config5 runs batches 1/8/32)."""
     out = {}
     c17 = dict(PRESETS["qwen3-1.7b"])
-    prompt = O.prompt_ids(args.prompt, c17["vocab"], 2)
+    prompt = J.prompt_ids(args.prompt, c17["vocab"], 2)
     for mx in (False, True):
         m = J.Model.synthesize(**c17, seed=0, mxfp4=mx, kv_pool_tokens=1024, max_pass_rows=256)
         J.generate_batch(m, [prompt], args.new)  # warm: graphs
@@ -544,12 +542,11 @@ def main():
         dist.close()
         return
     import jalapeno as J
-    import oracle as O
 
     peak, peak_kind = measured_peaks()
     target, draft = make_models(J, dist.local)
     ti, di = target.info, draft.info
-    prompt = O.prompt_ids(args.prompt, ti.vocab, 2 + dist.rank)
+    prompt = J.prompt_ids(args.prompt, ti.vocab, 2 + dist.rank)
     greedy = target.generate(prompt, args.new)
 
     def step(p, stream=True):
@@ -665,7 +662,7 @@ def main():
         sweep["greedy (no draft) e2e tok/s"] = args.new / (time.perf_counter() - t0)
         # the configuration's long-context setting: a prefilled 2048-token context
         if args.prompt < 2048:
-            lp = O.prompt_ids(2048, ti.vocab, 3 + dist.rank)
+            lp = J.prompt_ids(2048, ti.vocab, 3 + dist.rank)
             lg = target.generate(lp, args.new)
             J.generate_speculative(target, draft, lp, args.new, args.gamma, oracle_stream=lg,
                                    oracle_p=args.p, oracle_seed=5)  # warm: graphs for the longer context
@@ -676,12 +673,14 @@ def main():
                 "tok_s": (len(r.tokens) - len(lp)) / (r.decode_ms / 1000.0), "accepted": r.accepted,
                 "drafted": r.drafted}
         line["sweep"] = sweep
-        line["configs"] = other_configs(J, O, draft, args, peak)
+        line["configs"] = other_configs(J, draft, args, peak)
         c5 = config5_lines(args, dist, [8])[0]
         line["configs"]["configs[4] batch 8, 4096-token contexts, 256 new tokens"] = {
             key: c5[key] for key in ("value", "acceptance", "hbm_gbs_per_gpu", "roofline", "greedy_batch_tok_s",
                                      "ms_decode")}
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        import oracle as O  # the checker, timed as the CPU baseline only
+
         line["cpu_baseline"] = cpu_baseline(O, target, draft, prompt, greedy, args)
     if dist.rank == 0:
         print(json.dumps(line), flush=True)

@@ -605,3 +605,30 @@ def generate_speculative_batch(target: Model, draft: Model, prompts, count: int,
     check(lib.jl_generate_speculative_batch(target._h, draft._h, B, ptrs, lens, count, sc, opts, res,
                                             ctypes.byref(stats)))
     return _batch_result(outs, rounds, res, stats)
+
+
+def _philox4x32_10(c0, c1, c2, c3, k0: int, k1: int):
+    """Philox4x32-10 (Salmon et al., "Parallel random numbers: as easy as 1,
+    2, 3", SC 2011) over arrays of counters, in uint64 lanes."""
+    m = np.uint64(0xFFFFFFFF)
+    c = [np.asarray(x, np.uint64) & m for x in (c0, c1, c2, c3)]
+    k0, k1 = np.uint64(k0), np.uint64(k1)
+    for r in range(10):
+        if r:
+            k0 = (k0 + np.uint64(0x9E3779B9)) & m
+            k1 = (k1 + np.uint64(0xBB67AE85)) & m
+        p0 = np.uint64(0xD2511F53) * c[0]
+        p1 = np.uint64(0xCD9E8D57) * c[2]
+        c = [(p1 >> np.uint64(32)) ^ c[1] ^ k0, p1 & m, (p0 >> np.uint64(32)) ^ c[3] ^ k1, p0 & m]
+    return c
+
+
+def prompt_ids(n: int, vocab: int, seed: int) -> list[int]:
+    """Seeded uniform prompt ids for synthetic workloads: id 4i+j is word j
+    of Philox4x32-10 at counter (i, 0, 0, "prmp") under key (seed, "toks"),
+    modulo the vocabulary."""
+    i = np.arange((n + 3) // 4, dtype=np.uint64)
+    z = np.zeros_like(i)
+    w = _philox4x32_10(i, z, z, z + np.uint64(0x70726D70), seed & 0xFFFFFFFF, 0x746F6B73)
+    ids = np.stack(w, axis=1).reshape(-1)[:n] % np.uint64(vocab)
+    return [int(x) for x in ids]

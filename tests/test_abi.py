@@ -55,3 +55,12 @@ def test_null_arguments_are_rejected():
     assert J.lib.jl_weights_load(None, None) == J.JL_ERR_INVALID_ARG
     assert J.lib.jl_model_synthesize(None, None, None) == J.JL_ERR_INVALID_ARG
     assert J.lib.jl_cache_truncate(None, 0) == J.JL_ERR_INVALID_ARG
+
+
+def test_benchmark_prompts_equal_the_oracle_prompts():
+    """The package's synthetic prompt generator (the GPU benchmark's inputs)
+    gives the ids the oracle's parity tests use."""
+    import oracle as O
+
+    for n, vocab, seed in ((1, 10, 0), (20, 1000, 2), (4096, 151936, 3), (33, 8192, 1002), (7, 5, 2**33 + 5)):
+        assert J.prompt_ids(n, vocab, seed) == O.prompt_ids(n, vocab, seed)
