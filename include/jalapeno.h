@@ -298,6 +298,21 @@ jl_status jl_time_pass_draft(jl_model* m, const uint32_t* prompt, size_t n, size
  * reference counterpart: it feeds the launch count of the benchmark. */
 jl_status jl_pass_kernels(const jl_model* m, size_t rows, int draft_step, size_t* kernels);
 
+/* Kernel phase timeline, from the diagnostic build of this library
+ * (`make -C jalapenos-at-home_b200 timeline` -> lib/libjalapeno_timeline.so):
+ * the decode-pass kernels stamp the GPU's nanosecond clock at fixed points
+ * of their critical path.  jl_timeline_read copies the stamps of the last
+ * recorded pass (jl_time_pass / jl_time_pass_draft record one pass and
+ * replay it), launches x JL_TIMELINE_CTAS x JL_TIMELINE_POINTS values, 0
+ * where a CTA or point did not stamp; `stamps` NULL returns the launch
+ * count only.  JL_ERR_INVALID_ARG from the normal build.  No reference
+ * counterpart: it backs the per-kernel phase profiles. */
+#define JL_TIMELINE_CTAS 512
+#define JL_TIMELINE_POINTS 8
+jl_status jl_timeline_read(uint64_t* stamps, size_t cap, size_t* launches);
+/* Kernel of launch i of that pass (NULL past the last). */
+const char* jl_timeline_kernel(size_t launch);
+
 /* generate_scheduled: both models share token ids; the target has the
  * final say, so the output equals jl_generate(target, ...) whenever the
  * forward pass is row-count invariant (it is here). opts may be NULL. */

@@ -312,6 +312,14 @@ jl_status jl_pass_kernels(const jl_model* m, size_t rows, int draft_step, size_t
     return JL_OK;
 }
 
+jl_status jl_timeline_read(uint64_t* stamps, size_t cap, size_t* launches) {
+    static_assert(JL_TIMELINE_CTAS == jl::TL_CTAS && JL_TIMELINE_POINTS == jl::TL_POINTS, "timeline table shape");
+    JL_NEED(launches, "launches must be non-null");
+    JL_GUARD({ return tl_read(reinterpret_cast<unsigned long long*>(stamps), cap, launches); })
+}
+
+const char* jl_timeline_kernel(size_t launch) { return jl::tl_kernel(launch); }
+
 jl_status jl_project_noalloc(jl_model* m, int layer, jl_projection which, const float* x,
                              size_t rows, float* y, void* stream) {
     JL_NEED(m && x && y, "model, x and y must be non-null");

@@ -27,6 +27,7 @@
 #include "launch.cuh"
 #include "mx_pieces.cuh"
 #include "ptx.cuh"
+#include "timeline.cuh"
 
 namespace jl {
 
@@ -204,6 +205,7 @@ struct DecArgs {
     const PassHdr* hdr;
     int mcap;
     int* err;
+    TlSlot tl;  // phase stamps (timeline build)
 };
 
 template <int M, int EPI, int TR>
@@ -212,6 +214,7 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
     __shared__ uint64_t bar;
     __shared__ float red[32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) tl_stamp(a.tl, 0);
     const int K = a.K;
     const int r0 = blockIdx.x * TR;
     const int n = min(TR, a.out_rows - r0);
@@ -235,6 +238,7 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
     dec_norm_weights(a.norm, K, wv);
     __syncthreads();  // the barrier is initialised before anyone waits on it
     ptx::grid_dependency_wait();
+    if (threadIdx.x == 0) tl_stamp(a.tl, 1);
     ptx::launch_dependents();
     const int rows = min(a.hdr->rows, a.mcap);
     // residual add: the x values lane 0 of this warp adds to, read now so the
@@ -255,6 +259,7 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
         if (threadIdx.x == 0) atomicOr(a.err, 4);
         return;
     }
+    if (threadIdx.x == 0) tl_stamp(a.tl, 2);
     // warp w owns tile rows w, w + 8, ... (RPW of them; rows past n are
     // computed from unloaded shared memory and dropped)
     constexpr int RPW = TR / 8;
@@ -288,6 +293,7 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
                         a.y[(size_t)m * a.ldy + r0 + r] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
                     }
             }
+        if (threadIdx.x == 0) tl_stamp(a.tl, 3);
     } else {
         const uint8_t* wr[RPW];
         const uint8_t* sr[RPW];
@@ -311,6 +317,7 @@ __global__ void __launch_bounds__(256) k_dec_proj(DecArgs a) {
                         *d = EPI == DEC_ADD ? __fadd_rn(xold[h][m], v) : v;  // residual (model.rs:178-186)
                     }
             }
+        if (threadIdx.x == 0) tl_stamp(a.tl, 3);
     }
 }
 
@@ -389,6 +396,9 @@ jl_status record_dec_pass(const PassCtx& c, int layers) {
             d.hdr = c.pass().hdr;
             d.mcap = M;
             d.err = m->counters;
+            d.tl = tl_launch(epi == DEC_STORE ? "k_dec_proj<qkv>"
+                             : epi == DEC_ADD ? "k_dec_proj<add>"
+                                              : "k_dec_proj<swiglu>");
             const int tr = epi == DEC_STORE ? 16 : 8;
             const dim3 g((out_rows + tr - 1) / tr);
             const size_t sm = dec_proj_smem(K, epi == DEC_SWIGLU, tr);

@@ -18,6 +18,7 @@
 #include "jl_internal.h"
 #include "kernels.cuh"
 #include "loop.cuh"
+#include "timeline.cuh"
 
 namespace jl {
 
@@ -246,9 +247,10 @@ jl_status host_pass(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int
         return JL_OK;
     }
     if (full && n <= (size_t)SMALL_M) {
-        // one captured pass per row bucket 1, 2, 4, 8, 16
-        int b = 0;
-        while ((1 << b) < (int)n) ++b;
+        // one captured pass per row count, as the speculative loop's verify
+        // pass is: the projections' MMA columns and shared-memory rings are
+        // sized for the pass's rows
+        const int b = (int)n - 1;
         cudaGraphExec_t& exec = m->small_graph[b];
         if (exec && m->small_graph_splits[b] < splits) {
             cudaGraphExecDestroy(exec);
@@ -257,7 +259,7 @@ jl_status host_pass(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, int
         if (!exec) {
             cudaGraph_t g;
             JL_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-            PassCtx ctx{m, st, 1 << b, 1 << b, false, splits};
+            PassCtx ctx{m, st, (int)n, (int)n, false, splits};
             jl_status rs = record_pass_ctx(ctx, m->layers, true);
             cudaError_t ce = cudaStreamEndCapture(st, &g);
             if (rs != JL_OK) return rs;
@@ -372,6 +374,7 @@ jl_status record_fused_pass(const PassCtx& c, int layers) {
 }
 
 jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head) {
+    tl_begin_pass();
     const jl_model* m = c.m;
     const bool dec = c.draft && m->dec_ok && c.rows_cap <= 2 && c.chunks == 1;
     if (c.chunks > 1 && !(m->mx.fused && m->bf_head.a)) {
@@ -504,6 +507,7 @@ jl_status time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t rows, 
     std::unique_ptr<jl_cache, void (*)(jl_cache*)> guard(c, cache_free);
     uint32_t first = 0;
     JL_TRY(predict(m, c, prompt, n, false, &first, nullptr));
+    JL_TRY(tl_clear(m->stream));  // timeline build: only the timed passes' stamps remain
     std::vector<uint32_t> tokens(rows), out(rows);
     for (size_t i = 0; i < rows; ++i) tokens[i] = prompt[i % n];
     std::vector<double> wall, busy;
@@ -1167,6 +1171,84 @@ jl_status generate_speculative(jl_model* T, jl_model* D, const uint32_t* prompt,
     tc->len = (size_t)s->target_len;
     dc->len = (size_t)s->draft_len;
     return JL_OK;
+}
+
+
+// ---- kernel phase timeline (diagnostic build, timeline.cuh) ----------------
+
+namespace {
+struct Timeline {
+    unsigned long long* table = nullptr;
+    int device = -1;  // the table's device: launches elsewhere get no slot
+    int next = 0;
+    std::vector<std::string> names;
+};
+Timeline g_timeline;
+}  // namespace
+
+bool tl_enabled() {
+#ifdef JL_TIMELINE
+    return true;
+#else
+    return false;
+#endif
+}
+
+jl_status tl_prepare() {
+#ifdef JL_TIMELINE
+    if (!g_timeline.table) {
+        const size_t bytes = sizeof(unsigned long long) * TL_LAUNCHES * TL_CTAS * TL_POINTS;
+        JL_CUDA(cudaGetDevice(&g_timeline.device));
+        JL_CUDA(cudaMalloc(&g_timeline.table, bytes));
+        JL_CUDA(cudaMemset(g_timeline.table, 0, bytes));
+        JL_CUDA(cudaDeviceSynchronize());
+    }
+#endif
+    return JL_OK;
+}
+
+jl_status tl_clear(cudaStream_t stream) {
+    if (!tl_enabled() || !g_timeline.table) return JL_OK;
+    JL_CUDA(cudaMemsetAsync(g_timeline.table, 0, sizeof(unsigned long long) * TL_LAUNCHES * TL_CTAS * TL_POINTS,
+                            stream));
+    return JL_OK;
+}
+
+void tl_begin_pass() {
+    g_timeline.next = 0;
+    g_timeline.names.clear();
+}
+
+TlSlot tl_launch(const char* kernel) {
+    int dev = -1;
+    if (!tl_enabled() || !g_timeline.table || g_timeline.next >= TL_LAUNCHES || cudaGetDevice(&dev) != cudaSuccess ||
+        dev != g_timeline.device)
+        return TlSlot{nullptr, -1};
+    g_timeline.names.emplace_back(kernel);
+    return TlSlot{g_timeline.table, g_timeline.next++};
+}
+
+jl_status tl_read(unsigned long long* out, size_t cap, size_t* launches) {
+    if (!tl_enabled()) {
+        set_error("this library was built without the kernel timeline (make timeline)");
+        return JL_ERR_INVALID_ARG;
+    }
+    const size_t n = (size_t)g_timeline.next;
+    if (launches) *launches = n;
+    if (!out) return JL_OK;
+    const size_t need = n * TL_CTAS * TL_POINTS;
+    if (cap < need) {
+        set_error("timeline: %zu stamps needed, room for %zu", need, cap);
+        return JL_ERR_INVALID_ARG;
+    }
+    JL_CUDA(cudaSetDevice(g_timeline.device));
+    JL_CUDA(cudaDeviceSynchronize());
+    if (n) JL_CUDA(cudaMemcpy(out, g_timeline.table, need * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+    return JL_OK;
+}
+
+const char* tl_kernel(size_t launch) {
+    return launch < g_timeline.names.size() ? g_timeline.names[launch].c_str() : nullptr;
 }
 
 }  // namespace jl

@@ -262,7 +262,7 @@ struct jl_model {
     int att_rows = 16;
     float* att_ws = nullptr;
     int* att_cnt = nullptr;
-    int small_graph_splits[5] = {};       // att_splits each small_graph was captured with
+    int small_graph_splits[jl::SMALL_M] = {};  // att_splits each small_graph was captured with
     int draft_graph_splits[2] = {};
     uint32_t* host_out = nullptr;
     float* host_logits = nullptr;
@@ -270,7 +270,7 @@ struct jl_model {
     void* scratch_arena = nullptr;
     cudaStream_t stream = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-    cudaGraphExec_t small_graph[5] = {};  // full pass for rows <= 1, 2, 4, 8, 16
+    cudaGraphExec_t small_graph[jl::SMALL_M] = {};  // full pass of 1..16 rows, one per row count
     cudaGraphExec_t draft_graph[2] = {};  // draft-step pass of 1 or 2 rows (profiling)
     std::vector<jl::SpecGraph*> spec_graphs;  // owned; freed by model_free
     std::vector<jl::BatchGraph*> batch_graphs;  // owned; freed by model_free
@@ -443,5 +443,32 @@ jl_status build_mx(jl_model* m);
 jl_status launch_fill_u16(uint16_t* out, size_t n, uint16_t value, cudaStream_t stream);
 jl_status launch_quantize_mxfp4(const uint16_t* bf16, int rows, int cols, uint8_t* packed,
                                 uint8_t* scales, cudaStream_t stream);
+
+// ---- kernel phase timeline (the device side is timeline.cuh) ----
+
+constexpr int TL_LAUNCHES = 512, TL_CTAS = 512, TL_POINTS = 8;
+
+// A launch's rows of the table (a kernel argument); table null: no stamps.
+struct TlSlot {
+    unsigned long long* table;
+    int id;
+};
+
+// Host side (engine.cu).  tl_begin_pass restarts the launch ids; tl_launch
+// returns the slot of the next launch of the pass being recorded and keeps
+// its kernel name for the reader.  Both do nothing in the normal build.
+void tl_begin_pass();
+TlSlot tl_launch(const char* kernel);
+bool tl_enabled();
+// allocates the table (timeline build, once per process, on the current
+// device) when a model is created, never while a pass is being captured
+jl_status tl_prepare();
+// zeroes the table on `stream` (outside a capture), so rows that the passes
+// timed next do not write read as zeros rather than as older stamps
+jl_status tl_clear(cudaStream_t stream);
+// launches recorded in the last pass; copies their rows (launches x TL_CTAS
+// x TL_POINTS stamps) when `out` is non-null and `cap` holds them all
+jl_status tl_read(unsigned long long* out, size_t cap, size_t* launches);
+const char* tl_kernel(size_t launch);
 
 }  // namespace jl

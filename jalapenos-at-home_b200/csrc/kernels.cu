@@ -14,6 +14,7 @@
 #include "launch.cuh"
 #include "mx_pieces.cuh"
 #include "ptx.cuh"
+#include "timeline.cuh"
 
 namespace jl {
 
@@ -585,6 +586,7 @@ struct AttnSplit {
     // is hdr[r / 16] and whose attention pieces start at bout + chunk * cs_bout
     int chunked;
     size_t cs_bout;
+    TlSlot tl;  // phase stamps (timeline build)
 };
 
 // `split` warps serve each query head, taking every split-th 32-position
@@ -610,6 +612,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
     __shared__ __align__(16) float cacc[ATT_MAXWARPS][HEAD];
     __shared__ uint64_t bar;
     __shared__ int page_s[ATT_WIN];
+    if (threadIdx.x == 0) tl_stamp(sp.tl, 0);
     const int g = blockIdx.x, row = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nw = blockDim.x >> 5;
@@ -715,6 +718,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
     }
     __syncthreads();  // the barrier is initialised before anyone waits on it
     ptx::grid_dependency_wait();
+    if (threadIdx.x == 0) tl_stamp(sp.tl, 1);
     ptx::launch_dependents();
     if (crow < rows && !valid && sub == 0) {  // uniform over the CTA
         if (threadIdx.x == 0) atomicOr(kv.err, 2);
@@ -766,6 +770,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
     } else if (sub == 0) {
         *(float4*)(qw + 4 * lane) = *(const float4*)(qkv + (size_t)row * ld + h * HEAD + 4 * lane);
     }
+    if (threadIdx.x == 0) tl_stamp(sp.tl, 2);
     const float scale = sqrtf(128.0f);
     float m = -INFINITY, l = 0.f;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -889,6 +894,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
         if (w0 + ATT_WIN < w_hi) __syncthreads();  // the window is free for the next copy (uniform)
     }
     if (!ok && threadIdx.x == 0) atomicOr(kv.err, 4);  // a page copy did not arrive in time
+    if (threadIdx.x == 0) tl_stamp(sp.tl, 3);
     // merge the head's warps in warp order
     if (lane == 0) {
         cm[warp] = m;
@@ -983,11 +989,13 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
 #pragma unroll
     for (int d = 0; d < 4; ++d) o[d] = __fdiv_rn(o[d], L);
     *(float4*)(out + (size_t)row * out_ld + h * HEAD + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
+    if (threadIdx.x == 0) tl_stamp(sp.tl, 4);
     if (bout) {
         __syncwarp();  // every lane has finished reading q
         *(float4*)(qw + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
         __syncwarp();
         mx::emit_pieces_smem(qw, HEAD, 4, crow, 1, 1, lane, 32, h * HEAD, bN, bout);
+        if (threadIdx.x == 0) tl_stamp(sp.tl, 5);
     }
 }
 
@@ -1401,6 +1409,7 @@ jl_status configure_kernels() {
     JL_TRY(mx_configure());
     JL_TRY(dec_configure());
     JL_TRY(noalloc_prepare(dev));
+    JL_TRY(tl_prepare());
     if (dev < 64) done[dev] = true;
     return JL_OK;
 }
@@ -1468,7 +1477,8 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
         const dim3 g2(c.m->kv_heads, c.rows_cap, z), blk(32 * group * split);
         const int qw = c.m->q_heads * HEAD;
         const AttnRaw none{};
-        const AttnSplit sp{c.m->att_ws, c.m->att_cnt, chunked ? 1 : 0, chunked ? c.m->mx.sattn : 0};
+        const AttnSplit sp{c.m->att_ws, c.m->att_cnt, chunked ? 1 : 0, chunked ? c.m->mx.sattn : 0,
+                           tl_launch("k_attn_decode")};
         if (c.m->kv.dtype == JL_KV_F32)
             return launch_pdl(k_attn_decode<1, 0>, g2, blk, att_smem(1), c.stream, c.pass(),
                               (const float*)c.m->s.qkv, qkv_ld(c.m), group, split, kv_view(c.m, layer),
@@ -1528,7 +1538,7 @@ jl_status launch_attention_raw(const PassCtx& c, int layer, const uint16_t* qn, 
     const int split = att_split(group);
     const dim3 g2(m->kv_heads, c.rows_cap, att_grid_splits(c)), blk(32 * group * split);
     const int qw = m->q_heads * HEAD;
-    const AttnSplit sp{m->att_ws, m->att_cnt, 0, 0};
+    const AttnSplit sp{m->att_ws, m->att_cnt, 0, 0, tl_launch("k_attn_decode<raw>")};
     AttnRaw raw;
     raw.qn = qn;
     raw.kn = kn;

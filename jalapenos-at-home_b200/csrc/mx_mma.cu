@@ -35,6 +35,7 @@
 #include "launch.cuh"
 #include "mx_pieces.cuh"
 #include "ptx.cuh"
+#include "timeline.cuh"
 
 namespace jl {
 
@@ -268,6 +269,7 @@ struct MxArgs {
     // Ring slots whose weights are requested into L2 ahead of their copy
     // into shared memory (0: none)
     int l2_ahead;
+    TlSlot tl;  // phase stamps (timeline build)
 };
 
 enum : int { MX_STORE = 0, MX_ADD = 1, MX_SWIGLU = 2, MX_QKV = 3, MX_HEAD = 4 };
@@ -388,6 +390,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
     const int kc = ks > 1 ? (int)ptx::cluster_ctarank() : 0;
     const int cid = blockIdx.x / ks, NC = gridDim.x / ks;
     const int s0 = split_stage(a.S, G, ks, kc), s1 = split_stage(a.S, G, ks, kc + 1);
+    if (threadIdx.x == 0) tl_stamp(a.tl, 0);
     // epilogue scratch (staged outputs [m][128], SwiGLU up halves and RoPE
     // partners xs[m][64]), then the leader's reduction buffer: for each peer
     // rank and group of four rows of the pass, [128 tile rows][4] floats
@@ -445,6 +448,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
                 pre = g;
             }
             ptx::grid_dependency_wait();
+            tl_stamp(a.tl, 1);
             // Slot h of this CTA is stage s0 + (h % spt) * G of its
             // (h / spt)-th tile.  Once the activation copies of the slots
             // loaded before the wait are out, each slot's copy is followed
@@ -500,6 +504,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
                         ok = false;
                         break;
                     }
+                    if (g == 0) tl_stamp(a.tl, 2);
                     ptx::tc_fence_after();
                     uint8_t* base = smem + slot * sbytes;
                     const int n = min(G, s1 - s);
@@ -595,6 +600,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
             }
             if (!ptx::mbar_wait(&tfull[buf], use & 1, WAIT_LIMIT)) ok = false;
             ptx::tc_fence_after();
+            if (j == 0 && threadIdx.x == 64) tl_stamp(a.tl, 3);
             float val[MX_MAXTOK];
             const uint32_t lanebase = tmem + ((uint32_t)(quarter * 32) << 16) + ACC_COL + buf * acc_step;
             constexpr int CPR = cols_per_row(KIND), RPL = 32 / CPR;  // rows per 32-column load
@@ -638,6 +644,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
                 }
                 if (threadIdx.x == 64) ptx::mbar_arrive_expect_tx(&red_full, (uint32_t)((ks - 1) * RB * 128 * 16));
                 if (!ptx::mbar_wait_cluster(&red_full, j & 1, WAIT_LIMIT)) ok = false;
+                if (j == 0 && threadIdx.x == 64) tl_stamp(a.tl, 4);
 #pragma unroll
                 for (int m4 = 0; m4 < MX_MAXTOK; m4 += 4) {
                     if (m4 >= a.mcap) continue;
@@ -688,6 +695,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
                         val[m] = act;
                     }
                 }
+                if (j == 0 && threadIdx.x == 64) tl_stamp(a.tl, 5);
                 if (a.bout) {  // the tile's 64 activations: two 32-blocks of the down input
                     epi_bar();  // every up value has been read
                     if (row < 64) {
@@ -819,6 +827,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
                         val[m] = 0.f;
                     }
                 }
+                if (j == 0 && threadIdx.x == 64) tl_stamp(a.tl, 5);
                 if (a.bout) {  // the next projection's input: pieces of x * w
 #pragma unroll
                     for (int m = 0; m < MX_MAXTOK; ++m)
@@ -839,6 +848,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
             }
         }
     }
+    if (threadIdx.x == 64) tl_stamp(a.tl, 6);
     ptx::launch_dependents();
     ptx::tc_fence_before();
     __syncthreads();
@@ -848,6 +858,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1) k_mx_gemv(const MxArgs a0) {
     }
     if (warp == 1) ptx::tmem_dealloc(tmem, tcols);
     if (!ok && lane == 0) atomicOr(a.err, 4);  // a bounded wait gave up
+    if (threadIdx.x == 0) tl_stamp(a.tl, 7);
 }
 }  // namespace
 
@@ -1005,6 +1016,9 @@ jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream, int chunk
     cfg.dynamicSmemBytes = mx_smem(a.N, KIND, a.mcap, a.ksplit);
     MxArgs b = a;
     b.l2_ahead = EPI == MX_HEAD ? MX_L2_AHEAD : 0;
+    static const char* const names[] = {"k_mx_gemv<store>", "k_mx_gemv<add>", "k_mx_gemv<swiglu>",
+                                        "k_mx_gemv<qkv>", "k_mx_gemv<head>"};
+    b.tl = tl_launch(names[EPI]);
     if (chunks > 1 && a.N > 64) {
         // several tiles per CTA: two 128-column accumulators, so a tile's
         // epilogue overlaps the next tile's MMAs

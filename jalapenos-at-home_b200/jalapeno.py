@@ -18,7 +18,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-LIB_PATH = HERE / "lib" / "libjalapeno.so"
+# JALAPENO_LIB names another build of the library (the timeline build,
+# lib/libjalapeno_timeline.so, for timeline.py)
+LIB_PATH = Path(os.environ["JALAPENO_LIB"]) if os.environ.get("JALAPENO_LIB") else HERE / "lib" / "libjalapeno.so"
 
 JL_OK, JL_ERR_INVALID_ARG, JL_ERR_FORMAT, JL_ERR_OOM = 0, 1, 2, 3
 JL_ERR_CUDA, JL_ERR_TIMEOUT, JL_ERR_IO, JL_ERR_NO_DEVICE = 4, 5, 6, 7
@@ -37,7 +39,7 @@ EXPORTS = (
     "jl_schedule_fixed", "jl_schedule_adaptive", "jl_spec_options_default",
     "jl_generate_speculative", "jl_time_pass", "jl_time_projection", "jl_project",
     "jl_project_noalloc", "jl_pass_kernels", "jl_time_pass_draft", "jl_generate_batch",
-    "jl_generate_speculative_batch",
+    "jl_generate_speculative_batch", "jl_timeline_read", "jl_timeline_kernel",
 )
 PROJ_QKV, PROJ_O, PROJ_GATE_UP, PROJ_DOWN, PROJ_HEAD = 0, 1, 2, 3, 4
 
@@ -158,6 +160,8 @@ def _load():
         "jl_pass_kernels": ([vp, sz, ctypes.c_int, ctypes.POINTER(sz)], ctypes.c_int),
         "jl_time_pass_draft": ([vp, u32p, sz, sz, ctypes.POINTER(ctypes.c_double),
                                 ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
+        "jl_timeline_read": ([ctypes.POINTER(ctypes.c_uint64), sz, ctypes.POINTER(sz)], ctypes.c_int),
+        "jl_timeline_kernel": ([sz], ctypes.c_char_p),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -632,3 +636,19 @@ def prompt_ids(n: int, vocab: int, seed: int) -> list[int]:
     w = _philox4x32_10(i, z, z, z + np.uint64(0x70726D70), seed & 0xFFFFFFFF, 0x746F6B73)
     ids = np.stack(w, axis=1).reshape(-1)[:n] % np.uint64(vocab)
     return [int(x) for x in ids]
+
+
+TIMELINE_CTAS, TIMELINE_POINTS = 512, 8
+
+
+def timeline() -> tuple[list[str], np.ndarray]:
+    """Kernel names and stamps [launch][cta][point] (GPU nanoseconds, 0 where
+    nothing stamped) of the last recorded pass: jl_timeline_read, from the
+    timeline build of the library only (JALAPENO_LIB)."""
+    n = ctypes.c_size_t()
+    check(lib.jl_timeline_read(None, 0, ctypes.byref(n)))
+    buf = np.zeros((n.value, TIMELINE_CTAS, TIMELINE_POINTS), dtype=np.uint64)
+    check(lib.jl_timeline_read(_p(buf, ctypes.c_uint64), buf.size, ctypes.byref(n)))
+    names = [lib.jl_timeline_kernel(i).decode() for i in range(n.value)]
+    return names, buf
+

@@ -64,3 +64,14 @@ def test_benchmark_prompts_equal_the_oracle_prompts():
 
     for n, vocab, seed in ((1, 10, 0), (20, 1000, 2), (4096, 151936, 3), (33, 8192, 1002), (7, 5, 2**33 + 5)):
         assert J.prompt_ids(n, vocab, seed) == O.prompt_ids(n, vocab, seed)
+
+
+def test_timeline_is_refused_by_the_normal_build():
+    """jl_timeline_read belongs to the diagnostic build (make timeline); the
+    normal library answers with an error instead of stamps."""
+    if "timeline" in str(J.LIB_PATH):
+        pytest.skip("running against the timeline build")
+    n = ctypes.c_size_t()
+    assert J.lib.jl_timeline_read(None, 0, ctypes.byref(n)) == J.JL_ERR_INVALID_ARG
+    assert b"timeline" in J.lib.jl_last_error()
+    assert J.lib.jl_timeline_kernel(0) is None
