@@ -298,6 +298,13 @@ jl_status jl_time_pass_draft(jl_model* m, const uint32_t* prompt, size_t n, size
  * reference counterpart: it feeds the launch count of the benchmark. */
 jl_status jl_pass_kernels(const jl_model* m, size_t rows, int draft_step, size_t* kernels);
 
+/* Runs one device wait that nothing completes, bounded by `polls` polls
+ * (1..2^20) of the poll loop every pass kernel's waits use, which then sets
+ * the same error bit: returns JL_ERR_TIMEOUT with the bounded-wait message
+ * and leaves the model usable.  No reference counterpart: it tests the
+ * timeout path without faulting or hanging the GPU. */
+jl_status jl_wait_probe(jl_model* m, uint32_t polls);
+
 /* Kernel phase timeline, from the diagnostic build of this library
  * (`make -C jalapenos-at-home_b200 timeline` -> lib/libjalapeno_timeline.so):
  * the decode-pass kernels stamp the GPU's nanosecond clock at fixed points

@@ -312,6 +312,11 @@ jl_status jl_pass_kernels(const jl_model* m, size_t rows, int draft_step, size_t
     return JL_OK;
 }
 
+jl_status jl_wait_probe(jl_model* m, uint32_t polls) {
+    JL_NEED(m, "model must be non-null");
+    JL_GUARD({ return wait_probe(m, polls); })
+}
+
 jl_status jl_timeline_read(uint64_t* stamps, size_t cap, size_t* launches) {
     static_assert(JL_TIMELINE_CTAS == jl::TL_CTAS && JL_TIMELINE_POINTS == jl::TL_POINTS, "timeline table shape");
     JL_NEED(launches, "launches must be non-null");

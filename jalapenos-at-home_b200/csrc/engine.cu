@@ -18,6 +18,7 @@
 #include "jl_internal.h"
 #include "kernels.cuh"
 #include "loop.cuh"
+#include "ptx.cuh"
 #include "timeline.cuh"
 
 namespace jl {
@@ -85,11 +86,38 @@ jl_status check_device_flag(jl_model* m) {
                       (flag & 1) ? "KV page id outside the pool" : "position outside the context");
             return JL_ERR_CUDA;
         }
-        set_error("a bounded device wait gave up (flags 0x%x): %s", flag,
-                  (flag & 8) ? "fused draft step" : "projection copy or split-K reduction");
+        set_error("a bounded device wait gave up (flags 0x%x): a weight, activation or KV page copy, or a "
+                  "split-K reduction, did not complete in time", flag);
         return JL_ERR_TIMEOUT;
     }
     return JL_OK;
+}
+
+namespace {
+// One wait that nothing completes: an mbarrier expecting one arrival that
+// never comes, polled `polls` times by the same loop the pass kernels use,
+// then the same error bit they set.  No fault, no unbounded loop.
+__global__ void k_wait_probe(int* err, uint32_t polls) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&bar, 1);
+        ptx::fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && !ptx::mbar_wait(&bar, 0, polls)) atomicOr(err, 4);
+}
+}  // namespace
+
+jl_status wait_probe(jl_model* m, uint32_t polls) {
+    if (polls == 0 || polls > (1u << 20)) {
+        set_error("wait probe: polls must be 1..%u", 1u << 20);
+        return JL_ERR_INVALID_ARG;
+    }
+    JL_CUDA(cudaSetDevice(m->device));
+    k_wait_probe<<<1, 32, 0, m->stream>>>(m->counters, polls);
+    JL_CUDA(cudaGetLastError());
+    JL_CUDA(cudaStreamSynchronize(m->stream));
+    return check_device_flag(m);
 }
 
 jl_status check_ids(const jl_model* m, const uint32_t* ids, size_t n) {

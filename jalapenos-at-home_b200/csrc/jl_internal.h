@@ -317,6 +317,8 @@ jl_status configure_kernels();
 jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool all,
                   uint32_t* out_ids, float* out_logits, bool draft_step = false);
 jl_status hidden(jl_model* m, const uint32_t* ids, size_t n, size_t layers, float* out);
+// One bounded device wait that nothing completes (tests the timeout path).
+jl_status wait_probe(jl_model* m, uint32_t polls);
 jl_status time_pass(jl_model* m, const uint32_t* prompt, size_t n, size_t rows, size_t reps,
                     double* wall_ms, double* gpu_ms, bool draft_step = false);
 jl_status time_projection(jl_model* m, int layer, int which, int rows, int iters, double* ms,

@@ -39,7 +39,7 @@ EXPORTS = (
     "jl_schedule_fixed", "jl_schedule_adaptive", "jl_spec_options_default",
     "jl_generate_speculative", "jl_time_pass", "jl_time_projection", "jl_project",
     "jl_project_noalloc", "jl_pass_kernels", "jl_time_pass_draft", "jl_generate_batch",
-    "jl_generate_speculative_batch", "jl_timeline_read", "jl_timeline_kernel",
+    "jl_generate_speculative_batch", "jl_timeline_read", "jl_timeline_kernel", "jl_wait_probe",
 )
 PROJ_QKV, PROJ_O, PROJ_GATE_UP, PROJ_DOWN, PROJ_HEAD = 0, 1, 2, 3, 4
 
@@ -162,6 +162,7 @@ def _load():
                                 ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
         "jl_timeline_read": ([ctypes.POINTER(ctypes.c_uint64), sz, ctypes.POINTER(sz)], ctypes.c_int),
         "jl_timeline_kernel": ([sz], ctypes.c_char_p),
+        "jl_wait_probe": ([vp, ctypes.c_uint32], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -399,6 +400,11 @@ class Model:
         check(lib.jl_time_pass_draft(self._h, _p(t, ctypes.c_uint32), len(t), reps,
                                      ctypes.byref(wall), ctypes.byref(gpu)))
         return wall.value, gpu.value
+
+    def wait_probe(self, polls: int = 1000) -> None:
+        """One device wait that nothing completes, bounded by ``polls`` polls:
+        raises JlError(JL_ERR_TIMEOUT) and leaves the model usable."""
+        check(lib.jl_wait_probe(self._h, polls))
 
     def pass_kernels(self, rows: int, draft_step: bool = False) -> int:
         """Kernels one forward pass of `rows` rows launches (see jl_pass_kernels)."""
