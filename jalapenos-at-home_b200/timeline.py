@@ -1,11 +1,11 @@
 """Kernel phase timeline of one decode pass (the timeline build of the
 library: `make -C jalapenos-at-home_b200 timeline`).
 
-    python jalapenos-at-home_b200/timeline.py verify [--rows 5]   # Qwen3-8B MXFP4 verify pass
-    python jalapenos-at-home_b200/timeline.py draft               # Qwen3-0.6B MXFP4 draft step
+    python jalapenos-at-home_b200/timeline.py verify [--rows 5] [--prompt 32]   # Qwen3-8B MXFP4 verify pass
+    python jalapenos-at-home_b200/timeline.py draft [--prompt 32]               # Qwen3-0.6B MXFP4 draft step
 
 Builds the benchmark's model (seeded synthetic weights), runs Model.time_pass
-(or time_pass_draft) after a 32-token prompt, and reads the stamps the
+(or time_pass_draft) after a prompt of --prompt tokens, and reads the stamps the
 kernels wrote during the last replay of the pass.  For every kernel kind it
 prints, averaged over the layers, times in microseconds relative to the end
 of the previous launch (its last CTA's last stamp): when its CTAs started,
@@ -115,16 +115,18 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("pass_kind", choices=["verify", "draft"])
     ap.add_argument("--rows", type=int, default=5, help="verify: rows of the pass (k + 1)")
+    ap.add_argument("--prompt", type=int, default=32, help="context (prompt tokens) before the timed pass")
     args = ap.parse_args()
     cfg, seed = (QWEN3_8B, 0) if args.pass_kind == "verify" else (QWEN3_06B, 1)
-    m = J.Model.synthesize(**cfg, seed=seed, mxfp4=True, kv_pool_tokens=4096)
-    prompt = J.prompt_ids(32, cfg["vocab"], 2)
+    m = J.Model.synthesize(**cfg, seed=seed, mxfp4=True, kv_pool_tokens=max(4096, args.prompt + 256))
+    prompt = J.prompt_ids(args.prompt, cfg["vocab"], 2)
     if args.pass_kind == "verify":
         _, ms = m.time_pass(prompt, args.rows, reps=5)
-        print(f"Qwen3-8B MXFP4 pass of {args.rows} rows after a 32-token prompt: {ms:.4f} ms (CUDA events, median)")
+        print(f"Qwen3-8B MXFP4 pass of {args.rows} rows after a {args.prompt}-token prompt: {ms:.4f} ms "
+              "(CUDA events, median)")
     else:
         _, ms = m.time_pass_draft(prompt, reps=5)
-        print(f"Qwen3-0.6B MXFP4 draft step after a 32-token prompt: {ms:.4f} ms (CUDA events, median)")
+        print(f"Qwen3-0.6B MXFP4 draft step after a {args.prompt}-token prompt: {ms:.4f} ms (CUDA events, median)")
     names, st = J.timeline()
     report(summarize(names, st), cfg["layers"])
 
