@@ -35,6 +35,12 @@ constexpr int SMALL_M = 16;      // passes up to this many rows use the decode k
 constexpr int ATT_WIN = 2;       // KV pages per decode-attention window (one CTA per window over long contexts)
 constexpr int ATT_PART = 4 + HEAD;  // floats of one window's partial: max, sum, 2 pad, 128 outputs
 constexpr int ATT_ZMAX = 64;     // window CTAs per row at most: past 64 windows each CTA takes several
+// Window CTAs per row at most in the decode attention of passes whose q|k|v
+// arrive normalised (greedy, verify, batched; the model's raw draft steps
+// keep ATT_ZMAX): a verify pass's rows then fill the GPU with fewer,
+// longer CTAs.  Every such pass of a model uses the same cap, so a row's
+// result does not depend on the pass.
+constexpr int ATT_ZMAX_DECODE = 8;
 constexpr int MAX_SEQS = 64;     // sequences one pass may touch
 constexpr int MAX_CHUNKS = 32;   // 16-row chunks of one multi-chunk pass (fused decode kernels)
 constexpr int MAX_GAMMA = 16;    // largest draft length of the device-resident loop

@@ -586,6 +586,7 @@ struct AttnSplit {
     // is hdr[r / 16] and whose attention pieces start at bout + chunk * cs_bout
     int chunked;
     size_t cs_bout;
+    int zmax;   // window CTAs per row at most (ATT_ZMAX or ATT_ZMAX_DECODE)
     TlSlot tl;  // phase stamps (timeline build)
 };
 
@@ -643,7 +644,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
     // pass's longest row (a grid too small for a row, which no launch here
     // makes, falls back to CTA z = 0 doing every window).
     const int nwin = max(1, (npages + ATT_WIN - 1) / ATT_WIN);
-    const int wpc = (nwin + ATT_ZMAX - 1) / ATT_ZMAX;  // consecutive windows per CTA (1 up to 64 windows)
+    const int wpc = (nwin + sp.zmax - 1) / sp.zmax;  // consecutive windows per CTA (1 up to zmax windows)
     const int need = (nwin + wpc - 1) / wpc;
     const int nsplit = need <= (int)gridDim.z ? need : 1;
     const int zs = blockIdx.z;
@@ -1472,13 +1473,13 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
         const int split = att_split(group);
         // the split workspace holds att_rows rows x att_smax windows (a row
         // whose context needs more CTAs than a grid has is done by one CTA).
-        int z = att_grid_splits(c);
+        int z = std::min(att_grid_splits(c), ATT_ZMAX_DECODE);
         while (z > 1 && (size_t)c.rows_cap * z > (size_t)c.m->att_rows * c.m->att_smax) z >>= 1;
         const dim3 g2(c.m->kv_heads, c.rows_cap, z), blk(32 * group * split);
         const int qw = c.m->q_heads * HEAD;
         const AttnRaw none{};
         const AttnSplit sp{c.m->att_ws, c.m->att_cnt, chunked ? 1 : 0, chunked ? c.m->mx.sattn : 0,
-                           tl_launch("k_attn_decode")};
+                           ATT_ZMAX_DECODE, tl_launch("k_attn_decode")};
         if (c.m->kv.dtype == JL_KV_F32)
             return launch_pdl(k_attn_decode<1, 0>, g2, blk, att_smem(1), c.stream, c.pass(),
                               (const float*)c.m->s.qkv, qkv_ld(c.m), group, split, kv_view(c.m, layer),
@@ -1538,7 +1539,7 @@ jl_status launch_attention_raw(const PassCtx& c, int layer, const uint16_t* qn, 
     const int split = att_split(group);
     const dim3 g2(m->kv_heads, c.rows_cap, att_grid_splits(c)), blk(32 * group * split);
     const int qw = m->q_heads * HEAD;
-    const AttnSplit sp{m->att_ws, m->att_cnt, 0, 0, tl_launch("k_attn_decode<raw>")};
+    const AttnSplit sp{m->att_ws, m->att_cnt, 0, 0, ATT_ZMAX, tl_launch("k_attn_decode<raw>")};
     AttnRaw raw;
     raw.qn = qn;
     raw.kn = kn;
