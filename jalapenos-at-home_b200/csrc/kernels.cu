@@ -637,12 +637,14 @@ __global__ void __launch_bounds__(512) k_attn_decode(PassBuf pb, const float* __
     const int visible = valid ? rd.pos + 1 : 0;
     const int npages = (visible + PAGE - 1) / PAGE;
     // Position splits (blockIdx.z): a row whose context spans more than one
-    // window of ATT_WIN pages takes one CTA per window, and the last of them
-    // to finish merges their partial softmax sums in window order; a row
+    // window of ATT_WIN pages takes one CTA per window, up to sp.zmax CTAs
+    // (past that each CTA takes consecutive windows), and the last of them
+    // to finish merges their partial softmax sums in CTA order; a row
     // within one window is done by CTA z = 0 alone, as a whole.  The split
-    // depends only on the row's position; the host sizes every grid for its
-    // pass's longest row (a grid too small for a row, which no launch here
-    // makes, falls back to CTA z = 0 doing every window).
+    // depends only on the row's position and sp.zmax, which every pass of a
+    // kind shares; the host sizes every grid for its pass's longest row (a
+    // grid too small for a row, which no launch here makes, falls back to
+    // CTA z = 0 doing every window).
     const int nwin = max(1, (npages + ATT_WIN - 1) / ATT_WIN);
     const int wpc = (nwin + sp.zmax - 1) / sp.zmax;  // consecutive windows per CTA (1 up to zmax windows)
     const int need = (nwin + wpc - 1) / wpc;
@@ -1472,7 +1474,8 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     if ((c.rows_cap <= SMALL_M || chunked) && group <= 8) {  // decode passes: a warp per query head
         const int split = att_split(group);
         // the split workspace holds att_rows rows x att_smax windows (a row
-        // whose context needs more CTAs than a grid has is done by one CTA).
+        // whose context needs more CTAs than a grid has is done by one CTA;
+        // with at most ATT_ZMAX_DECODE CTAs per row the halving never runs).
         int z = std::min(att_grid_splits(c), ATT_ZMAX_DECODE);
         while (z > 1 && (size_t)c.rows_cap * z > (size_t)c.m->att_rows * c.m->att_smax) z >>= 1;
         const dim3 g2(c.m->kv_heads, c.rows_cap, z), blk(32 * group * split);
