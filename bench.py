@@ -475,7 +475,7 @@ def config5_lines(args, dist, batches):
     return lines
 
 
-def other_configs(J, draft, args, peak):
+def other_configs(J, draft, args, peak, device):
     """BASELINE.json configs[0..2] and a compact configs[4], each with its
     path roofline at the measured copy bandwidth.  Decode time is device time
     of the generation loop (CUDA events), prefill excluded.
@@ -489,7 +489,7 @@ def other_configs(J, draft, args, peak):
     c17 = dict(PRESETS["qwen3-1.7b"])
     prompt = J.prompt_ids(args.prompt, c17["vocab"], 2)
     for mx in (False, True):
-        m = J.Model.synthesize(**c17, seed=0, mxfp4=mx, kv_pool_tokens=1024, max_pass_rows=256)
+        m = J.Model.synthesize(**c17, seed=0, mxfp4=mx, kv_pool_tokens=1024, max_pass_rows=256, device=device)
         J.generate_batch(m, [prompt], args.new)  # warm: graphs
         r = J.generate_batch(m, [prompt], args.new)
         new = len(r.results[0].tokens) - len(prompt)
@@ -673,7 +673,7 @@ def main():
                 "tok_s": (len(r.tokens) - len(lp)) / (r.decode_ms / 1000.0), "accepted": r.accepted,
                 "drafted": r.drafted}
         line["sweep"] = sweep
-        line["configs"] = other_configs(J, draft, args, peak)
+        line["configs"] = other_configs(J, draft, args, peak, dist.local)
         c5 = config5_lines(args, dist, [8])[0]
         line["configs"]["configs[4] batch 8, 4096-token contexts, 256 new tokens"] = {
             key: c5[key] for key in ("value", "acceptance", "hbm_gbs_per_gpu", "roofline", "greedy_batch_tok_s",

@@ -33,3 +33,30 @@ def test_two_ranks_aggregate_over_gloo(tmp_path):
         assert abs(x["value"] - 129 / 0.2) < 1e-9
         assert abs(x["e2e"] - 129 / 2.0) < 1e-9
         assert x["slowest_ms"] == 200.0
+
+
+def test_every_benchmark_model_is_placed_on_the_ranks_gpu():
+    """Under torchrun each rank builds its models on its own GPU
+    (LOCAL_RANK): a model left on GPU 0 fails a speculative call with a draft
+    on the rank's GPU.  Every model the benchmark synthesises passes a device."""
+    import re
+
+    src = (HERE.parent / "bench.py").read_text()
+
+    def call_args(pattern):
+        out = []
+        for m in re.finditer(pattern, src):
+            depth, i = 0, src.index("(", m.start())
+            for j in range(i, len(src)):
+                depth += {"(": 1, ")": -1}.get(src[j], 0)
+                if depth == 0:
+                    break
+            out.append(src[i:j + 1])
+        return out
+
+    calls = call_args(r"Model\.synthesize\(")
+    assert calls
+    for args in calls:
+        assert "device=" in args or "**opts" in args, args
+    for args in call_args(r"opts = dict\("):
+        assert "device=" in args, args
