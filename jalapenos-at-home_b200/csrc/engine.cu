@@ -1236,7 +1236,9 @@ jl_status tl_prepare() {
 }
 
 jl_status tl_clear(cudaStream_t stream) {
-    if (!tl_enabled() || !g_timeline.table) return JL_OK;
+    int dev = -1;
+    if (!tl_enabled() || !g_timeline.table || cudaGetDevice(&dev) != cudaSuccess || dev != g_timeline.device)
+        return JL_OK;
     JL_CUDA(cudaMemsetAsync(g_timeline.table, 0, sizeof(unsigned long long) * TL_LAUNCHES * TL_CTAS * TL_POINTS,
                             stream));
     return JL_OK;
