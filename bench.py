@@ -65,8 +65,13 @@ def parse():
                     help="BASELINE.json configs[4]: per-GPU batches of independent sequences with 4096-token "
                          "contexts and 256 new tokens (one JSON line per batch size)")
     ap.add_argument("--batches", default="1,8,32", help="--config5 batch sizes")
+    ap.add_argument("--prefill", default="",
+                    help="comma-separated prompt lengths: time Model::predict of one prompt of each length on "
+                         "the Qwen3-8B MXFP4 target (one JSON line per length), nothing else")
+    ap.add_argument("--prompt-attention", choices=["tensor", "cuda"], default="tensor",
+                    help="with --prefill: prompt attention on tcgen05 MMAs (default) or on the CUDA-core kernel")
     ap.add_argument("--small", action="store_true",
-                    help="with --profile: two layers of each model at full width and an 8192-entry "
+                    help="with --profile or --prefill: two layers of each model at full width and an 8192-entry "
                          "vocabulary (under 0.5 GB on the device), for multi-pass ncu captures")
     return ap.parse_args()
 
@@ -524,6 +529,38 @@ def workload_config(args):
             "parallelism": f"replicas x{args.gpus}, no collective"}
 
 
+def run_prefill(args, dist):
+    """Prompt processing of the target (model.rs:209-240 with all = false):
+    each length's prompt as the multi-chunk tensor-core passes predict runs,
+    with the prompt attention of a bf16 pool on tensor cores.  One untimed
+    call, then the fastest of three timed calls (wall clock around the
+    synchronous public call: ids in, one id out).  Rank 0 prints."""
+    import jalapeno as J
+
+    lengths = [int(x) for x in args.prefill.split(",") if x]
+    t = dict(PRESETS["qwen3-8b"])
+    if args.small:  # for ncu captures: two layers at full width, an 8192-entry vocabulary
+        t.update(layers=2, vocab=8192)
+    target = J.Model.synthesize(**t, seed=0, mxfp4=True, name="Qwen3-8B-MXFP4",
+                                kv_pool_tokens=max(lengths) + 64, device=dist.local)
+    tc = target.prompt_attention(args.prompt_attention == "tensor")
+    for n in lengths:
+        prompt = J.prompt_ids(n, t["vocab"], 3)
+        target.predict(prompt, target.cache())
+        best = float("inf")
+        for _ in range(3):
+            cache = target.cache()
+            t0 = time.perf_counter()
+            target.predict(prompt, cache)
+            best = min(best, time.perf_counter() - t0)
+            del cache
+        if dist.rank == 0:
+            print(json.dumps({"metric": "Qwen3-8B MXFP4 prefill" + (" (2 layers, --small)" if args.small else ""),
+                              "prompt_tokens": n, "ms": round(best * 1e3, 2),
+                              "tok_s": round(n / best, 1), "kv": "bf16 paged", "data": "synthetic",
+                              "prompt_attention": "tcgen05" if tc else "cuda cores"}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -539,6 +576,10 @@ def main():
         return
     if args.config5:
         run_config5(args, dist)
+        dist.close()
+        return
+    if args.prefill:
+        run_prefill(args, dist)
         dist.close()
         return
     import jalapeno as J

@@ -305,6 +305,14 @@ jl_status jl_pass_kernels(const jl_model* m, size_t rows, int draft_step, size_t
  * timeout path without faulting or hanging the GPU. */
 jl_status jl_wait_probe(jl_model* m, uint32_t polls);
 
+/* Chooses the kernel of prompt attention for the prompt passes recorded
+ * after the call: tensor_cores = 1 (the default) runs it on tcgen05 MMAs
+ * wherever the model allows (fused MXFP4 model, bf16 KV pool, GQA group of
+ * 1, 2, 4 or 8), 0 keeps the CUDA-core kernel.  *active (may be NULL)
+ * receives 1 when prompts now run on tensor cores.  No reference
+ * counterpart: it lets tests compare the two kernels on identical inputs. */
+jl_status jl_model_prompt_attention(jl_model* m, int tensor_cores, int* active);
+
 /* Kernel phase timeline, from the diagnostic build of this library
  * (`make -C jalapenos-at-home_b200 timeline` -> lib/libjalapeno_timeline.so):
  * the decode-pass kernels stamp the GPU's nanosecond clock at fixed points

@@ -317,6 +317,14 @@ jl_status jl_wait_probe(jl_model* m, uint32_t polls) {
     JL_GUARD({ return wait_probe(m, polls); })
 }
 
+jl_status jl_model_prompt_attention(jl_model* m, int tensor_cores, int* active) {
+    JL_NEED(m, "model must be non-null");
+    JL_NEED(tensor_cores == 0 || tensor_cores == 1, "tensor_cores must be 0 or 1");
+    m->prompt_attn_cuda_cores = tensor_cores == 0;
+    if (active) *active = prefill_tc_supported(m) ? 1 : 0;
+    return JL_OK;
+}
+
 jl_status jl_timeline_read(uint64_t* stamps, size_t cap, size_t* launches) {
     static_assert(JL_TIMELINE_CTAS == jl::TL_CTAS && JL_TIMELINE_POINTS == jl::TL_POINTS, "timeline table shape");
     JL_NEED(launches, "launches must be non-null");

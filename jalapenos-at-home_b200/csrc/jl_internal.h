@@ -14,6 +14,7 @@
 //    up to the bucket it was captured for.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (a type only: the driver entry point is looked up at run time)
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -252,6 +253,11 @@ struct jl_model {
     size_t arena_bytes = 0;
     float2* rope = nullptr;               // [max_positions][HALF] (cos, sin)
     jl::KvPool kv;
+    // TMA tensor maps of each layer's K and V pages ([layer][K|V]) for the
+    // tensor-core prompt attention; empty for f32 pools and pools too large
+    // for 32-bit coordinates (the CUDA-core kernel serves those)
+    std::vector<CUtensorMap> kv_tmaps;
+    bool prompt_attn_cuda_cores = false;  // jl_model_prompt_attention(m, 0, ...)
     int max_rows = 0;
     jl::PassBuf pass;                     // device
     // Pinned staging of pass descriptors: a ring of slots (jl::stage_begin /
@@ -320,6 +326,11 @@ struct PassCtx;
 jl_status record_pass_ctx(const PassCtx& c, int layers, bool with_head);
 // Sets kernel attributes once per device, before any stream capture.
 jl_status configure_kernels();
+// Tensor-core prompt attention (attn_prefill_tc.cu).
+jl_status kv_tensor_maps(jl_model* m);
+jl_status configure_prefill_tc();
+bool prefill_tc_supported(const jl_model* m);
+jl_status launch_attention_prefill_tc(const PassCtx& c, int layer, uint8_t* bout, int bN);
 jl_status predict(jl_model* m, jl_cache* c, const uint32_t* ids, size_t n, bool all,
                   uint32_t* out_ids, float* out_logits, bool draft_step = false);
 jl_status hidden(jl_model* m, const uint32_t* ids, size_t n, size_t layers, float* out);

@@ -1411,6 +1411,7 @@ jl_status configure_kernels() {
     JL_CUDA(cudaFuncSetAttribute(k_attn_decode<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem(1)));
     JL_TRY(mx_configure());
     JL_TRY(dec_configure());
+    JL_TRY(configure_prefill_tc());
     JL_TRY(noalloc_prepare(dev));
     JL_TRY(tl_prepare());
     if (dev < 64) done[dev] = true;
@@ -1453,6 +1454,8 @@ jl_status launch_attention(const PassCtx& c, int layer, bool pieces) {
     uint8_t* bout = pieces ? c.m->mx.battn : nullptr;
     const bool chunked = c.chunks > 1;
     const int bN = 8 * (chunked ? SMALL_M : c.rows_cap);
+    // one sequence's prompt on tensor cores (bf16 pools, groups of 1, 2, 4, 8)
+    if (chunked && c.prefill && prefill_tc_supported(c.m)) return launch_attention_prefill_tc(c, layer, bout, bN);
     if (chunked && c.prefill && group <= 8) {  // one sequence's prompt: K/V pages shared by 8 rows
         const dim3 g3(c.m->kv_heads, c.rows_cap / PF_ROWS), blk(PF_WARPS * 32);
         const int qw = c.m->q_heads * HEAD;

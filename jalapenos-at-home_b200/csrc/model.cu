@@ -94,6 +94,7 @@ jl_status finish_model(jl_model* m, const jl_model_options& o) {
         set_error("cannot allocate a KV pool of %zu bytes (%zu tokens)", kv_bytes, tokens);
         return JL_ERR_OOM;
     }
+    JL_TRY(kv_tensor_maps(m));  // the tensor-core prompt attention's TMA view of the pool
     m->kv.free_list.resize(m->kv.pages);
     for (size_t i = 0; i < m->kv.pages; ++i) m->kv.free_list[i] = (int32_t)(m->kv.pages - 1 - i);
     // decode attention over long contexts: the partial sums of up to

@@ -149,6 +149,30 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// ---- tensor copies (TMA with a tensor map) --------------------------------------
+
+// A 2-D box of the tensor `map` (a CUtensorMap in kernel parameter, constant or
+// global memory) at coordinates (x, y) into shared memory, counted against
+// `bar` (complete_tx).  x times the element size must be a multiple of 16
+// bytes; dst is aligned as the map's swizzle requires (1024 bytes for 128B).
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const void* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Orders this thread's earlier generic-proxy shared-memory writes before later
+// async-proxy reads of them (tcgen05.mma operands, bulk copies).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---- programmatic dependent launch --------------------------------------------
 
 // Waits until the previous kernel in the stream has completed (or triggered).

@@ -40,6 +40,7 @@ EXPORTS = (
     "jl_generate_speculative", "jl_time_pass", "jl_time_projection", "jl_project",
     "jl_project_noalloc", "jl_pass_kernels", "jl_time_pass_draft", "jl_generate_batch",
     "jl_generate_speculative_batch", "jl_timeline_read", "jl_timeline_kernel", "jl_wait_probe",
+    "jl_model_prompt_attention",
 )
 PROJ_QKV, PROJ_O, PROJ_GATE_UP, PROJ_DOWN, PROJ_HEAD = 0, 1, 2, 3, 4
 
@@ -163,6 +164,7 @@ def _load():
         "jl_timeline_read": ([ctypes.POINTER(ctypes.c_uint64), sz, ctypes.POINTER(sz)], ctypes.c_int),
         "jl_timeline_kernel": ([sz], ctypes.c_char_p),
         "jl_wait_probe": ([vp, ctypes.c_uint32], ctypes.c_int),
+        "jl_model_prompt_attention": ([vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -400,6 +402,14 @@ class Model:
         check(lib.jl_time_pass_draft(self._h, _p(t, ctypes.c_uint32), len(t), reps,
                                      ctypes.byref(wall), ctypes.byref(gpu)))
         return wall.value, gpu.value
+
+    def prompt_attention(self, tensor_cores: bool = True) -> bool:
+        """Kernel of the prompt attention for later prompt passes: tcgen05
+        MMAs (default, where the model allows) or CUDA cores.  Returns whether
+        prompts now run on tensor cores."""
+        active = ctypes.c_int(0)
+        check(lib.jl_model_prompt_attention(self._h, int(bool(tensor_cores)), ctypes.byref(active)))
+        return bool(active.value)
 
     def wait_probe(self, polls: int = 1000) -> None:
         """One device wait that nothing completes, bounded by ``polls`` polls:
