@@ -12,11 +12,11 @@
 //     MN-major one.
 //   * S = Q K^T in TMEM, with Q as two bf16 pieces (hi + lo, exact to 2^-17
 //     of each element), both MMAs accumulating into one f32 tile.
-//   * Softmax on CUDA cores: thread (row m, half h) reads keys 64h..64h+63 of
-//     row m from TMEM; the two halves exchange their maxima through shared
+//   * Softmax on CUDA cores: thread (row m, part t) reads keys 32t..32t+31 of
+//     row m from TMEM; the four parts exchange their maxima through shared
 //     memory, and the running max and sum are kept online as in k_attn_prefill.
 //   * P goes back to shared memory as two bf16 pieces (hi + lo) and
-//     O_tile = P V lands in TMEM; each thread folds its 64 output dims into
+//     O_tile = P V lands in TMEM; each thread folds its 32 output dims into
 //     registers (o = o * correction + O_tile).
 // The scores of tile j + 1 are issued right behind P V of tile j, so that MMA
 // runs while the threads fold O.  Keys past a row's position, and keys of
@@ -48,7 +48,11 @@ using mx::swz128;
 
 constexpr int TC_M = 128;        // MMA rows of a CTA
 constexpr int TC_KEYS = 128;     // keys per tile (two pages)
-constexpr int TC_THREADS = 256;  // two threads per MMA row
+constexpr int TC_PARTS = 4;                // threads per MMA row
+constexpr int TC_THREADS = 128 * TC_PARTS;
+constexpr int TC_KP = TC_KEYS / TC_PARTS;  // keys of a tile per thread
+constexpr int TC_DP = HEAD / TC_PARTS;     // output dims per thread
+static_assert(TC_KP == 32 && TC_DP == 32, "one 32-column TMEM load per thread and tile");
 constexpr uint32_t TC_IMG = 16384;  // one 128-row x 128-byte swizzled image
 constexpr uint32_t TC_PAGE_IMG = PAGE * 128;  // one page's rows of an image
 // shared-memory images (1024-byte aligned): Q and P as [64-element K block]
@@ -80,6 +84,24 @@ __device__ __forceinline__ void split_bf16(float x, uint32_t& hi, uint32_t& lo) 
     const __nv_bfloat16 l = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(h)));
     hi = __bfloat16_as_ushort(h);
     lo = __bfloat16_as_ushort(l);
+}
+
+// The same for a pair: (x, y) as packed bf16x2 hi and lo words (x low).
+__device__ __forceinline__ void split_bf16x2(float x, float y, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(x, hf.x), __fsub_rn(y, hf.y));
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// 2^x by the hardware's approximation (ex2.approx.ftz: relative error about
+// 2^-22 for the x <= 0 the softmax weights take, results below 2^-126 flushed
+// to zero).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 // The MMAs of one tile, issued by one thread.  Not inlined: their 64-bit
@@ -127,12 +149,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint8_t* sm = (uint8_t*)(((uintptr_t)tc_raw + 1023) & ~(uintptr_t)1023);
     __shared__ uint64_t bar_k, bar_v, bar_s, bar_o;
     __shared__ uint32_t tmem_s;
-    __shared__ float xchg[2][TC_M];  // the two halves of a row: tile maxima, then sums
+    __shared__ float xchg[TC_PARTS][TC_M];  // the parts of a row: tile maxima, then sums
     __shared__ int live_s;           // rows 0..live_s-1 of the CTA are live
     __shared__ int pvalid[2][2];     // [tile parity][page of the tile]: copied
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quarter = warp & 3, half = warp >> 2;
+    const int quarter = warp & 3, part = warp >> 2;
     const int m = quarter * 32 + lane;  // MMA row = TMEM lane
     const int group = a.group, PT = TC_M / group;
     const int g = blockIdx.x, r0 = blockIdx.y * PT;
@@ -241,10 +263,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         else okv = false;
     };
 
-    float o[64];  // output dims 64 * half .. of row m, unnormalised
+    float o[TC_DP];  // output dims TC_DP * part .. of row m, unnormalised
 #pragma unroll
-    for (int i = 0; i < 64; ++i) o[i] = 0.f;
-    float mrun = -INFINITY, lpart = 0.f;  // running max of raw scores; this half's running sum
+    for (int i = 0; i < TC_DP; ++i) o[i] = 0.f;
+    float mrun = -INFINITY, lpart = 0.f;  // running max of raw scores; this part's running sum
     const float c2 = (float)(1.4426950408889634 / 11.313708498984761);  // log2(e) / sqrt(HEAD)
     bool ok = true;
     if (tid == 0 && nt > 0) {
@@ -273,47 +295,48 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         // keys k0 + c, c < nvis, are this row's (causal, page copied); S is
         // read from TMEM twice (maximum, then weights) rather than held
-        const int k0 = j * TC_KEYS + 64 * half;
-        const int nvis = pvalid[par][half] ? max(0, min(64, pos_m - k0 + 1)) : 0;
-        float s[32];
+        const int k0 = j * TC_KEYS + TC_KP * part;
+        const int nvis = pvalid[par][part >> 1] ? max(0, min(TC_KP, pos_m - k0 + 1)) : 0;
+        const bool whole = nvis == TC_KP;  // no masking (every tile but a CTA's last one or two)
+        float s[TC_KP];
+        ptx::tmem_ld32(t_row + TC_KP * part, s);
         float tmax = -INFINITY;
+        if (whole) {
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-            ptx::tmem_ld32(t_row + 64 * half + 32 * h2, s);
+            for (int c = 0; c < TC_KP; ++c) tmax = fmaxf(tmax, s[c]);
+        } else {
 #pragma unroll
-            for (int c = 0; c < 32; ++c)
-                if (32 * h2 + c < nvis) tmax = fmaxf(tmax, s[c]);
+            for (int c = 0; c < TC_KP; ++c)
+                if (c < nvis) tmax = fmaxf(tmax, s[c]);
         }
-        xchg[half][m] = tmax;
-        __syncthreads();  // both halves' maxima
-        const float mnew = fmaxf(mrun, fmaxf(xchg[0][m], xchg[1][m]));
-        const float corr = mrun == -INFINITY ? 0.f : exp2f(__fmul_rn(__fsub_rn(mrun, mnew), c2));
+        xchg[part][m] = tmax;
+        __syncthreads();  // every part's maximum
+        const float mnew = fmaxf(mrun, fmaxf(fmaxf(xchg[0][m], xchg[1][m]), fmaxf(xchg[2][m], xchg[3][m])));
+        const float corr = mrun == -INFINITY ? 0.f : ex2(__fmul_rn(__fsub_rn(mrun, mnew), c2));
         mrun = mnew;
+        const float mc = __fmul_rn(mnew, c2);
         float psum = 0.f;
-        uint8_t* ph_img = sm + OFF_PH + half * TC_IMG;
-        uint8_t* pl_img = sm + OFF_PL + half * TC_IMG;
+        // keys 32 part .. of the row: P image part / 2, chunks 4 (part & 1) ..
+        uint8_t* ph_img = sm + OFF_PH + (part >> 1) * TC_IMG;
+        uint8_t* pl_img = sm + OFF_PL + (part >> 1) * TC_IMG;
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-            ptx::tmem_ld32(t_row + 64 * half + 32 * h2, s);
+        for (int ch = 0; ch < 4; ++ch) {  // 8 keys = one 16-byte chunk of the row
+            uint32_t wh[4], wl[4];
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {  // 8 keys = one 16-byte chunk of the row
-                uint32_t wh[4], wl[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int c = 8 * ch + 2 * e, kc = 32 * h2 + c;
-                    const float p0 = kc < nvis ? exp2f(__fmul_rn(__fsub_rn(s[c], mnew), c2)) : 0.f;
-                    const float p1 = kc + 1 < nvis ? exp2f(__fmul_rn(__fsub_rn(s[c + 1], mnew), c2)) : 0.f;
-                    psum = __fadd_rn(psum, __fadd_rn(p0, p1));
-                    uint32_t h0, l0, h1, l1;
-                    split_bf16(p0, h0, l0);
-                    split_bf16(p1, h1, l1);
-                    wh[e] = h0 | (h1 << 16);
-                    wl[e] = l0 | (l1 << 16);
+            for (int e = 0; e < 4; ++e) {
+                const int c = 8 * ch + 2 * e;
+                // 2^(s c2 - m c2): one multiply-add per weight
+                float p0 = ex2(__fmaf_rn(s[c], c2, -mc)), p1 = ex2(__fmaf_rn(s[c + 1], c2, -mc));
+                if (!whole) {
+                    p0 = c < nvis ? p0 : 0.f;
+                    p1 = c + 1 < nvis ? p1 : 0.f;
                 }
-                const uint32_t off = swz128((uint32_t)m, (uint32_t)(16 * (4 * h2 + ch)));
-                *(uint4*)(ph_img + off) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
-                *(uint4*)(pl_img + off) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+                psum = __fadd_rn(psum, __fadd_rn(p0, p1));
+                split_bf16x2(p0, p1, wh[e], wl[e]);
             }
+            const uint32_t off = swz128((uint32_t)m, (uint32_t)(16 * (4 * (part & 1) + ch)));
+            *(uint4*)(ph_img + off) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+            *(uint4*)(pl_img + off) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
         }
         lpart = __fmaf_rn(lpart, corr, psum);
         ptx::fence_proxy_async_smem();
@@ -355,13 +378,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             issue_tile(j + 1, &vmap, OFF_V, &bar_v, false);
             ++v_iss;
         }
-        float t[32];
-        ptx::tmem_ld32(t_row + 128 + 64 * half, t);
+        float t[TC_DP];
+        ptx::tmem_ld32(t_row + 128 + TC_DP * part, t);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = __fmaf_rn(o[i], corr, t[i]);
-        ptx::tmem_ld32(t_row + 128 + 64 * half + 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[32 + i] = __fmaf_rn(o[32 + i], corr, t[i]);
+        for (int i = 0; i < TC_DP; ++i) o[i] = __fmaf_rn(o[i], corr, t[i]);
         ptx::tc_fence_before();
     }
     // after a failed wait: let every copy and MMA this CTA issued finish
@@ -379,16 +399,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // outputs: o / l for live rows, zero for the others, staged as
     // [position][group * HEAD + 4] f32 over the Q and K images (the pad
     // spreads positions over the banks)
-    xchg[half][m] = lpart;
+    xchg[part][m] = lpart;
     __syncthreads();
-    const float l = __fadd_rn(xchg[0][m], xchg[1][m]);
+    const float l = __fadd_rn(__fadd_rn(xchg[0][m], xchg[1][m]), __fadd_rn(xchg[2][m], xchg[3][m]));
     const int st = group * HEAD + 4;
     float* ost = (float*)sm;
     {
-        float* dst = ost + (size_t)prow * st + (m % group) * HEAD + 64 * half;
+        float* dst = ost + (size_t)prow * st + (m % group) * HEAD + TC_DP * part;
         const bool lv = pos_m >= 0 && l > 0.f;
 #pragma unroll
-        for (int i = 0; i < 64; i += 4)
+        for (int i = 0; i < TC_DP; i += 4)
             *(float4*)(dst + i) = lv ? make_float4(__fdiv_rn(o[i], l), __fdiv_rn(o[i + 1], l),
                                                    __fdiv_rn(o[i + 2], l), __fdiv_rn(o[i + 3], l))
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
