@@ -983,6 +983,26 @@ size_t mx_smem(int N, int kind, int mcap, int ks) {
     return (size_t)st * mx_slot_bytes(N, kind, gr) + part * ks + 1024;
 }
 
+// Multi-chunk launches of N > 64 columns run several tiles per CTA and hold
+// the SM alone (MX_ONE_PER_SM), so their ring takes the shared memory a CTA
+// may have: slots of MX_MULTI_GROUP stages, as many (up to MX_MAXSTAGES) as
+// fit beside the epilogue scratch.  Measured on a 4096-token Qwen3-8B
+// prompt: three one-stage slots 398 ms, six one-stage slots 397 ms, three
+// two-stage slots 332 ms, two three-stage slots 351 ms.
+constexpr int MX_MULTI_GROUP = 2;
+constexpr size_t MX_SMEM_LIMIT = 227 * 1024 - 2048;  // dynamic + this kernel's static shared memory
+int mx_multi_slots(int N, int kind, int mcap, int ks) {
+    const size_t part = (size_t)((mcap + 3) & ~3) * 512;
+    const size_t slot = (size_t)mx_slot_bytes(N, kind, MX_MULTI_GROUP);
+    int slots = 0;
+    while (slots < MX_MAXSTAGES && (size_t)(slots + 1) * slot + part * ks + 1024 <= MX_SMEM_LIMIT) ++slots;
+    return slots;
+}
+size_t mx_multi_smem(int N, int kind, int mcap, int ks) {
+    const size_t part = (size_t)((mcap + 3) & ~3) * 512;
+    return (size_t)mx_multi_slots(N, kind, mcap, ks) * mx_slot_bytes(N, kind, MX_MULTI_GROUP) + part * ks + 1024;
+}
+
 // Ring slots requested into L2 beyond the ring by k_mx_gemv's loader: on for
 // the output table (measured on B200: the 8B's 1.245 GB table 220 -> 202 us
 // per pass), off for the layer projections (slightly slower with it).
@@ -996,8 +1016,9 @@ constexpr size_t MX_ONE_PER_SM = 116 * 1024;
 
 template <int EPI, int KIND>
 jl_status configure_mx() {
-    const size_t most = std::max(mx_smem(64, KIND, MX_MAXTOK, MX_MAXCLUSTER),
-                                 mx_smem(8 * MX_MAXTOK, KIND, MX_MAXTOK, MX_MAXCLUSTER));
+    const size_t most = std::max(std::max(mx_smem(64, KIND, MX_MAXTOK, MX_MAXCLUSTER),
+                                          mx_smem(8 * MX_MAXTOK, KIND, MX_MAXTOK, MX_MAXCLUSTER)),
+                                 MX_SMEM_LIMIT);
     JL_CUDA(cudaFuncSetAttribute(k_mx_gemv<EPI, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)std::max<size_t>(MX_PROBE_SMEM, most)));
     JL_CUDA(cudaFuncSetAttribute(k_mx_gemv<EPI, KIND>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
@@ -1007,14 +1028,23 @@ jl_status configure_mx() {
 template <int EPI, int KIND>
 jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream, int chunks) {
     // One wave of CTAs (one per SM at these shapes): a multi-chunk launch
-    // gives each chunk its share, so a CTA runs several tiles through its
-    // ring instead of each chunk waiting for a wave of its own.
-    const int nc = std::max(1, std::min(a.T, a.ksplit > 1 ? mx_clusters(a.ksplit) : sms) / chunks);
+    // gives each chunk its share of the wave's clusters (at most one per
+    // tile), so a CTA runs several tiles through its ring instead of each
+    // chunk waiting for a wave of its own.  When the chunks' tiles are many
+    // times the SMs, split-K is dropped: a CTA then runs whole tiles, one
+    // epilogue each, with no partials to exchange.
+    // (A 4096-token Qwen3-8B prompt: 398 ms with min(T, clusters) / chunks
+    // clusters per chunk and the planned split-K, 301 ms with this share,
+    // 255 ms with split-K dropped as well.)
+    const int ks = (chunks > 1 && a.N > 64 && (long long)a.T * chunks >= 4LL * sms) ? 1 : a.ksplit;
+    const int per = ks > 1 ? mx_clusters(ks) : sms;
+    const int nc = std::max(1, std::min(a.T, per / chunks));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(nc * a.ksplit, chunks);
+    cfg.gridDim = dim3(nc * ks, chunks);
     cfg.blockDim = dim3(MX_THREADS);
-    cfg.dynamicSmemBytes = mx_smem(a.N, KIND, a.mcap, a.ksplit);
+    cfg.dynamicSmemBytes = mx_smem(a.N, KIND, a.mcap, ks);
     MxArgs b = a;
+    b.ksplit = ks;
     b.l2_ahead = EPI == MX_HEAD ? MX_L2_AHEAD : 0;
     static const char* const names[] = {"k_mx_gemv<store>", "k_mx_gemv<add>", "k_mx_gemv<swiglu>",
                                         "k_mx_gemv<qkv>", "k_mx_gemv<head>"};
@@ -1025,15 +1055,21 @@ jl_status launch_gemv_t(const MxArgs& a, int sms, cudaStream_t stream, int chunk
         b.nbuf = 2;
         b.acc_step = 256;
         cfg.dynamicSmemBytes = std::max(cfg.dynamicSmemBytes, MX_ONE_PER_SM);
+        const int slots = mx_multi_slots(a.N, KIND, a.mcap, ks);
+        if (slots * MX_MULTI_GROUP > a.stages * a.group) {  // the deeper ring, where it fits
+            b.stages = slots;
+            b.group = MX_MULTI_GROUP;
+            cfg.dynamicSmemBytes = std::max(mx_multi_smem(a.N, KIND, a.mcap, ks), MX_ONE_PER_SM);
+        }
     }
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     int n = 1;
-    if (a.ksplit > 1) {
+    if (ks > 1) {
         attr[1].id = cudaLaunchAttributeClusterDimension;
-        attr[1].val.clusterDim.x = (unsigned)a.ksplit;
+        attr[1].val.clusterDim.x = (unsigned)ks;
         attr[1].val.clusterDim.y = 1;
         attr[1].val.clusterDim.z = 1;
         n = 2;
